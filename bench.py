@@ -1,0 +1,502 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quaternion linear forward.
+
+Metric: QuaternionLinear microseconds per call (bf16), with the fraction of
+the HBM (decode) or tensor-core (prefill) roofline.  One *step* is one call of
+the layer on one batch of seeded synthetic input.
+
+Default workload (N=1): the decode layer in=out=4096 bf16, M=1 token, fused
+bias [4096] and LoRA rank 32 (the decode configuration of the reference's
+benchmark set).  The same run also reports decode at M=16 and the prefill
+layer in=4096 -> out=11008 at M=2048 under "also".
+
+Timing: W untimed warm-up steps, then exactly K steps captured in one CUDA
+graph and replayed once between CUDA events (device time), bracketed by a
+barrier and torch.cuda.synchronize() on both sides; the max over ranks is
+reported.  Consecutive steps rotate through enough copies of the weights
+(and inputs) to exceed the 126 MB L2, so every step streams its weights from
+HBM.  "e2e" times K steps through the public module API with the input copied
+from pinned host memory and the output read back every step.
+
+With torchrun (N>1) every rank runs an independent replica of the workload
+(weak scaling); value = max-over-ranks time / (K * N), the job-wide time per
+call.  `--impl reference` times the CPU restatement of the reference's K1
+(naive) operator on the host cores (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = "quaternion-based-math-1_b200"
+L2_BYTES = 126 * 2**20
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+WORKLOADS = {
+    "decode_m1": dict(fn="decode_4096", M=1, bound="hbm"),
+    "decode_m16": dict(fn="decode_4096", M=16, bound="hbm"),
+    "prefill_m2048": dict(fn="prefill_11008", M=2048, bound="tensor"),
+}
+DEFAULT = "decode_m1"
+
+
+def _pkg():
+    if REPO not in sys.path:
+        sys.path.insert(0, REPO)
+    return importlib.import_module(PKG), importlib.import_module(f"{PKG}.workloads")
+
+
+def _oracle():
+    p = os.path.join(REPO, "oracle")
+    if p not in sys.path:
+        sys.path.insert(0, p)
+    import oracle  # the CPU restatement: timed baseline only
+
+    return oracle
+
+
+def _peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    except (OSError, KeyError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def _layer(wl, name):
+    spec = WORKLOADS[name]
+    return getattr(wl, spec["fn"])(spec["M"])
+
+
+def algorithmic_work(lay):
+    """(bytes, flops) one call must move / perform, from the layer's shapes."""
+    es = 2 if lay.dtype != "f32" else 4
+    M, K, N = lay.M, 4 * lay.K_g, 4 * lay.N_g
+    nbytes = es * (4 * lay.N_g * lay.K_g + M * K + M * N)
+    flops = 2.0 * M * N * K
+    if lay.bias is not None:
+        nbytes += es * N
+    if lay.lora_a is not None:
+        r = lay.lora_a.shape[0]
+        nbytes += es * (r * K + N * r)
+        flops += 2.0 * M * r * (K + N)
+    return nbytes, flops
+
+
+def workload_config(name, lay, ncopy):
+    return {
+        "workload": f"qlinear_{4 * lay.K_g}x{4 * lay.N_g}_{lay.dtype}_m{lay.M}"
+                    + ("_bias" if lay.bias is not None else "")
+                    + (f"_lora{lay.lora_a.shape[0]}" if lay.lora_a is not None else ""),
+        "name": name,
+        "M": lay.M,
+        "in_features": 4 * lay.K_g,
+        "out_features": 4 * lay.N_g,
+        "lora_rank": 0 if lay.lora_a is None else int(lay.lora_a.shape[0]),
+        "bias": lay.bias is not None,
+        "seed": lay.meta.get("seed"),
+        "inputs": "seeded synthetic N(0,1) activations, N(0,1/in) weights (variance), "
+                  "bias N(0,0.02), LoRA N(0,0.01)",
+        "l2": f"inputs larger than L2: {ncopy} rotating copies of weights/inputs",
+    }
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in getattr(self, "lines", []):
+            f = [c.strip() for c in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# device timing
+# ---------------------------------------------------------------------------
+
+def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES):
+    """Device copies rotated to exceed L2, preallocated outputs and workspace."""
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
+    nbytes, _ = algorithmic_work(lay)
+    ncopy = max(2, min(64, math.ceil(min_bytes / max(nbytes, 1))))
+
+    def t(a):
+        return None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev).to(dt)
+
+    base = dict(x=t(lay.x), w=[t(a) for a in lay.weights], b=t(lay.bias), la=t(lay.lora_a),
+                lb=t(lay.lora_b))
+    copies = [base]
+    for _ in range(ncopy - 1):
+        copies.append({k: (None if v is None else ([a.clone() for a in v] if isinstance(v, list)
+                                                    else v.clone()))
+                       for k, v in base.items()})
+    M, K_g, N_g = lay.M, lay.K_g, lay.N_g
+    rank = 0 if lay.lora_a is None else lay.lora_a.shape[0]
+    ys = [torch.empty(M, 4 * N_g, dtype=dt, device=dev) for _ in range(ncopy)]
+    ws_bytes = qb._lib.workspace_size(dt, M, K_g, N_g, rank)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    lib = qb._lib.load()
+    code = qb._lib.dtype_code(dt)
+    stream_of = qb._lib.stream_handle
+
+    def call(i):
+        c = copies[i % ncopy]
+        y = ys[i % ncopy]
+        st = lib.qlin_forward(code, c["x"].data_ptr(), 4 * K_g, *(w.data_ptr() for w in c["w"]), K_g,
+                              c["b"].data_ptr() if c["b"] is not None else None,
+                              c["la"].data_ptr() if c["la"] is not None else None,
+                              c["lb"].data_ptr() if c["lb"] is not None else None,
+                              rank, float(lay.lora_scale), y.data_ptr(), 4 * N_g, M, K_g, N_g,
+                              ws.data_ptr(), ws_bytes, stream_of(dev))
+        if st != 0:
+            qb._lib.check(st, "qlin_forward")
+
+    launches = 2 + (1 if rank else 0) if lay.dtype != "f32" else 1 + (1 if rank else 0)
+    return call, ncopy, copies, ys, launches
+
+
+def time_device(qb, lay, torch, dev, K, W, dist=None):
+    call, ncopy, copies, ys, launches = _device_case(qb, lay, torch, dev)
+    for i in range(W):
+        call(i)
+    torch.cuda.synchronize(dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        call(0)  # stream warm-up before capture
+    torch.cuda.current_stream(dev).wait_stream(side)
+    with torch.cuda.graph(graph):
+        for i in range(K):
+            call(i)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    graph.replay()
+    end.record()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del graph
+    return ms, ncopy, launches
+
+
+def time_dense(lay, torch, dev, K, W):
+    """cuBLAS x @ W^T of the same logical shape (context only)."""
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
+    M, Kf, N = lay.M, 4 * lay.K_g, 4 * lay.N_g
+    wbytes = N * Kf * 2
+    ncopy = max(2, min(32, math.ceil(2 * L2_BYTES / (wbytes + 2 * M * (Kf + N)))))
+    g = torch.Generator(device="cpu").manual_seed(0)
+    ws = [(torch.randn(N, Kf, generator=g) / math.sqrt(Kf)).to(dev, dt) for _ in range(ncopy)]
+    xs = [torch.randn(M, Kf, generator=g).to(dev, dt) for _ in range(ncopy)]
+    ys = [torch.empty(M, N, device=dev, dtype=dt) for _ in range(ncopy)]
+    for i in range(W):
+        torch.matmul(xs[i % ncopy], ws[i % ncopy].t(), out=ys[i % ncopy])
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(K):
+        torch.matmul(xs[i % ncopy], ws[i % ncopy].t(), out=ys[i % ncopy])
+    e.record()
+    torch.cuda.synchronize(dev)
+    return s.elapsed_time(e) * 1e3 / K
+
+
+def time_e2e(qb, lay, torch, dev, K, W):
+    """K steps through the public module API with host input and host output."""
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
+    nbytes, _ = algorithmic_work(lay)
+    ncopy = max(2, min(32, math.ceil(2 * L2_BYTES / max(nbytes, 1))))
+    fin, fout = 4 * lay.K_g, 4 * lay.N_g
+    layers = []
+    for c in range(ncopy):
+        base = qb.QuaternionLinear(fin, fout, bias=lay.bias is not None, device=dev, dtype=dt)
+        with torch.no_grad():
+            for n, a in zip(("wr", "wi", "wj", "wk"), lay.weights):
+                getattr(base, n).copy_(torch.from_numpy(a))
+            if lay.bias is not None:
+                base.bias.copy_(torch.from_numpy(lay.bias))
+        mod = base
+        if lay.lora_a is not None:
+            mod = qb.LoRAQuaternionLinear(base, rank=lay.lora_a.shape[0])
+            with torch.no_grad():
+                mod.lora_A.copy_(torch.from_numpy(lay.lora_a))
+                mod.lora_B.copy_(torch.from_numpy(lay.lora_b))
+        mod.eval()
+        layers.append(mod)
+    x_host = torch.from_numpy(lay.x).to(dt).pin_memory()
+    y_host = torch.empty(lay.M, fout, dtype=dt).pin_memory()
+    x_dev = torch.empty(lay.M, fin, dtype=dt, device=dev)
+
+    def step(i):
+        x_dev.copy_(x_host, non_blocking=True)
+        y = layers[i % ncopy](x_dev)
+        y_host.copy_(y, non_blocking=True)
+
+    with torch.inference_mode():
+        for i in range(W):
+            step(i)
+        torch.cuda.synchronize(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(K):
+            step(i)
+        e.record()
+        torch.cuda.synchronize(dev)
+    es = x_host.element_size()
+    return s.elapsed_time(e) * 1e3 / K, lay.M * fin * es, lay.M * fout * es
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle's numpy restatement of the reference K1 operator
+# ---------------------------------------------------------------------------
+
+def cpu_port_call(oracle, lay, rows):
+    """quaternion/planar.py:39-61 (+ bias, + lora.py:60-63) in float32 BLAS."""
+    x = lay.x[rows]
+    y = oracle.quaternion_linear_naive(x, *lay.weights, dtype=np.float32)
+    if lay.bias is not None:
+        y = y + lay.bias
+    if lay.lora_a is not None:
+        y = y + np.float32(lay.lora_scale) * ((x @ lay.lora_a.T) @ lay.lora_b.T)
+    return y
+
+
+def time_cpu(lay, budget_s=10.0, max_steps=None, warmup=1):
+    """Bounded CPU sample; returns (us_per_call, threads, sample description)."""
+    oracle = _oracle()
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:  # pragma: no cover
+        threadpool_limits = None
+    threads = os.cpu_count() or 1
+    ctx = threadpool_limits(limits=threads) if threadpool_limits else None
+    # row sample sized so one step stays near 50 ms of CPU work
+    probe_rows = min(lay.M, 8)
+    t0 = time.perf_counter()
+    cpu_port_call(oracle, lay, np.arange(probe_rows))
+    per_row = max((time.perf_counter() - t0) / probe_rows, 1e-7)
+    rows_n = lay.M if per_row * lay.M <= 0.05 else max(1, min(lay.M, int(0.05 / per_row)))
+    rows = np.arange(rows_n)
+    for _ in range(warmup):
+        cpu_port_call(oracle, lay, rows)
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        cpu_port_call(oracle, lay, rows)
+        times.append(time.perf_counter() - t0)
+        if max_steps is not None and len(times) >= max_steps:
+            break
+        if max_steps is None and time.perf_counter() - t_start > budget_s:
+            break
+    if ctx is not None:
+        ctx.unregister() if hasattr(ctx, "unregister") else None
+    per_call = statistics.median(times) * (lay.M / rows_n)
+    sample = (f"{len(times)} calls of the numpy/OpenBLAS float32 K1 restatement on {rows_n} of "
+              f"{lay.M} token rows, scaled to the full batch")
+    return per_call * 1e6, threads, sample, len(times)
+
+
+# ---------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default=DEFAULT, choices=sorted(WORKLOADS))
+    ap.add_argument("--no-extra", action="store_true", help="skip the secondary workloads")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    K, W = args.steps, max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    qb, wl = _pkg()
+    lay = _layer(wl, args.workload)
+    metric = "QuaternionLinear us/call (bf16), % of HBM/TC roofline"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        us, threads, sample, n = time_cpu(lay, budget_s=1e9, max_steps=K, warmup=W)
+        cfg = workload_config(args.workload, lay, 1)
+        print(json.dumps({
+            "impl": "reference", "metric": metric, "value": us, "unit": "us/call",
+            "n_gpus": args.gpus, "steps": K, "warmup": W, "ms_per_step": us / 1e3,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (numpy port of the reference K1 operator)", "data": "synthetic",
+            "config": cfg,
+            "cpu_baseline": {"value": us, "unit": "us/call", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": us, "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    import torch
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+
+        torch.cuda.set_device(local)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                 device_id=torch.device("cuda", local))
+        dist = tdist
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks, peak_src = _peaks()
+
+    nbytes, flops = algorithmic_work(lay)
+    with ClockSampler(local) as clk:
+        ms, ncopy, launches = time_device(qb, lay, torch, dev, K, W, dist)
+    us_call = ms * 1e3 / K
+    clocks = clk.summary()
+    bound = WORKLOADS[args.workload]["bound"]
+    if bound == "hbm":
+        achieved = nbytes / (us_call * 1e-6) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                "basis": f"{nbytes} algorithmic bytes per call / device time per call "
+                         f"({launches} launches per call)",
+                "peak_source": peak_src}
+    else:
+        achieved = flops / (us_call * 1e-6) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                "basis": f"{flops:.4g} dense-equivalent FLOP per call / device time per call",
+                "peak_source": peak_src}
+
+    result = {
+        "metric": metric, "value": us_call / world, "unit": "us/call", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": lay.dtype, "data": "synthetic",
+        "config": dict(workload_config(args.workload, lay, ncopy),
+                       parallelism=f"replicas{world}" if world > 1 else "single"),
+        "per_gpu_us_per_call": us_call,
+        "roofline": roof,
+        "clocks": clocks,
+        "gpu_launches": K * launches,
+    }
+
+    e2e_us, h2d, d2h = time_e2e(qb, lay, torch, dev, K, W)
+    if dist is not None:
+        t = torch.tensor([e2e_us], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_us = float(t.item())
+    result["e2e"] = {"value": e2e_us / world, "unit": "us/call", "h2d_bytes_per_step": h2d,
+                     "d2h_bytes_per_step": d2h}
+
+    if world == 1 and rank == 0:
+        us, threads, sample, _ = time_cpu(lay, budget_s=args.cpu_budget)
+        result["cpu_baseline"] = {"value": us, "unit": "us/call", "cores": threads, "kind": "port",
+                                  "sample": sample}
+        result["dense_cublas_us"] = time_dense(lay, torch, dev, K, W)
+        if not args.no_extra:
+            also = {}
+            for name in WORKLOADS:
+                if name == args.workload:
+                    continue
+                xl = _layer(wl, name)
+                kk = K if WORKLOADS[name]["bound"] == "hbm" else max(3, min(K, 200))
+                xms, xcopy, xl_launch = time_device(qb, xl, torch, dev, kk, W)
+                xus = xms * 1e3 / kk
+                xb, xf = algorithmic_work(xl)
+                entry = {"us_per_call": xus, "steps": kk, "config": workload_config(name, xl, xcopy),
+                         "dense_cublas_us": time_dense(xl, torch, dev, kk, W)}
+                if WORKLOADS[name]["bound"] == "hbm":
+                    a = xb / (xus * 1e-6) / 1e9
+                    entry["roofline"] = {"bound": "hbm", "achieved": a, "peak": peaks["hbm_gbs"],
+                                         "unit": "GB/s", "frac": a / peaks["hbm_gbs"]}
+                else:
+                    a = xf / (xus * 1e-6) / 1e12
+                    entry["roofline"] = {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"],
+                                         "unit": "TFLOP/s", "frac": a / peaks["bf16_tflops"]}
+                also[name] = entry
+            result["also"] = also
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

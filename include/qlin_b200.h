@@ -1,0 +1,141 @@
+/*
+ * qlin_b200.h -- C ABI of the B200 (sm_100a) quaternion linear forward.
+ *
+ * The quaternion linear layer replaces a real linear layer y = x W^T with
+ * four real weight components Wr, Wi, Wj, Wk of shape [N_g, K_g] and the
+ * Hamilton product per (output group, input group) pair.  Layout contract
+ * (reference quaternion/packing.py:5-25): x[m, 4i+q] is component q (r,i,j,k)
+ * of input quaternion i; y[m, 4o+a] is component a of output quaternion o;
+ * W_c[o, i] is row-major with leading dimension ld_w.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*; NULL = legacy default stream), returns a
+ * status code, and never throws.  Work is enqueued asynchronously on the
+ * given stream; nothing synchronises and nothing allocates device memory.
+ */
+#ifndef QLIN_B200_H
+#define QLIN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types.  x, weights, bias, LoRA A/B and y all share one type. */
+enum {
+  QLIN_F32 = 0,  /* fp32 in, fp32 CUDA-core FMA accumulate, fp32 out        */
+  QLIN_BF16 = 1, /* bf16 in, fp32 accumulate (tensor cores), one rounding out */
+  QLIN_F16 = 2   /* fp16 in, fp32 accumulate (tensor cores), one rounding out */
+};
+
+/* Status codes. */
+enum {
+  QLIN_OK = 0,
+  QLIN_ERR_SHAPE = 1,     /* bad dims or leading dims (reference: ValueError)   */
+  QLIN_ERR_DTYPE = 2,     /* unsupported element type (reference: RuntimeError) */
+  QLIN_ERR_ALIGN = 3,     /* pointer / leading-dim alignment not met by the path */
+  QLIN_ERR_WORKSPACE = 4, /* workspace missing or smaller than qlin_workspace_size */
+  QLIN_ERR_LAUNCH = 5,    /* a CUDA runtime call or kernel launch failed        */
+  QLIN_ERR_DEVICE = 6,    /* the current device is not sm_100 (B200 class)      */
+  QLIN_ERR_TIMEOUT = 7,   /* a bounded device-side wait ran out (see below)     */
+  QLIN_ERR_ARG = 8        /* null pointer or invalid option                     */
+};
+
+/* Kernel selection for qlin_forward_ex (QLIN_ALGO_AUTO is what qlin_forward uses). */
+enum {
+  QLIN_ALGO_AUTO = 0,
+  QLIN_ALGO_SIMT = 1,   /* CUDA-core tiled kernel: every dtype, every shape     */
+  QLIN_ALGO_TC = 2      /* TMA + tcgen05/TMEM kernel: bf16/f16, aligned shapes  */
+};
+
+/* Human-readable name of a status code (static storage). */
+const char* qlin_status_string(int status);
+
+/* ABI version (major * 100 + minor). */
+int qlin_abi_version(void);
+
+/*
+ * Bytes of device workspace qlin_forward needs for this problem (0 for some
+ * paths).  rank = LoRA rank (0 = no LoRA).  The workspace holds the planar
+ * copy of x and the LoRA down projection; it is only used during the call's
+ * kernels, so one buffer can be reused by calls on the same stream.
+ */
+int qlin_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank,
+                        size_t* bytes);
+
+/*
+ * y = QuaternionLinear(x) (+ bias) (+ lora_scale * ((x A^T) B^T)).
+ *
+ * Replaces, for the device path:
+ *   quaternion/linear.py:41-72    quaternion_linear(x, wr, wi, wj, wk)
+ *   quaternion/linear.py:120-124  QuaternionLinear.forward (bias added)
+ *   quaternion/planar.py:39-61    quaternion_linear_naive   (same math, K1)
+ *   quaternion/planar.py:100-129  quaternion_linear_planar  (same math, K2)
+ *   quaternion/lora.py:60-63      LoRAQuaternionLinear.forward (fused residual)
+ *   kernels/cuda/quaternion_linear.cu:117-159  quaternion_linear_forward (K4)
+ *   kernels/triton/quaternion.py:104-133       _launch (K3)
+ *
+ *   x      [M, 4*K_g], leading dimension ld_x (elements, >= 4*K_g)
+ *   wr..wk [N_g, K_g] each, leading dimension ld_w (>= K_g)
+ *   bias   [4*N_g] or NULL
+ *   lora_a [rank, 4*K_g] contiguous, lora_b [4*N_g, rank] contiguous, or both
+ *          NULL with rank = 0; lora_scale = alpha / rank
+ *   y      [M, 4*N_g], leading dimension ld_y (>= 4*N_g); must not alias x
+ *   workspace: device buffer of at least qlin_workspace_size() bytes,
+ *          256-byte aligned (may be NULL when that size is 0)
+ * M = 0 is a no-op.  Accumulation is fp32; bf16/f16 outputs are rounded
+ * once, after bias and LoRA are added.
+ */
+int qlin_forward(int dtype,
+                 const void* x, int64_t ld_x,
+                 const void* wr, const void* wi, const void* wj, const void* wk,
+                 int64_t ld_w,
+                 const void* bias,
+                 const void* lora_a, const void* lora_b, int rank, float lora_scale,
+                 void* y, int64_t ld_y,
+                 int64_t M, int64_t K_g, int64_t N_g,
+                 void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* qlin_forward with an explicit kernel choice (QLIN_ALGO_*); used by tests
+ * to run both device paths on the same inputs.  QLIN_ALGO_TC returns
+ * QLIN_ERR_ALIGN when the shape or pointers do not meet its TMA rules. */
+int qlin_forward_ex(int dtype,
+                    const void* x, int64_t ld_x,
+                    const void* wr, const void* wi, const void* wj, const void* wk,
+                    int64_t ld_w,
+                    const void* bias,
+                    const void* lora_a, const void* lora_b, int rank, float lora_scale,
+                    void* y, int64_t ld_y,
+                    int64_t M, int64_t K_g, int64_t N_g,
+                    void* workspace, size_t workspace_bytes,
+                    int algo, void* stream);
+
+/* Which algorithm qlin_forward would pick for this problem (QLIN_ALGO_*). */
+int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank);
+
+/*
+ * Device-side error word.  Every wait inside the kernels (TMA arrival, MMA
+ * completion) is bounded; a wait that runs out records QLIN_ERR_TIMEOUT here
+ * and the kernel returns without further work instead of hanging the GPU.
+ * qlin_get_device_error synchronises `stream`, reads the word for the
+ * current device and clears it when `clear` is non-zero.
+ */
+int qlin_get_device_error(void* stream, int clear, int* device_status);
+
+/*
+ * Column gather for the column-partitioned layer: src holds G shards
+ * [G, M, n_shard] (the layout an all-gather of per-rank [M, n_shard]
+ * outputs produces); dst receives [M, G * n_shard] with leading dimension
+ * ld_dst.  Element size = that of dtype.
+ */
+int qlin_gather_columns(int dtype, const void* src, void* dst, int64_t G, int64_t M,
+                        int64_t n_shard, int64_t ld_dst, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QLIN_B200_H */

@@ -1,0 +1,143 @@
+"""ctypes binding of the in-tree C ABI (``lib/libqlin_b200.so``).
+
+This is the only way the package reaches the device: there is no CPU path and
+no fallback.  A missing or unloadable library raises ``RuntimeError`` at the
+first call.  Status codes from ``include/qlin_b200.h`` become exceptions with
+the reference's classes: shape errors are ``ValueError``
+(``quaternion/packing.py:45-52``), everything else ``RuntimeError``
+(``kernels/cuda/quaternion_linear.cu:120-128,153``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libqlin_b200.so")
+
+F32, BF16, F16 = 0, 1, 2
+ALGO_AUTO, ALGO_SIMT, ALGO_TC = 0, 1, 2
+
+OK = 0
+ERR_SHAPE = 1
+ERR_TIMEOUT = 7
+
+_DTYPE_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+_lib = None
+_lock = threading.Lock()
+
+EXPORTED = (
+    "qlin_status_string",
+    "qlin_abi_version",
+    "qlin_workspace_size",
+    "qlin_forward",
+    "qlin_forward_ex",
+    "qlin_select_algo",
+    "qlin_get_device_error",
+    "qlin_gather_columns",
+)
+
+
+def load(path: str | None = None):
+    """Load (once) and return the ctypes handle of the C ABI library."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise RuntimeError(
+                f"quaternion linear CUDA library not built ({p}); run "
+                "`python quaternion-based-math-1_b200/build.py` (nvcc, sm_100a)"
+            )
+        lib = ctypes.CDLL(p)
+        P, I64, I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+        lib.qlin_status_string.argtypes = [I]
+        lib.qlin_status_string.restype = ctypes.c_char_p
+        lib.qlin_abi_version.restype = I
+        lib.qlin_workspace_size.argtypes = [I, I64, I64, I64, I, ctypes.POINTER(ctypes.c_size_t)]
+        lib.qlin_workspace_size.restype = I
+        fwd = [I, P, I64, P, P, P, P, I64, P, P, P, I, ctypes.c_float, P, I64, I64, I64, I64,
+               P, ctypes.c_size_t]
+        lib.qlin_forward.argtypes = fwd + [P]
+        lib.qlin_forward.restype = I
+        lib.qlin_forward_ex.argtypes = fwd + [I, P]
+        lib.qlin_forward_ex.restype = I
+        lib.qlin_select_algo.argtypes = [I, I64, I64, I64, I]
+        lib.qlin_select_algo.restype = I
+        lib.qlin_get_device_error.argtypes = [P, I, ctypes.POINTER(I)]
+        lib.qlin_get_device_error.restype = I
+        lib.qlin_gather_columns.argtypes = [I, P, P, I64, I64, I64, I64, P]
+        lib.qlin_gather_columns.restype = I
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def status_string(code: int) -> str:
+    return load().qlin_status_string(int(code)).decode()
+
+
+def check(code: int, what: str) -> None:
+    if code == OK:
+        return
+    msg = f"{what}: {status_string(code)} (status {code})"
+    if code == ERR_SHAPE:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dtype]
+    except KeyError:
+        raise RuntimeError(
+            f"unsupported dtype {dtype}; the B200 quaternion kernels take float32, bfloat16 "
+            "or float16"
+        ) from None
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def workspace_size(dtype: torch.dtype, M: int, K_g: int, N_g: int, rank: int) -> int:
+    n = ctypes.c_size_t(0)
+    check(load().qlin_workspace_size(dtype_code(dtype), M, K_g, N_g, rank, ctypes.byref(n)),
+          "qlin_workspace_size")
+    return int(n.value)
+
+
+def device_error(device: torch.device | None = None, clear: bool = True) -> int:
+    """Synchronise the current stream and return (and clear) the device error word."""
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    st = ctypes.c_int(0)
+    with torch.cuda.device(dev):
+        check(load().qlin_get_device_error(stream_handle(dev), int(clear), ctypes.byref(st)),
+              "qlin_get_device_error")
+    return int(st.value)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def forward_raw(x2, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y2, ld_y,
+                M, K_g, N_g, algo=ALGO_AUTO):
+    """Call ``qlin_forward_ex`` on prepared 2-D device tensors (see linear.py)."""
+    lib = load()
+    dev = x2.device
+    ws_bytes = workspace_size(x2.dtype, M, K_g, N_g, rank)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev) if ws_bytes else None
+    code = lib.qlin_forward_ex(
+        dtype_code(x2.dtype), _ptr(x2), ld_x, _ptr(w[0]), _ptr(w[1]), _ptr(w[2]), _ptr(w[3]), ld_w,
+        _ptr(bias), _ptr(lora_a), _ptr(lora_b), int(rank), float(lora_scale),
+        _ptr(y2), ld_y, M, K_g, N_g, _ptr(ws), ws_bytes, int(algo), stream_handle(dev),
+    )
+    check(code, "qlin_forward")
+    return y2

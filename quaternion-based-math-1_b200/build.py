@@ -1,0 +1,69 @@
+"""Build the in-tree shared library ``lib/libqlin_b200.so`` for sm_100a.
+
+The library exports the C ABI declared in ``include/qlin_b200.h``.  It links
+the CUDA runtime statically and resolves the one driver entry point it needs
+(``cuTensorMapEncodeTiled``) at run time, so it depends on nothing but the
+driver.  Run ``python quaternion-based-math-1_b200/build.py`` (or
+``__graft_entry__.build()``); nvcc cross-compiles without a GPU.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+LIB_DIR = os.path.join(PKG, "lib")
+LIB_PATH = os.path.join(LIB_DIR, "libqlin_b200.so")
+SOURCES = [os.path.join(CSRC, "qlin_abi.cu")]
+DEPENDS = SOURCES + [os.path.join(CSRC, f) for f in ("qlin_common.cuh", "qlin_simt.cuh", "qlin_tc.cuh")] + [
+    os.path.join(REPO, "include", "qlin_b200.h")
+]
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo", "-O3", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-shared", "-cudart", "static",
+    "-Xptxas", "-v",
+    "-I", os.path.join(REPO, "include"),
+]
+
+
+def find_nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def needs_build() -> bool:
+    if not os.path.exists(LIB_PATH):
+        return True
+    t = os.path.getmtime(LIB_PATH)
+    return any(os.path.getmtime(p) > t for p in DEPENDS)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and not needs_build():
+        return LIB_PATH
+    os.makedirs(LIB_DIR, exist_ok=True)
+    tmp = LIB_PATH + ".tmp"
+    cmd = [find_nvcc(), *NVCC_FLAGS, "-o", tmp, *SOURCES]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    log = os.path.join(LIB_DIR, "build.log")
+    with open(log, "w") as f:
+        f.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({res.returncode}); see {log}\n{res.stderr[-4000:]}")
+    os.replace(tmp, LIB_PATH)
+    if verbose:
+        print(res.stderr)
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose=True))

@@ -1,0 +1,452 @@
+// C ABI of the B200 quaternion linear forward (declarations: include/qlin_b200.h).
+//
+// Host responsibilities: argument validation with the reference's error
+// classes (shape -> QLIN_ERR_SHAPE, which the Python layer raises as
+// ValueError like quaternion/packing.py:45-52 and quaternion/linear.py:55-61),
+// kernel selection, workspace carving, TMA descriptor encoding and launch on
+// the caller's stream.  No exception crosses the ABI, nothing allocates.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "../../include/qlin_b200.h"
+#include "qlin_simt.cuh"
+#include "qlin_tc.cuh"
+
+namespace {
+
+using namespace qlin;
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  bool init = false;
+  int cc_major = 0, cc_minor = 0, num_sms = 0;
+  bool tc_attr_set[4] = {false, false, false, false};
+  int max_split[4] = {0, 0, 0, 0};  // largest cluster split found schedulable per N_TOK
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_mutex;
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QLIN_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.init) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return QLIN_ERR_LAUNCH;
+    d.cc_major = prop.major;
+    d.cc_minor = prop.minor;
+    d.num_sms = prop.multiProcessorCount;
+    d.init = true;
+  }
+  *out = &d;
+  return (d.cc_major == 10) ? QLIN_OK : QLIN_ERR_DEVICE;
+}
+
+int get_encoder() {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_encode) return QLIN_OK;
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !fn)
+    return QLIN_ERR_LAUNCH;
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return QLIN_OK;
+}
+
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+inline size_t elem_size(int dtype) { return dtype == QLIN_F32 ? 4 : 2; }
+
+// Workspace pieces.  TC path: planar x (4 * M * K_g 16-bit) + scaled LoRA t
+// ([M, round_up(rank, 8)] 16-bit).  SIMT path: LoRA t ([M, rank] fp32).
+struct WsLayout {
+  size_t xp_off = 0, xp_bytes = 0, t_off = 0, t_bytes = 0, tf_off = 0, tf_bytes = 0, total = 0;
+  int64_t ld_t = 0;
+};
+WsLayout ws_layout(int dtype, int64_t M, int64_t K_g, int rank) {
+  WsLayout w;
+  size_t off = 0;
+  if (dtype != QLIN_F32) {
+    w.xp_off = off;
+    w.xp_bytes = (size_t)(4 * M * K_g * 2);
+    off = (size_t)round_up((int64_t)(off + w.xp_bytes), 256);
+    if (rank > 0) {
+      w.ld_t = round_up(rank, 8);
+      w.t_off = off;
+      w.t_bytes = (size_t)(M * w.ld_t * 2);
+      off = (size_t)round_up((int64_t)(off + w.t_bytes), 256);
+    }
+  }
+  if (rank > 0) {
+    w.tf_off = off;
+    w.tf_bytes = (size_t)(M * rank * 4);
+    off = (size_t)round_up((int64_t)(off + w.tf_bytes), 256);
+  }
+  w.total = off;
+  return w;
+}
+
+int validate(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi, const void* wj,
+             const void* wk, int64_t ld_w, const void* lora_a, const void* lora_b, int rank,
+             const void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g) {
+  if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
+  if (M < 0 || K_g <= 0 || N_g <= 0 || rank < 0) return QLIN_ERR_SHAPE;
+  if (ld_x < 4 * K_g || ld_w < K_g || ld_y < 4 * N_g) return QLIN_ERR_SHAPE;
+  if (M > INT32_MAX || N_g > INT32_MAX / 4 || K_g > INT32_MAX / 4) return QLIN_ERR_SHAPE;
+  if (M == 0) return QLIN_OK;
+  if (!x || !wr || !wi || !wj || !wk || !y) return QLIN_ERR_ARG;
+  if (rank > 0 && (!lora_a || !lora_b)) return QLIN_ERR_ARG;
+  return QLIN_OK;
+}
+
+bool tc_eligible(int dtype, const void* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
+                 const void* lora_b, int rank, const void* y, int64_t ld_y, int64_t K_g) {
+  if (dtype == QLIN_F32) return false;
+  if (K_g % 8 != 0 || ld_x % 8 != 0 || ld_w % 8 != 0 || ld_y % 4 != 0) return false;
+  if (!aligned(x, 16) || !aligned(y, 8)) return false;
+  for (int p = 0; p < 4; ++p)
+    if (!aligned(w[p], 16)) return false;
+  if (rank > 0 && (rank % 8 != 0 || !aligned(lora_b, 16))) return false;
+  return true;
+}
+
+int select_algo(int dtype) { return dtype == QLIN_F32 ? QLIN_ALGO_SIMT : QLIN_ALGO_TC; }
+
+int n_tok_for(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128)); }
+int n_tok_index(int n_tok) { return n_tok == 16 ? 0 : (n_tok == 32 ? 1 : (n_tok == 64 ? 2 : 3)); }
+
+CUresult encode(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* base, const cuuint64_t* dims,
+                const cuuint64_t* strides, const cuuint32_t* box) {
+  cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(map, dt, (cuuint32_t)rank, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <typename T, int N_TOK>
+int launch_tc_impl(DeviceInfo* dev, int dev_slot, const CUtensorMap* maps, const TcParams& base_prm,
+                   int64_t M, int64_t N_g, cudaStream_t stream) {
+  using Cfg = TcCfg<N_TOK>;
+  auto kernel = qlin_tc_kernel<T, N_TOK>;
+  const int ti = n_tok_index(N_TOK);
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!dev->tc_attr_set[ti]) {
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
+          cudaSuccess)
+        return QLIN_ERR_LAUNCH;
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        cudaGetLastError();  // stays limited to portable cluster sizes
+      // Largest power-of-two cluster (<= 16) that the device can schedule.
+      int best = 1;
+      for (int s = 2; s <= 16; s *= 2) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(s, 1, 1);
+        cfg.blockDim = dim3(kTcThreads, 1, 1);
+        cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = s;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) == cudaSuccess && n >= 1)
+          best = s;
+        else
+          cudaGetLastError();
+      }
+      dev->max_split[ti] = Cfg::kAllowSplit ? best : 1;
+      dev->tc_attr_set[ti] = true;
+    }
+  }
+  (void)dev_slot;
+  TcParams prm = base_prm;
+  const int64_t o_blocks = (N_g + kTcBlockO - 1) / kTcBlockO;
+  const int64_t t_blocks = (M + N_TOK - 1) / N_TOK;
+  if (o_blocks > 65535 || t_blocks > 65535) return QLIN_ERR_SHAPE;
+  const int64_t tiles = o_blocks * t_blocks;
+  int split = 1;
+  while (split * 2 <= dev->max_split[ti] && tiles * split * 2 <= dev->num_sms &&
+         prm.num_chunks >= split * 2)
+    split *= 2;
+  prm.split_k = split;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)split, (unsigned)o_blocks, (unsigned)t_blocks);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  if (split > 1) {
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = split;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], maps[3], maps[4],
+                                     maps[5], maps[6], prm);
+  return e == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+}
+
+template <typename T>
+int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
+           const T* bias, const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y,
+           int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, uint8_t* ws, cudaStream_t stream) {
+  if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
+  const CUtensorMapDataType dt =
+      std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const WsLayout L = ws_layout(QLIN_BF16, M, K_g, rank);
+  T* xp = reinterpret_cast<T*>(ws + L.xp_off);
+  T* t = rank > 0 ? reinterpret_cast<T*>(ws + L.t_off) : nullptr;
+  const int n_tok = n_tok_for(M);
+
+  // 1. component planes of x
+  {
+    const int64_t threads = M * (K_g / 8);
+    const int64_t blocks = (threads + 255) / 256;
+    qlin_planarize_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(x, ld_x, xp, M, K_g);
+  }
+  // 2. LoRA down projection, scaled and rounded like the operands
+  if (rank > 0) {
+    dim3 grid((unsigned)((M + 15) / 16), (unsigned)((rank + 7) / 8));
+    qlin_lora_down_kernel<T, 16><<<grid, 256, 0, stream>>>(x, ld_x, lora_a, rank, M, 4 * K_g,
+                                                            lora_scale, nullptr, t, L.ld_t);
+  }
+  // 3. tensor maps
+  CUtensorMap maps[7];
+  std::memset(maps, 0, sizeof(maps));
+  for (int p = 0; p < 4; ++p) {
+    cuuint64_t dims[2] = {(cuuint64_t)K_g, (cuuint64_t)N_g};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld_w * 2)};
+    cuuint32_t box[2] = {kTcChunk, kTcBlockO};
+    if (encode(&maps[p], dt, 2, const_cast<void*>(w[p]), dims, strides, box) != CUDA_SUCCESS)
+      return QLIN_ERR_ALIGN;
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)K_g, (cuuint64_t)M, 4};
+    cuuint64_t strides[2] = {(cuuint64_t)(K_g * 2), (cuuint64_t)(M * K_g * 2)};
+    cuuint32_t box[3] = {kTcChunk, (cuuint32_t)n_tok, 1};
+    if (encode(&maps[4], dt, 3, xp, dims, strides, box) != CUDA_SUCCESS) return QLIN_ERR_ALIGN;
+  }
+  int lora_chunks = 0;
+  if (rank > 0) {
+    cuuint64_t dims[3] = {(cuuint64_t)rank, 4, (cuuint64_t)N_g};
+    cuuint64_t strides[2] = {(cuuint64_t)(rank * 2), (cuuint64_t)(4 * rank * 2)};
+    cuuint32_t box[3] = {kTcChunk, 1, kTcBlockO};
+    if (encode(&maps[5], dt, 3, const_cast<T*>(lora_b), dims, strides, box) != CUDA_SUCCESS)
+      return QLIN_ERR_ALIGN;
+    cuuint64_t tdims[2] = {(cuuint64_t)rank, (cuuint64_t)M};
+    cuuint64_t tstrides[1] = {(cuuint64_t)(L.ld_t * 2)};
+    cuuint32_t tbox[2] = {kTcChunk, (cuuint32_t)n_tok};
+    if (encode(&maps[6], dt, 2, t, tdims, tstrides, tbox) != CUDA_SUCCESS) return QLIN_ERR_ALIGN;
+    lora_chunks = (int)((rank + kTcChunk - 1) / kTcChunk);
+  }
+  TcParams prm;
+  prm.bias = bias;
+  prm.y = y;
+  prm.ld_y = ld_y;
+  prm.M = (int)M;
+  prm.N_g = (int)N_g;
+  prm.num_chunks = (int)((K_g + kTcChunk - 1) / kTcChunk);
+  prm.lora_chunks = lora_chunks;
+  prm.split_k = 1;
+  switch (n_tok) {
+    case 16: return launch_tc_impl<T, 16>(dev, 0, maps, prm, M, N_g, stream);
+    case 32: return launch_tc_impl<T, 32>(dev, 0, maps, prm, M, N_g, stream);
+    case 64: return launch_tc_impl<T, 64>(dev, 0, maps, prm, M, N_g, stream);
+    default: return launch_tc_impl<T, 128>(dev, 0, maps, prm, M, N_g, stream);
+  }
+}
+
+template <typename T>
+int run_simt(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
+             const T* bias, const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y,
+             int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, uint8_t* ws, cudaStream_t stream) {
+  const WsLayout L = ws_layout(QLIN_F32, M, K_g, rank);
+  float* tf = nullptr;
+  if (rank > 0) {
+    tf = reinterpret_cast<float*>(ws + L.tf_off);
+    dim3 grid((unsigned)((M + 15) / 16), (unsigned)((rank + 7) / 8));
+    qlin_lora_down_kernel<T, 16><<<grid, 256, 0, stream>>>(x, ld_x, lora_a, rank, M, 4 * K_g,
+                                                            lora_scale, tf, nullptr, 0);
+  }
+  const T* wr = static_cast<const T*>(w[0]);
+  const T* wi = static_cast<const T*>(w[1]);
+  const T* wj = static_cast<const T*>(w[2]);
+  const T* wk = static_cast<const T*>(w[3]);
+  const int64_t big_tiles = ((M + 31) / 32) * ((N_g + 31) / 32);
+  if (big_tiles >= dev->num_sms) {
+    dim3 grid((unsigned)((N_g + 31) / 32), (unsigned)((M + 31) / 32));
+    if (grid.y > 65535) return QLIN_ERR_SHAPE;
+    qlin_simt_kernel<T, 32, 32, 16, 2, 2><<<grid, dim3(16, 16), 0, stream>>>(
+        x, ld_x, wr, wi, wj, wk, ld_w, bias, tf, lora_b, rank, lora_scale, y, ld_y, M, K_g, N_g);
+  } else {
+    dim3 grid((unsigned)((N_g + 15) / 16), (unsigned)((M + 15) / 16));
+    if (grid.y > 65535) return QLIN_ERR_SHAPE;
+    qlin_simt_kernel<T, 16, 16, 16, 1, 1><<<grid, dim3(16, 16), 0, stream>>>(
+        x, ld_x, wr, wi, wj, wk, ld_w, bias, tf, lora_b, rank, lora_scale, y, ld_y, M, K_g, N_g);
+  }
+  return QLIN_OK;
+}
+
+template <typename T>
+int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void* const w[4],
+             int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b, int rank,
+             float lora_scale, void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
+             uint8_t* ws, cudaStream_t stream) {
+  const T* xt = static_cast<const T*>(x);
+  const T* bt = static_cast<const T*>(bias);
+  const T* la = static_cast<const T*>(lora_a);
+  const T* lb = static_cast<const T*>(lora_b);
+  T* yt = static_cast<T*>(y);
+  if constexpr (std::is_same<T, float>::value) {
+    return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
+                       stream);
+  } else {
+    if (algo == QLIN_ALGO_TC)
+      return run_tc<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
+                       stream);
+    return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
+                       stream);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* qlin_status_string(int status) {
+  switch (status) {
+    case QLIN_OK: return "ok";
+    case QLIN_ERR_SHAPE: return "invalid shape or leading dimension";
+    case QLIN_ERR_DTYPE: return "unsupported dtype";
+    case QLIN_ERR_ALIGN: return "pointer or leading-dimension alignment not supported by this path";
+    case QLIN_ERR_WORKSPACE: return "workspace missing or too small";
+    case QLIN_ERR_LAUNCH: return "CUDA launch or runtime error";
+    case QLIN_ERR_DEVICE: return "current device is not sm_100 (B200 class)";
+    case QLIN_ERR_TIMEOUT: return "a bounded device-side wait ran out";
+    case QLIN_ERR_ARG: return "null pointer or invalid option";
+    default: return "unknown status";
+  }
+}
+
+int qlin_abi_version(void) { return 100; }
+
+int qlin_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, size_t* bytes) {
+  if (!bytes) return QLIN_ERR_ARG;
+  if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
+  if (M < 0 || K_g <= 0 || N_g <= 0 || rank < 0) return QLIN_ERR_SHAPE;
+  *bytes = ws_layout(dtype, M, K_g, rank).total;
+  return QLIN_OK;
+}
+
+int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
+  (void)M; (void)K_g; (void)N_g; (void)rank;
+  return select_algo(dtype);
+}
+
+int qlin_forward_ex(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi, const void* wj,
+                    const void* wk, int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b,
+                    int rank, float lora_scale, void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
+                    void* workspace, size_t workspace_bytes, int algo, void* stream) {
+  int st = validate(dtype, x, ld_x, wr, wi, wj, wk, ld_w, lora_a, lora_b, rank, y, ld_y, M, K_g, N_g);
+  if (st != QLIN_OK) return st;
+  if (M == 0) return QLIN_OK;
+  if (algo < QLIN_ALGO_AUTO || algo > QLIN_ALGO_TC) return QLIN_ERR_ARG;
+  if (rank == 0) lora_a = lora_b = nullptr;
+  DeviceInfo* dev = nullptr;
+  st = device_info(&dev);
+  if (st != QLIN_OK) return st;
+  const void* w[4] = {wr, wi, wj, wk};
+  if (algo == QLIN_ALGO_AUTO) {
+    algo = select_algo(dtype);
+    if (algo == QLIN_ALGO_TC && !tc_eligible(dtype, x, ld_x, w, ld_w, lora_b, rank, y, ld_y, K_g))
+      algo = QLIN_ALGO_SIMT;
+  } else if (algo == QLIN_ALGO_TC && !tc_eligible(dtype, x, ld_x, w, ld_w, lora_b, rank, y, ld_y, K_g)) {
+    return QLIN_ERR_ALIGN;
+  }
+  const WsLayout L = ws_layout(dtype, M, K_g, rank);
+  if (L.total > 0 && (!workspace || workspace_bytes < L.total || !aligned(workspace, 256)))
+    return QLIN_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaGetLastError();  // clear stale errors so the check below is this call's
+  switch (dtype) {
+    case QLIN_F32:
+      st = dispatch<float>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
+                           K_g, N_g, ws, s);
+      break;
+    case QLIN_BF16:
+      st = dispatch<__nv_bfloat16>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
+                                   ld_y, M, K_g, N_g, ws, s);
+      break;
+    default:
+      st = dispatch<__half>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
+                            K_g, N_g, ws, s);
+      break;
+  }
+  if (st != QLIN_OK) return st;
+  return cudaGetLastError() == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+}
+
+int qlin_forward(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi, const void* wj,
+                 const void* wk, int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b,
+                 int rank, float lora_scale, void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  return qlin_forward_ex(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
+                         ld_y, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_AUTO, stream);
+}
+
+int qlin_get_device_error(void* stream, int clear, int* device_status) {
+  if (!device_status) return QLIN_ERR_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return QLIN_ERR_LAUNCH;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, qlin::g_device_error, sizeof(int)) != cudaSuccess) return QLIN_ERR_LAUNCH;
+  if (clear && v != 0) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(qlin::g_device_error, &zero, sizeof(int)) != cudaSuccess) return QLIN_ERR_LAUNCH;
+  }
+  *device_status = v;
+  return QLIN_OK;
+}
+
+int qlin_gather_columns(int dtype, const void* src, void* dst, int64_t G, int64_t M, int64_t n_shard,
+                        int64_t ld_dst, void* stream) {
+  if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
+  if (G <= 0 || M < 0 || n_shard <= 0 || ld_dst < G * n_shard) return QLIN_ERR_SHAPE;
+  if (M == 0) return QLIN_OK;
+  if (!src || !dst) return QLIN_ERR_ARG;
+  DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st != QLIN_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t total = G * M * n_shard;
+  const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, (int64_t)dev->num_sms * 16);
+  cudaGetLastError();
+  if (elem_size(dtype) == 4)
+    qlin_gather_kernel<uint32_t><<<blocks, 256, 0, s>>>(static_cast<const uint32_t*>(src),
+                                                        static_cast<uint32_t*>(dst), G, M, n_shard, ld_dst);
+  else
+    qlin_gather_kernel<uint16_t><<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(src),
+                                                        static_cast<uint16_t*>(dst), G, M, n_shard, ld_dst);
+  return cudaGetLastError() == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+}
+
+}  // extern "C"

@@ -1,0 +1,73 @@
+"""The C ABI library loads without a GPU, exports every function that
+include/qlin_b200.h declares, and validates arguments before touching the
+device (so shape errors surface with the reference's error class)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+
+
+def _declared_functions():
+    src = open(os.path.join(REPO, "include", "qlin_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(qlin_\w+)\s*\(", src)))
+
+
+def test_header_declares_the_entry_points():
+    names = _declared_functions()
+    for n in ("qlin_forward", "qlin_forward_ex", "qlin_workspace_size", "qlin_gather_columns",
+              "qlin_get_device_error", "qlin_status_string"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(qb):
+    lib = qb._lib.load()
+    raw = ctypes.CDLL(qb._lib.LIB_PATH)
+    for name in _declared_functions():
+        assert hasattr(raw, name), f"{name} not exported"
+    assert set(qb._lib.EXPORTED) <= set(_declared_functions())
+    assert lib.qlin_abi_version() >= 100
+
+
+def test_status_strings(qb):
+    for code in range(0, 9):
+        assert qb._lib.status_string(code)
+    assert qb._lib.status_string(1).startswith("invalid shape")
+
+
+def test_workspace_size(qb):
+    import torch
+    assert qb._lib.workspace_size(torch.float32, 128, 256, 256, 0) == 0
+    ws = qb._lib.workspace_size(torch.bfloat16, 16, 1024, 1024, 32)
+    assert ws >= 4 * 16 * 1024 * 2 + 16 * 32 * 2
+    with pytest.raises(ValueError):
+        qb._lib.workspace_size(torch.bfloat16, -1, 1024, 1024, 0)
+
+
+def test_shape_errors_are_reported_before_device_use(qb):
+    lib = qb._lib.load()
+    P = None
+    # ld_x < 4*K_g -> QLIN_ERR_SHAPE, no CUDA call needed
+    code = lib.qlin_forward(1, 1, 10, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, P)
+    assert code == 1
+    # M == 0 is a no-op that succeeds without a device
+    code = lib.qlin_forward(1, P, 16, P, P, P, P, 4, P, P, P, 0, 0.0, P, 16, 0, 4, 4, P, 0, P)
+    assert code == 0
+    # unknown dtype
+    code = lib.qlin_forward(7, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, P)
+    assert code == 2
+    # rank > 0 without LoRA pointers
+    code = lib.qlin_forward(1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 8, 1.0, 1, 16, 2, 4, 4, P, 0, P)
+    assert code == 8
+    assert lib.qlin_gather_columns(1, P, P, 0, 1, 1, 1, P) == 1
+
+
+def test_shape_status_maps_to_valueerror(qb):
+    with pytest.raises(ValueError):
+        qb._lib.check(1, "x")
+    with pytest.raises(RuntimeError):
+        qb._lib.check(5, "x")
