@@ -176,7 +176,7 @@ class ClockSampler:
 # device timing
 # ---------------------------------------------------------------------------
 
-def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES):
+def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES, flags=0):
     """Device copies rotated to exceed L2, preallocated outputs and workspace."""
     dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
     nbytes, _ = algorithmic_work(lay)
@@ -204,21 +204,22 @@ def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES):
     def call(i):
         c = copies[i % ncopy]
         y = ys[i % ncopy]
-        st = lib.qlin_forward(code, c["x"].data_ptr(), 4 * K_g, *(w.data_ptr() for w in c["w"]), K_g,
-                              c["b"].data_ptr() if c["b"] is not None else None,
-                              c["la"].data_ptr() if c["la"] is not None else None,
-                              c["lb"].data_ptr() if c["lb"] is not None else None,
-                              rank, float(lay.lora_scale), y.data_ptr(), 4 * N_g, M, K_g, N_g,
-                              ws.data_ptr(), ws_bytes, stream_of(dev))
+        st = lib.qlin_forward_ex(code, c["x"].data_ptr(), 4 * K_g, *(w.data_ptr() for w in c["w"]), K_g,
+                                 c["b"].data_ptr() if c["b"] is not None else None,
+                                 c["la"].data_ptr() if c["la"] is not None else None,
+                                 c["lb"].data_ptr() if c["lb"] is not None else None,
+                                 rank, float(lay.lora_scale), y.data_ptr(), 4 * N_g, M, K_g, N_g,
+                                 ws.data_ptr(), ws_bytes, 0, flags, stream_of(dev))
         if st != 0:
             qb._lib.check(st, "qlin_forward")
 
-    launches = 2 + (1 if rank else 0) if lay.dtype != "f32" else 1 + (1 if rank else 0)
-    return call, ncopy, copies, ys, launches
+    with torch.cuda.device(dev):
+        plan = qb._lib.plan(dt, M, K_g, N_g, rank)
+    return call, ncopy, copies, ys, plan
 
 
-def time_device(qb, lay, torch, dev, K, W, dist=None):
-    call, ncopy, copies, ys, launches = _device_case(qb, lay, torch, dev)
+def time_device(qb, lay, torch, dev, K, W, dist=None, flags=0):
+    call, ncopy, copies, ys, plan = _device_case(qb, lay, torch, dev, flags=flags)
     for i in range(W):
         call(i)
     torch.cuda.synchronize(dev)
@@ -248,7 +249,7 @@ def time_device(qb, lay, torch, dev, K, W, dist=None):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     del graph
-    return ms, ncopy, launches
+    return ms, ncopy, plan
 
 
 def time_dense(lay, torch, dev, K, W):
@@ -426,7 +427,8 @@ def main():
 
     nbytes, flops = algorithmic_work(lay)
     with ClockSampler(local) as clk:
-        ms, ncopy, launches = time_device(qb, lay, torch, dev, K, W, dist)
+        ms, ncopy, plan = time_device(qb, lay, torch, dev, K, W, dist)
+    launches = plan["launches"]
     us_call = ms * 1e3 / K
     clocks = clk.summary()
     bound = WORKLOADS[args.workload]["bound"]
@@ -454,7 +456,13 @@ def main():
         "roofline": roof,
         "clocks": clocks,
         "gpu_launches": K * launches,
+        "plan": plan,
     }
+
+    # Same workload with the weights declared static (inference): each call
+    # streams its weights while the previous call's kernels finish.
+    sms, _, _ = time_device(qb, lay, torch, dev, K, W, dist, flags=qb._lib.FLAG_STATIC_WEIGHTS)
+    result["static_weights_us_per_call"] = sms * 1e3 / K / world
 
     e2e_us, h2d, d2h = time_e2e(qb, lay, torch, dev, K, W)
     if dist is not None:
@@ -476,10 +484,11 @@ def main():
                     continue
                 xl = _layer(wl, name)
                 kk = K if WORKLOADS[name]["bound"] == "hbm" else max(3, min(K, 200))
-                xms, xcopy, xl_launch = time_device(qb, xl, torch, dev, kk, W)
+                xms, xcopy, xplan = time_device(qb, xl, torch, dev, kk, W)
                 xus = xms * 1e3 / kk
                 xb, xf = algorithmic_work(xl)
-                entry = {"us_per_call": xus, "steps": kk, "config": workload_config(name, xl, xcopy),
+                entry = {"us_per_call": xus, "steps": kk, "plan": xplan,
+                         "config": workload_config(name, xl, xcopy),
                          "dense_cublas_us": time_dense(xl, torch, dev, kk, W)}
                 if WORKLOADS[name]["bound"] == "hbm":
                     a = xb / (xus * 1e-6) / 1e9

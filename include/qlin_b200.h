@@ -50,6 +50,19 @@ enum {
   QLIN_ALGO_TC = 2      /* TMA + tcgen05/TMEM kernel: bf16/f16, aligned shapes  */
 };
 
+/*
+ * Flags of qlin_forward_ex.
+ *
+ * QLIN_FLAG_STATIC_WEIGHTS: the caller guarantees that no work queued earlier
+ * on the stream writes wr..wk, bias or lora_b (inference with fixed
+ * weights).  The kernels then start streaming the weights while the previous
+ * kernel of the stream is still finishing (programmatic dependent launch);
+ * x, the workspace and y are still only touched after it completed.
+ * Without the flag every kernel waits for its predecessor before reading
+ * any memory (plain stream order), overlapping only its launch and set-up.
+ */
+enum { QLIN_FLAG_STATIC_WEIGHTS = 1 };
+
 /* Human-readable name of a status code (static storage). */
 const char* qlin_status_string(int status);
 
@@ -59,8 +72,9 @@ int qlin_abi_version(void);
 /*
  * Bytes of device workspace qlin_forward needs for this problem (0 for some
  * paths).  rank = LoRA rank (0 = no LoRA).  The workspace holds the planar
- * copy of x and the LoRA down projection; it is only used during the call's
- * kernels, so one buffer can be reused by calls on the same stream.
+ * copy of x (M > 64), the LoRA down projection and the fp32 partial sums of
+ * a K split; it is only used during the call's kernels and needs no
+ * initialisation, so one buffer can be reused by calls on the same stream.
  */
 int qlin_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank,
                         size_t* bytes);
@@ -99,9 +113,10 @@ int qlin_forward(int dtype,
                  void* workspace, size_t workspace_bytes,
                  void* stream);
 
-/* qlin_forward with an explicit kernel choice (QLIN_ALGO_*); used by tests
- * to run both device paths on the same inputs.  QLIN_ALGO_TC returns
- * QLIN_ERR_ALIGN when the shape or pointers do not meet its TMA rules. */
+/* qlin_forward with an explicit kernel choice (QLIN_ALGO_*; tests run both
+ * device paths on the same inputs) and flags (QLIN_FLAG_*).  QLIN_ALGO_TC
+ * returns QLIN_ERR_ALIGN when the shape or pointers do not meet its TMA
+ * rules. */
 int qlin_forward_ex(int dtype,
                     const void* x, int64_t ld_x,
                     const void* wr, const void* wi, const void* wj, const void* wk,
@@ -111,7 +126,17 @@ int qlin_forward_ex(int dtype,
                     void* y, int64_t ld_y,
                     int64_t M, int64_t K_g, int64_t N_g,
                     void* workspace, size_t workspace_bytes,
-                    int algo, void* stream);
+                    int algo, int flags, void* stream);
+
+/*
+ * Launch plan qlin_forward uses for this problem on the current device
+ * (diagnostics; no reference counterpart).  Fills every non-null output:
+ * algo (QLIN_ALGO_*, assuming aligned pointers), tokens per tensor-core tile,
+ * K split (CTAs sharing one output tile), kernel launches per call, and how
+ * many CTAs of the tensor-core kernel the device keeps resident at once.
+ */
+int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int* algo,
+              int* tile_tokens, int* split_k, int* launches, int* resident_ctas);
 
 /* Which algorithm qlin_forward would pick for this problem (QLIN_ALGO_*). */
 int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank);

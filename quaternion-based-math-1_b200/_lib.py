@@ -21,6 +21,7 @@ LIB_PATH = os.path.join(PKG_DIR, "lib", "libqlin_b200.so")
 
 F32, BF16, F16 = 0, 1, 2
 ALGO_AUTO, ALGO_SIMT, ALGO_TC = 0, 1, 2
+FLAG_STATIC_WEIGHTS = 1
 
 OK = 0
 ERR_SHAPE = 1
@@ -38,6 +39,7 @@ EXPORTED = (
     "qlin_forward",
     "qlin_forward_ex",
     "qlin_select_algo",
+    "qlin_plan",
     "qlin_get_device_error",
     "qlin_gather_columns",
 )
@@ -66,10 +68,13 @@ def load(path: str | None = None):
                P, ctypes.c_size_t]
         lib.qlin_forward.argtypes = fwd + [P]
         lib.qlin_forward.restype = I
-        lib.qlin_forward_ex.argtypes = fwd + [I, P]
+        lib.qlin_forward_ex.argtypes = fwd + [I, I, P]
         lib.qlin_forward_ex.restype = I
         lib.qlin_select_algo.argtypes = [I, I64, I64, I64, I]
         lib.qlin_select_algo.restype = I
+        IP = ctypes.POINTER(I)
+        lib.qlin_plan.argtypes = [I, I64, I64, I64, I, IP, IP, IP, IP, IP]
+        lib.qlin_plan.restype = I
         lib.qlin_get_device_error.argtypes = [P, I, ctypes.POINTER(I)]
         lib.qlin_get_device_error.restype = I
         lib.qlin_gather_columns.argtypes = [I, P, P, I64, I64, I64, I64, P]
@@ -123,12 +128,22 @@ def device_error(device: torch.device | None = None, clear: bool = True) -> int:
     return int(st.value)
 
 
+def plan(dtype: torch.dtype, M: int, K_g: int, N_g: int, rank: int) -> dict:
+    """Launch plan of qlin_forward on the current device (see qlin_plan)."""
+    outs = [ctypes.c_int(0) for _ in range(5)]
+    check(load().qlin_plan(dtype_code(dtype), M, K_g, N_g, rank, *(ctypes.byref(o) for o in outs)),
+          "qlin_plan")
+    algo, tok, split, launches, resident = (o.value for o in outs)
+    return {"algo": {ALGO_SIMT: "simt", ALGO_TC: "tcgen05"}.get(algo, str(algo)),
+            "tile_tokens": tok, "split_k": split, "launches": launches, "resident_ctas": resident}
+
+
 def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
 def forward_raw(x2, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y2, ld_y,
-                M, K_g, N_g, algo=ALGO_AUTO):
+                M, K_g, N_g, algo=ALGO_AUTO, flags=0):
     """Call ``qlin_forward_ex`` on prepared 2-D device tensors (see linear.py)."""
     lib = load()
     dev = x2.device
@@ -137,7 +152,7 @@ def forward_raw(x2, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y2, l
     code = lib.qlin_forward_ex(
         dtype_code(x2.dtype), _ptr(x2), ld_x, _ptr(w[0]), _ptr(w[1]), _ptr(w[2]), _ptr(w[3]), ld_w,
         _ptr(bias), _ptr(lora_a), _ptr(lora_b), int(rank), float(lora_scale),
-        _ptr(y2), ld_y, M, K_g, N_g, _ptr(ws), ws_bytes, int(algo), stream_handle(dev),
+        _ptr(y2), ld_y, M, K_g, N_g, _ptr(ws), ws_bytes, int(algo), int(flags), stream_handle(dev),
     )
     check(code, "qlin_forward")
     return y2

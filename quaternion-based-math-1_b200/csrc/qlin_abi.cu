@@ -28,8 +28,10 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   bool init = false;
   int cc_major = 0, cc_minor = 0, num_sms = 0;
-  bool tc_attr_set[4] = {false, false, false, false};
-  int max_split[4] = {0, 0, 0, 0};  // largest cluster split found schedulable per N_TOK
+  // per (element type, N_TOK) kernel instance: attributes set, and how many
+  // CTAs of it the device keeps resident at once
+  bool tc_attr_set[2][4] = {{false, false, false, false}, {false, false, false, false}};
+  int resident[2][4] = {};
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mutex;
@@ -69,24 +71,59 @@ inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 inline size_t elem_size(int dtype) { return dtype == QLIN_F32 ? 4 : 2; }
 
-// Workspace pieces.  TC path: planar x (4 * M * K_g 16-bit) + scaled LoRA t
-// ([M, round_up(rank, 8)] 16-bit).  SIMT path: LoRA t ([M, rank] fp32).
+// Tokens up to which the tensor-core path builds its activation operand in
+// shared memory (stacked mode) instead of reading component planes.
+constexpr int64_t kStackMaxTokens = 64;
+
+// Upper bound of the SM count of an sm_100 part, used to size the split-K
+// partials before a device is known.
+constexpr int64_t kMaxSms = 160;
+
+int n_tok_for(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : (M <= kStackMaxTokens ? 64 : 128)); }
+int n_tok_index(int n_tok) { return n_tok == 16 ? 0 : (n_tok == 32 ? 1 : (n_tok == 64 ? 2 : 3)); }
+
+// Largest K split the tensor-core path uses for this problem on a device with
+// `sms` SMs: all CTAs of all splits of all tiles fit in one wave, every CTA
+// keeps at least one K chunk, at most kTcMaxSplit; no split when the tiles
+// alone fill half the device.
+int max_split_for(int64_t M, int64_t K_g, int64_t N_g, int64_t sms) {
+  const int64_t n_tok = n_tok_for(M);
+  const int64_t tiles = ((N_g + kTcBlockO - 1) / kTcBlockO) * ((M + n_tok - 1) / n_tok);
+  const int64_t chunks = (K_g + kTcChunk - 1) / kTcChunk;
+  if (tiles * 2 > sms) return 1;
+  const int64_t s = std::min<int64_t>({(int64_t)kTcMaxSplit, chunks, std::max<int64_t>(1, sms / tiles)});
+  return (int)std::max<int64_t>(1, s);
+}
+
+// Workspace pieces.  Tensor-core path: planar x (4 * M * K_g 16-bit, M > 64),
+// scaled LoRA t ([M, round_up(rank, 8)] 16-bit), split-K partials (fp32 x4 per
+// split, tile, token and row).  CUDA-core path: LoRA t ([M, rank] fp32).
 struct WsLayout {
-  size_t xp_off = 0, xp_bytes = 0, t_off = 0, t_bytes = 0, tf_off = 0, tf_bytes = 0, total = 0;
+  size_t xp_off = 0, xp_bytes = 0, t_off = 0, t_bytes = 0, tf_off = 0, tf_bytes = 0;
+  size_t part_off = 0, part_bytes = 0, total = 0;
   int64_t ld_t = 0;
 };
-WsLayout ws_layout(int dtype, int64_t M, int64_t K_g, int rank) {
+
+WsLayout ws_layout(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
   WsLayout w;
   size_t off = 0;
   if (dtype != QLIN_F32) {
     w.xp_off = off;
-    w.xp_bytes = (size_t)(4 * M * K_g * 2);
+    w.xp_bytes = M > kStackMaxTokens ? (size_t)(4 * M * K_g * 2) : 0;
     off = (size_t)round_up((int64_t)(off + w.xp_bytes), 256);
     if (rank > 0) {
       w.ld_t = round_up(rank, 8);
       w.t_off = off;
       w.t_bytes = (size_t)(M * w.ld_t * 2);
       off = (size_t)round_up((int64_t)(off + w.t_bytes), 256);
+    }
+    const int split = max_split_for(M, K_g, N_g, kMaxSms);
+    if (split > 1) {
+      const int64_t n_tok = n_tok_for(M);
+      const int64_t tiles = ((N_g + kTcBlockO - 1) / kTcBlockO) * ((M + n_tok - 1) / n_tok);
+      w.part_off = off;
+      w.part_bytes = (size_t)(split * tiles * n_tok * kTcBlockO * 16);
+      off = (size_t)round_up((int64_t)(off + w.part_bytes), 256);
     }
   }
   if (rank > 0) {
@@ -112,20 +149,18 @@ int validate(int dtype, const void* x, int64_t ld_x, const void* wr, const void*
 }
 
 bool tc_eligible(int dtype, const void* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
-                 const void* lora_b, int rank, const void* y, int64_t ld_y, int64_t K_g) {
+                 const void* lora_a, const void* lora_b, int rank, const void* y, int64_t ld_y,
+                 int64_t K_g) {
   if (dtype == QLIN_F32) return false;
   if (K_g % 8 != 0 || ld_x % 8 != 0 || ld_w % 8 != 0 || ld_y % 4 != 0) return false;
   if (!aligned(x, 16) || !aligned(y, 8)) return false;
   for (int p = 0; p < 4; ++p)
     if (!aligned(w[p], 16)) return false;
-  if (rank > 0 && (rank % 8 != 0 || !aligned(lora_b, 16))) return false;
+  if (rank > 0 && (rank % 8 != 0 || !aligned(lora_b, 16) || !aligned(lora_a, 16))) return false;
   return true;
 }
 
 int select_algo(int dtype) { return dtype == QLIN_F32 ? QLIN_ALGO_SIMT : QLIN_ALGO_TC; }
-
-int n_tok_for(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128)); }
-int n_tok_index(int n_tok) { return n_tok == 16 ? 0 : (n_tok == 32 ? 1 : (n_tok == 64 ? 2 : 3)); }
 
 CUresult encode(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* base, const cuuint64_t* dims,
                 const cuuint64_t* strides, const cuuint32_t* box) {
@@ -135,100 +170,132 @@ CUresult encode(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* base, 
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
+// Stacked activation operand for N_TOK <= 64 (decode-sized M), planes above.
+template <int N_TOK>
+constexpr bool kStackFor = N_TOK <= kStackMaxTokens;
+
 template <typename T, int N_TOK>
-int launch_tc_impl(DeviceInfo* dev, int dev_slot, const CUtensorMap* maps, const TcParams& base_prm,
-                   int64_t M, int64_t N_g, cudaStream_t stream) {
-  using Cfg = TcCfg<N_TOK>;
-  auto kernel = qlin_tc_kernel<T, N_TOK>;
+int ensure_tc_attrs(DeviceInfo* dev) {
+  using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>>;
+  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>>;
   const int ti = n_tok_index(N_TOK);
-  {
-    std::lock_guard<std::mutex> lock(g_mutex);
-    if (!dev->tc_attr_set[ti]) {
-      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
-          cudaSuccess)
-        return QLIN_ERR_LAUNCH;
-      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-        cudaGetLastError();  // stays limited to portable cluster sizes
-      // Largest power-of-two cluster (<= 16) that the device can schedule.
-      int best = 1;
-      for (int s = 2; s <= 16; s *= 2) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(s, 1, 1);
-        cfg.blockDim = dim3(kTcThreads, 1, 1);
-        cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-        cudaLaunchAttribute attr;
-        attr.id = cudaLaunchAttributeClusterDimension;
-        attr.val.clusterDim.x = s;
-        attr.val.clusterDim.y = 1;
-        attr.val.clusterDim.z = 1;
-        cfg.attrs = &attr;
-        cfg.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) == cudaSuccess && n >= 1)
-          best = s;
-        else
-          cudaGetLastError();
-      }
-      dev->max_split[ti] = Cfg::kAllowSplit ? best : 1;
-      dev->tc_attr_set[ti] = true;
-    }
-  }
-  (void)dev_slot;
+  const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (dev->tc_attr_set[di][ti]) return QLIN_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
+      cudaSuccess)
+    return QLIN_ERR_LAUNCH;
+  // Every kernel of the call prefers the full shared-memory carveout, so the
+  // SMs need no L1/shared reconfiguration between the prologue, the main
+  // kernel and the split-K reduction.
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
+      cudaFuncSetAttribute(qlin_splitk_reduce_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
+      cudaFuncSetAttribute(qlin_prologue_kernel<T, 1>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
+      cudaFuncSetAttribute(qlin_prologue_kernel<T, 8>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+    return QLIN_ERR_LAUNCH;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kTcThreads, Cfg::kSmemBytes) !=
+      cudaSuccess)
+    return QLIN_ERR_LAUNCH;
+  dev->resident[di][ti] = per_sm * dev->num_sms;
+  dev->tc_attr_set[di][ti] = true;
+  return QLIN_OK;
+}
+
+template <typename T, int N_TOK>
+int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& base_prm, int64_t M,
+                   int64_t K_g, int64_t N_g, float4* partials, cudaStream_t stream) {
+  using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>>;
+  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>>;
+  int st = ensure_tc_attrs<T, N_TOK>(dev);
+  if (st != QLIN_OK) return st;
   TcParams prm = base_prm;
   const int64_t o_blocks = (N_g + kTcBlockO - 1) / kTcBlockO;
   const int64_t t_blocks = (M + N_TOK - 1) / N_TOK;
   if (o_blocks > 65535 || t_blocks > 65535) return QLIN_ERR_SHAPE;
-  const int64_t tiles = o_blocks * t_blocks;
-  int split = 1;
-  while (split * 2 <= dev->max_split[ti] && tiles * split * 2 <= dev->num_sms &&
-         prm.num_chunks >= split * 2)
-    split *= 2;
+  const int split = max_split_for(M, K_g, N_g, dev->num_sms);
   prm.split_k = split;
+  prm.partials = split > 1 ? partials : nullptr;
+  if (split > 1 && !partials) return QLIN_ERR_WORKSPACE;
 
+  // Programmatic dependent launch: the kernel's set-up overlaps the tail of
+  // the previous kernel of the stream; it waits for that kernel
+  // (griddepcontrol.wait) before touching memory.
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)split, (unsigned)o_blocks, (unsigned)t_blocks);
   cfg.blockDim = dim3(kTcThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr;
-  if (split > 1) {
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = split;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-  }
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], maps[3], maps[4],
                                      maps[5], maps[6], prm);
-  return e == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+  if (e != cudaSuccess) return QLIN_ERR_LAUNCH;
+  if (split > 1) {
+    // The reduction is a programmatic dependent of the main kernel, which
+    // lets it launch at once; it waits for the main grid before reading.
+    const int64_t threads = t_blocks * o_blocks * N_TOK * kTcBlockO;
+    cudaLaunchConfig_t rc = {};
+    rc.gridDim = dim3((unsigned)((threads + 255) / 256), 1, 1);
+    rc.blockDim = dim3(256, 1, 1);
+    rc.stream = stream;
+    rc.attrs = &attr;
+    rc.numAttrs = 1;
+    e = cudaLaunchKernelEx(&rc, qlin_splitk_reduce_kernel<T>, (const float4*)partials, split,
+                           (int)t_blocks, (int)o_blocks, N_TOK, static_cast<const T*>(prm.bias),
+                           static_cast<T*>(prm.y), prm.ld_y, prm.M, prm.N_g, prm.static_weights);
+    if (e != cudaSuccess) return QLIN_ERR_LAUNCH;
+  }
+  return QLIN_OK;
 }
 
 template <typename T>
 int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
            const T* bias, const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y,
-           int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, uint8_t* ws, cudaStream_t stream) {
+           int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, uint8_t* ws, int flags,
+           cudaStream_t stream) {
   if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const WsLayout L = ws_layout(QLIN_BF16, M, K_g, rank);
+  const WsLayout L = ws_layout(QLIN_BF16, M, K_g, N_g, rank);
   T* xp = reinterpret_cast<T*>(ws + L.xp_off);
   T* t = rank > 0 ? reinterpret_cast<T*>(ws + L.t_off) : nullptr;
   const int n_tok = n_tok_for(M);
+  const bool stack = M <= kStackMaxTokens;
 
-  // 1. component planes of x
+  // 1. prologue: component planes of x (plane mode) and the scaled LoRA down
+  //    projection; none for stacked mode without LoRA
   {
-    const int64_t threads = M * (K_g / 8);
-    const int64_t blocks = (threads + 255) / 256;
-    qlin_planarize_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(x, ld_x, xp, M, K_g);
+    const int64_t planar_blocks = stack ? 0 : (M * (K_g / 8) + 255) / 256;
+    const int rr = stack ? 1 : 8;
+    const int64_t lora_blocks = rank > 0 ? ((M + 7) / 8) * ((rank + rr - 1) / rr) : 0;
+    const int64_t blocks = planar_blocks + lora_blocks;
+    if (blocks > INT32_MAX) return QLIN_ERR_SHAPE;
+    if (blocks > 0) {
+      cudaLaunchConfig_t pc = {};
+      pc.gridDim = dim3((unsigned)blocks, 1, 1);
+      pc.blockDim = dim3(256, 1, 1);
+      pc.stream = stream;
+      cudaLaunchAttribute pattr;
+      pattr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      pattr.val.programmaticStreamSerializationAllowed = 1;
+      pc.attrs = &pattr;
+      pc.numAttrs = 1;
+      cudaError_t e = stack ? cudaLaunchKernelEx(&pc, qlin_prologue_kernel<T, 1>, x, ld_x, xp, M, K_g,
+                                                 planar_blocks, lora_a, rank, lora_scale, t, L.ld_t)
+                            : cudaLaunchKernelEx(&pc, qlin_prologue_kernel<T, 8>, x, ld_x, xp, M, K_g,
+                                                 planar_blocks, lora_a, rank, lora_scale, t, L.ld_t);
+      if (e != cudaSuccess) return QLIN_ERR_LAUNCH;
+    }
   }
-  // 2. LoRA down projection, scaled and rounded like the operands
-  if (rank > 0) {
-    dim3 grid((unsigned)((M + 15) / 16), (unsigned)((rank + 7) / 8));
-    qlin_lora_down_kernel<T, 16><<<grid, 256, 0, stream>>>(x, ld_x, lora_a, rank, M, 4 * K_g,
-                                                            lora_scale, nullptr, t, L.ld_t);
-  }
-  // 3. tensor maps
+  // 2. tensor maps
   CUtensorMap maps[7];
   std::memset(maps, 0, sizeof(maps));
   for (int p = 0; p < 4; ++p) {
@@ -238,7 +305,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
     if (encode(&maps[p], dt, 2, const_cast<void*>(w[p]), dims, strides, box) != CUDA_SUCCESS)
       return QLIN_ERR_ALIGN;
   }
-  {
+  if (!stack) {
     cuuint64_t dims[3] = {(cuuint64_t)K_g, (cuuint64_t)M, 4};
     cuuint64_t strides[2] = {(cuuint64_t)(K_g * 2), (cuuint64_t)(M * K_g * 2)};
     cuuint32_t box[3] = {kTcChunk, (cuuint32_t)n_tok, 1};
@@ -257,20 +324,27 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
     if (encode(&maps[6], dt, 2, t, tdims, tstrides, tbox) != CUDA_SUCCESS) return QLIN_ERR_ALIGN;
     lora_chunks = (int)((rank + kTcChunk - 1) / kTcChunk);
   }
+  // 3. main kernel (+ split-K reduction)
   TcParams prm;
+  prm.x = x;
+  prm.ld_x = ld_x;
   prm.bias = bias;
   prm.y = y;
   prm.ld_y = ld_y;
   prm.M = (int)M;
   prm.N_g = (int)N_g;
+  prm.K_g = (int)K_g;
   prm.num_chunks = (int)((K_g + kTcChunk - 1) / kTcChunk);
   prm.lora_chunks = lora_chunks;
   prm.split_k = 1;
+  prm.partials = nullptr;
+  prm.static_weights = (flags & QLIN_FLAG_STATIC_WEIGHTS) ? 1 : 0;
+  float4* partials = L.part_bytes ? reinterpret_cast<float4*>(ws + L.part_off) : nullptr;
   switch (n_tok) {
-    case 16: return launch_tc_impl<T, 16>(dev, 0, maps, prm, M, N_g, stream);
-    case 32: return launch_tc_impl<T, 32>(dev, 0, maps, prm, M, N_g, stream);
-    case 64: return launch_tc_impl<T, 64>(dev, 0, maps, prm, M, N_g, stream);
-    default: return launch_tc_impl<T, 128>(dev, 0, maps, prm, M, N_g, stream);
+    case 16: return launch_tc_impl<T, 16>(dev, maps, prm, M, K_g, N_g, partials, stream);
+    case 32: return launch_tc_impl<T, 32>(dev, maps, prm, M, K_g, N_g, partials, stream);
+    case 64: return launch_tc_impl<T, 64>(dev, maps, prm, M, K_g, N_g, partials, stream);
+    default: return launch_tc_impl<T, 128>(dev, maps, prm, M, K_g, N_g, partials, stream);
   }
 }
 
@@ -278,7 +352,7 @@ template <typename T>
 int run_simt(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
              const T* bias, const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y,
              int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, uint8_t* ws, cudaStream_t stream) {
-  const WsLayout L = ws_layout(QLIN_F32, M, K_g, rank);
+  const WsLayout L = ws_layout(QLIN_F32, M, K_g, N_g, rank);
   float* tf = nullptr;
   if (rank > 0) {
     tf = reinterpret_cast<float*>(ws + L.tf_off);
@@ -309,7 +383,7 @@ template <typename T>
 int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void* const w[4],
              int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b, int rank,
              float lora_scale, void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
-             uint8_t* ws, cudaStream_t stream) {
+             uint8_t* ws, int flags, cudaStream_t stream) {
   const T* xt = static_cast<const T*>(x);
   const T* bt = static_cast<const T*>(bias);
   const T* la = static_cast<const T*>(lora_a);
@@ -321,10 +395,21 @@ int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void*
   } else {
     if (algo == QLIN_ALGO_TC)
       return run_tc<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
-                       stream);
+                       flags, stream);
     return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
                        stream);
   }
+}
+
+template <typename T, int N_TOK>
+int plan_tc(DeviceInfo* dev, int64_t M, int64_t K_g, int64_t N_g, int* split, int* resident) {
+  int st = ensure_tc_attrs<T, N_TOK>(dev);
+  if (st != QLIN_OK) return st;
+  const int ti = n_tok_index(N_TOK);
+  const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
+  *split = max_split_for(M, K_g, N_g, dev->num_sms);
+  *resident = dev->resident[di][ti];
+  return QLIN_OK;
 }
 
 }  // namespace
@@ -352,7 +437,7 @@ int qlin_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank
   if (!bytes) return QLIN_ERR_ARG;
   if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
   if (M < 0 || K_g <= 0 || N_g <= 0 || rank < 0) return QLIN_ERR_SHAPE;
-  *bytes = ws_layout(dtype, M, K_g, rank).total;
+  *bytes = ws_layout(dtype, M, K_g, N_g, rank).total;
   return QLIN_OK;
 }
 
@@ -361,14 +446,51 @@ int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
   return select_algo(dtype);
 }
 
+int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int* algo, int* tile_tokens,
+              int* split_k, int* launches, int* resident_ctas) {
+  if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
+  if (M <= 0 || K_g <= 0 || N_g <= 0 || rank < 0) return QLIN_ERR_SHAPE;
+  DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st != QLIN_OK) return st;
+  const int a = (dtype == QLIN_F32 || K_g % 8 != 0 || (rank > 0 && rank % 8 != 0)) ? QLIN_ALGO_SIMT
+                                                                                     : QLIN_ALGO_TC;
+  int nt = 0, sp = 1, res = 0, nl = 0;
+  if (a == QLIN_ALGO_TC) {
+    nt = n_tok_for(M);
+    const bool bf = dtype == QLIN_BF16;
+    switch (nt) {
+      case 16: st = bf ? plan_tc<__nv_bfloat16, 16>(dev, M, K_g, N_g, &sp, &res)
+                       : plan_tc<__half, 16>(dev, M, K_g, N_g, &sp, &res); break;
+      case 32: st = bf ? plan_tc<__nv_bfloat16, 32>(dev, M, K_g, N_g, &sp, &res)
+                       : plan_tc<__half, 32>(dev, M, K_g, N_g, &sp, &res); break;
+      case 64: st = bf ? plan_tc<__nv_bfloat16, 64>(dev, M, K_g, N_g, &sp, &res)
+                       : plan_tc<__half, 64>(dev, M, K_g, N_g, &sp, &res); break;
+      default: st = bf ? plan_tc<__nv_bfloat16, 128>(dev, M, K_g, N_g, &sp, &res)
+                       : plan_tc<__half, 128>(dev, M, K_g, N_g, &sp, &res); break;
+    }
+    if (st != QLIN_OK) return st;
+    nl = 1 + ((M > kStackMaxTokens || rank > 0) ? 1 : 0) + (sp > 1 ? 1 : 0);
+  } else {
+    nl = rank > 0 ? 2 : 1;
+  }
+  if (algo) *algo = a;
+  if (tile_tokens) *tile_tokens = nt;
+  if (split_k) *split_k = sp;
+  if (launches) *launches = nl;
+  if (resident_ctas) *resident_ctas = res;
+  return QLIN_OK;
+}
+
 int qlin_forward_ex(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi, const void* wj,
                     const void* wk, int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b,
                     int rank, float lora_scale, void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
-                    void* workspace, size_t workspace_bytes, int algo, void* stream) {
+                    void* workspace, size_t workspace_bytes, int algo, int flags, void* stream) {
   int st = validate(dtype, x, ld_x, wr, wi, wj, wk, ld_w, lora_a, lora_b, rank, y, ld_y, M, K_g, N_g);
   if (st != QLIN_OK) return st;
   if (M == 0) return QLIN_OK;
   if (algo < QLIN_ALGO_AUTO || algo > QLIN_ALGO_TC) return QLIN_ERR_ARG;
+  if (flags & ~QLIN_FLAG_STATIC_WEIGHTS) return QLIN_ERR_ARG;
   if (rank == 0) lora_a = lora_b = nullptr;
   DeviceInfo* dev = nullptr;
   st = device_info(&dev);
@@ -376,12 +498,14 @@ int qlin_forward_ex(int dtype, const void* x, int64_t ld_x, const void* wr, cons
   const void* w[4] = {wr, wi, wj, wk};
   if (algo == QLIN_ALGO_AUTO) {
     algo = select_algo(dtype);
-    if (algo == QLIN_ALGO_TC && !tc_eligible(dtype, x, ld_x, w, ld_w, lora_b, rank, y, ld_y, K_g))
+    if (algo == QLIN_ALGO_TC &&
+        !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g))
       algo = QLIN_ALGO_SIMT;
-  } else if (algo == QLIN_ALGO_TC && !tc_eligible(dtype, x, ld_x, w, ld_w, lora_b, rank, y, ld_y, K_g)) {
+  } else if (algo == QLIN_ALGO_TC &&
+             !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g)) {
     return QLIN_ERR_ALIGN;
   }
-  const WsLayout L = ws_layout(dtype, M, K_g, rank);
+  const WsLayout L = ws_layout(dtype, M, K_g, N_g, rank);
   if (L.total > 0 && (!workspace || workspace_bytes < L.total || !aligned(workspace, 256)))
     return QLIN_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -390,15 +514,15 @@ int qlin_forward_ex(int dtype, const void* x, int64_t ld_x, const void* wr, cons
   switch (dtype) {
     case QLIN_F32:
       st = dispatch<float>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
-                           K_g, N_g, ws, s);
+                           K_g, N_g, ws, flags, s);
       break;
     case QLIN_BF16:
       st = dispatch<__nv_bfloat16>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
-                                   ld_y, M, K_g, N_g, ws, s);
+                                   ld_y, M, K_g, N_g, ws, flags, s);
       break;
     default:
       st = dispatch<__half>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
-                            K_g, N_g, ws, s);
+                            K_g, N_g, ws, flags, s);
       break;
   }
   if (st != QLIN_OK) return st;
@@ -410,7 +534,7 @@ int qlin_forward(int dtype, const void* x, int64_t ld_x, const void* wr, const v
                  int rank, float lora_scale, void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
                  void* workspace, size_t workspace_bytes, void* stream) {
   return qlin_forward_ex(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
-                         ld_y, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_AUTO, stream);
+                         ld_y, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_AUTO, 0, stream);
 }
 
 int qlin_get_device_error(void* stream, int clear, int* device_status) {

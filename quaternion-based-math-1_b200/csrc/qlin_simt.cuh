@@ -5,6 +5,8 @@
 //  * qlin_lora_down_kernel -- t = x A^T for the fused LoRA residual.
 //  * qlin_planarize_kernel -- x[m, 4i+q] -> xp[q][m][i] (component planes), the
 //                             operand layout of the tensor-core kernel.
+//  * qlin_prologue_kernel  -- the tensor-core path's prologue: component planes
+//                             and the scaled LoRA down projection in one launch.
 //  * qlin_gather_kernel    -- [G, M, n] shards -> [M, G*n] columns.
 #pragma once
 
@@ -185,6 +187,107 @@ qlin_planarize_kernel(const T* __restrict__ x, int64_t ld_x, T* __restrict__ xp,
   for (int q = 0; q < 4; ++q) {
     uint4* dst = reinterpret_cast<uint4*>(xp + q * plane + m * K_g + 8 * g);
     *dst = make_uint4(out[q][0], out[q][1], out[q][2], out[q][3]);
+  }
+}
+
+// Prologue of the tensor-core path, one launch:
+//  * blocks [0, planar_blocks): component planes of x (as qlin_planarize_kernel);
+//  * the remaining blocks: scaled LoRA down projection
+//      t[m, r] = lora_scale * sum_k x[m, k] A[r, k]
+//    one block per (8 tokens, RR ranks), threads striding over K in 8-element
+//    (16-byte) vectors, fp32 accumulation, rounded to T once.  RR = 1 spreads
+//    a few tokens over many blocks; RR = 8 reuses each x row for 8 ranks.
+// Launched as a programmatic dependent of the previous kernel of the stream:
+// it lets the next kernel launch, then waits for the previous one before
+// touching memory.  Requires K % 8 == 0 and 16-byte aligned x, lora_a and
+// rows (ld_x % 8 == 0).
+template <typename T, int RR>
+__global__ void __launch_bounds__(256)
+qlin_prologue_kernel(const T* __restrict__ x, int64_t ld_x, T* __restrict__ xp, int64_t M, int64_t K_g,
+                     int64_t planar_blocks, const T* __restrict__ lora_a, int rank, float lora_scale,
+                     T* __restrict__ t_tc, int64_t ld_t) {
+  static_assert(sizeof(T) == 2, "16-bit elements");
+  pdl_launch_dependents();
+  pdl_wait_prior();
+  if ((int64_t)blockIdx.x < planar_blocks) {
+    const int64_t groups = K_g / 8;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= M * groups) return;
+    const int64_t m = idx / groups, g = idx % groups;
+    const uint4* src = reinterpret_cast<const uint4*>(x + m * ld_x + 32 * g);
+    uint32_t w[16];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 v = __ldg(src + c);
+      w[4 * c + 0] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+    }
+    const int64_t plane = M * K_g;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t a = w[4 * j + (q >> 1)], b = w[4 * j + 2 + (q >> 1)];
+        o[j] = __byte_perm(a, b, (q & 1) ? 0x7632 : 0x5410);
+      }
+      *reinterpret_cast<uint4*>(xp + q * plane + m * K_g + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    return;
+  }
+  constexpr int TT = 8;
+  const int64_t b = (int64_t)blockIdx.x - planar_blocks;
+  const int rblocks = (rank + RR - 1) / RR;
+  const int64_t m0 = (b / rblocks) * TT;
+  const int r0 = (int)(b % rblocks) * RR;
+  const int64_t K = 4 * K_g, nvec = K / 8;
+  float acc[TT][RR];
+#pragma unroll
+  for (int t = 0; t < TT; ++t)
+#pragma unroll
+    for (int r = 0; r < RR; ++r) acc[t][r] = 0.f;
+  for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
+    float a[RR][8];
+#pragma unroll
+    for (int r = 0; r < RR; ++r) {
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (r0 + r < rank) u = __ldg(reinterpret_cast<const uint4*>(lora_a + (int64_t)(r0 + r) * K) + v);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[r][j] = to_f32(e[j]);
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      if (m0 + t >= M) break;
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(x + (m0 + t) * ld_x) + v);
+      const T* e = reinterpret_cast<const T*>(&u);
+      float xv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xv[j] = to_f32(e[j]);
+#pragma unroll
+      for (int r = 0; r < RR; ++r)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[t][r] += a[r][j] * xv[j];
+    }
+  }
+  __shared__ float red[8][TT * RR];
+  static_assert(TT * RR <= 256, "one thread per reduced value");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int t = 0; t < TT; ++t)
+#pragma unroll
+    for (int r = 0; r < RR; ++r) {
+      float s = acc[t][r];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      if (lane == 0) red[warp][t * RR + r] = s;
+    }
+  __syncthreads();
+  if (threadIdx.x < TT * RR) {
+    const int t = threadIdx.x / RR, r = threadIdx.x % RR;
+    float s = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < 8; ++w2) s += red[w2][threadIdx.x];
+    if (m0 + t < M && r0 + r < rank) t_tc[(m0 + t) * ld_t + r0 + r] = from_f32<T>(lora_scale * s);
   }
 }
 

@@ -1,29 +1,54 @@
 // Tensor-core quaternion linear forward for sm_100a (TMA + tcgen05 + TMEM).
 //
-// Decomposition.  With component planes X_q[m, i] = x[m, 4i+q] (written by
-// qlin_planarize_kernel) the Hamilton-product layer is sixteen real products
+// Decomposition.  With component planes X_q[m, i] = x[m, 4i+q] the
+// Hamilton-product layer is sixteen real products
 //
 //     Y_a[m, o] = sum_p s(a,p) * sum_i W_p[o, i] * X_{p^a}[m, i]
 //
 // (a = output component, p = weight component, q = p XOR a is the input
 // component it pairs with, s(a,p) = +-1 is the sign of the 4x4 block matrix
-// of reference quaternion/packing.py:18-21).  Each (a, p) term is one UMMA
-// whose A operand is a W_p tile exactly as TMA loads it from the caller's
-// weight tensor and whose B operand is an X_q tile; the sign is the
-// instruction descriptor's negate-A bit.  The four output components
-// accumulate in four fp32 TMEM accumulators.  Nothing is expanded: every
-// weight byte crosses HBM once per tile, a quarter of a dense layer's.
+// of reference quaternion/packing.py:18-21).  The A operand of every UMMA is
+// a W_p tile exactly as TMA loads it from the caller's weight tensor, so each
+// weight byte crosses HBM once per tile -- a quarter of a dense layer's
+// traffic -- and the 4x real matrix is never formed anywhere.  The sign and
+// component swap are applied on the activation side, in one of two ways:
 //
-// CTA tile: 128 output quaternions (UMMA M = 128, one TMEM lane each) x
-// N_TOK tokens (UMMA N) x all four components.  K is walked in chunks of 32
-// input quaternions (64-byte rows, 64-byte TMA/UMMA swizzle).  For few tiles
-// (decode) the K chunks of one tile are split over the CTAs of a cluster and
-// the fp32 partials are summed through distributed shared memory.
+//  * planes (M > 64): the prologue writes X_q planes to the workspace, TMA
+//    loads them, and each (a, p) term is one UMMA (N = tokens) whose sign is
+//    the instruction descriptor's negate-A bit -- 16 UMMAs per K step into
+//    four TMEM accumulators;
+//  * stacked (M <= 64): two builder warps read x directly and write, per
+//    weight component p, the operand Xhat_p whose rows are (a, token) and
+//    hold s(a,p) * X_{p^a}; one UMMA per p (N = 4 * tokens) then produces all
+//    four output components at once -- 4 UMMAs per K step, each reading its
+//    weight tile from shared memory once.
+//
+// In both modes accumulator column a * N_TOK + token holds Y_a, so the
+// epilogue is shared.  CTA tile: 128 output quaternions (UMMA M = 128, one
+// TMEM lane each) x N_TOK tokens.  K is walked in chunks of 32 input
+// quaternions (64-byte rows, 64-byte TMA/UMMA swizzle).  With few tiles
+// (decode) the chunks of one tile are split over several CTAs so that every
+// SM streams weights; their fp32 partials of the real tokens go to the
+// workspace and a small dependent kernel sums them.  LoRA: the scaled down
+// projection t (prologue kernel) is the B operand of four extra UMMAs per 32
+// ranks whose A operands are the [o, a]-strided rows of LoRA B, accumulated
+// before the single rounding.
+//
+// Stream order: every kernel of this path is launched as a programmatic
+// dependent of the previous kernel of the stream.  Its set-up (barriers,
+// TMEM, descriptor prefetch) overlaps that kernel's tail, and it waits
+// (griddepcontrol.wait) before it reads or writes memory -- except that with
+// static weights (the caller's promise that earlier work does not write the
+// weights) the first weight tiles are requested before the wait.
 //
 // Roles (128 threads): thread 0 issues TMA, warp 1 owns TMEM and its lane 0
-// issues UMMA, all four warps run the epilogue (warp w reads TMEM lanes
-// 32w..32w+31).  Every mbarrier wait is bounded (qlin_common.cuh).
+// issues UMMA, warps 2-3 build Xhat (stacked mode), all four warps run the
+// epilogue (warp w reads TMEM lanes 32w..32w+31).  Every mbarrier wait is
+// bounded (qlin_common.cuh); on a timeout the kernel records
+// QLIN_ERR_TIMEOUT, skips the remaining work and still meets every barrier.
 #pragma once
+
+#include <type_traits>
 
 #include "qlin_common.cuh"
 
@@ -33,18 +58,23 @@ constexpr int kTcBlockO = 128;   // output quaternions per CTA tile (UMMA M)
 constexpr int kTcChunk = 32;     // input quaternions per K chunk (64-byte rows)
 constexpr int kTcThreads = 128;
 constexpr int kTcWTileBytes = kTcBlockO * kTcChunk * 2;  // 8 KB
+constexpr int kTcMaxSplit = 16;  // largest K split of one output tile
+constexpr int kTcBuilderBar = 1; // named barrier of the two builder warps
 
-template <int N_TOK>
+template <int N_TOK, bool STACK>
 struct TcCfg {
-  static constexpr int kXTileBytes = N_TOK * kTcChunk * 2;
+  // Activation operand per weight component and stage: stacked [4*N_TOK rows]
+  // or one plane [N_TOK rows], 64 bytes per row either way.
+  static constexpr int kXTileBytes = (STACK ? 4 : 1) * N_TOK * kTcChunk * 2;
   static constexpr int kStageBytes = 4 * kTcWTileBytes + 4 * kXTileBytes;
-  static constexpr int kStages = N_TOK >= 128 ? 3 : (N_TOK >= 64 ? 4 : (N_TOK >= 32 ? 5 : 6));
+  static constexpr int kFit = (200 * 1024) / kStageBytes;
+  static constexpr int kStages = kFit > 6 ? 6 : (kFit < 2 ? 2 : kFit);
   static constexpr int kTmemCols = 4 * N_TOK;  // 64 .. 512, power of two
   static constexpr int kBarOffset = kStages * kStageBytes;
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
   static_assert(N_TOK == 16 || N_TOK == 32 || N_TOK == 64 || N_TOK == 128, "UMMA N");
-  // Split-K partials (4 * N_TOK * 128 fp32) reuse the stage buffers.
-  static constexpr bool kAllowSplit = 4 * N_TOK * 128 * 4 <= kStages * kStageBytes;
+  static_assert(!STACK || N_TOK <= 64, "stacked operand has 4*N_TOK <= 256 rows");
+  static_assert(kSmemBytes <= 232448, "fits the 227 KB opt-in shared memory");
 };
 
 // neg(a, p): sign of W_p in output component a (rows of packing.py:18-21).
@@ -53,26 +83,43 @@ __host__ __device__ constexpr bool quat_neg(int a, int p) {
 }
 
 struct TcParams {
-  const void* bias;   // [4*N_g] or null
-  void* y;            // [M, ld_y]
+  const void* x;       // [M, ld_x] (stacked mode reads it directly)
+  int64_t ld_x;
+  const void* bias;    // [4*N_g] or null
+  void* y;             // [M, ld_y]
   int64_t ld_y;
-  int M, N_g;
-  int num_chunks;     // ceil(K_g / 32)
-  int lora_chunks;    // ceil(rank / 32), 0 without LoRA
-  int split_k;        // CTAs per cluster along K (1 = no split)
+  int M, N_g, K_g;
+  int num_chunks;      // ceil(K_g / 32)
+  int lora_chunks;     // ceil(rank / 32), 0 without LoRA
+  int split_k;         // CTAs sharing one output tile along K (1 = no split)
+  float4* partials;    // split_k > 1: [split][t_blocks][o_blocks][N_TOK][128] fp32 x4
+  int static_weights;  // weights/bias/LoRA B are not written by earlier work on the stream
 };
 
-template <typename T, int N_TOK>
+__device__ __forceinline__ void builder_bar_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kTcBuilderBar), "n"(64) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+template <typename T, int N_TOK, bool STACK>
 __global__ void __launch_bounds__(kTcThreads, 1)
 qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant__ CUtensorMap map_wi,
                const __grid_constant__ CUtensorMap map_wj, const __grid_constant__ CUtensorMap map_wk,
                const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_lb,
                const __grid_constant__ CUtensorMap map_t, const TcParams prm) {
-  using Cfg = TcCfg<N_TOK>;
+  using Cfg = TcCfg<N_TOK, STACK>;
   constexpr int S = Cfg::kStages;
   constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   constexpr uint32_t kIdescPos = make_idesc_f16(128, N_TOK, kFmt, false);
   constexpr uint32_t kIdescNeg = make_idesc_f16(128, N_TOK, kFmt, true);
+  constexpr uint32_t kIdescStack = make_idesc_f16(128, STACK ? 4 * N_TOK : N_TOK, kFmt, false);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -88,21 +135,57 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int o0 = blockIdx.y * kTcBlockO;
   const int t0 = blockIdx.z * N_TOK;
-  const int ks = blockIdx.x;  // K split index == rank in the cluster
+  const int ks = blockIdx.x;  // K split index
   const int c_begin = (int)((int64_t)ks * prm.num_chunks / prm.split_k);
   const int c_end = (int)((int64_t)(ks + 1) * prm.num_chunks / prm.split_k);
   const int my_main = c_end - c_begin;
   const int my_lora = (ks == prm.split_k - 1) ? prm.lora_chunks : 0;
   const int total = my_main + my_lora;
+  const int m_tile = (prm.M - t0) < N_TOK ? (prm.M - t0) : N_TOK;  // real tokens in the tile
+
+  // The next kernel of the stream may launch now: every kernel of this path
+  // waits (griddepcontrol.wait) for its predecessor to complete before it
+  // reads or writes memory the predecessor may use.
+  pdl_launch_dependents();
 
   auto w_tile = [&](int s, int p) { return smem + s * Cfg::kStageBytes + p * kTcWTileBytes; };
   auto x_tile = [&](int s, int q) {
     return smem + s * Cfg::kStageBytes + 4 * kTcWTileBytes + q * Cfg::kXTileBytes;
   };
+  const CUtensorMap* wmap[4] = {&map_wr, &map_wi, &map_wj, &map_wk};
+  const int pre = total < S ? total : S;
+  // Weight (and LoRA B) tiles of the first stages.
+  auto issue_pre_weights = [&]() {
+    for (int it = 0; it < pre; ++it) {
+      if (it < my_main) {
+        const int k = (c_begin + it) * kTcChunk;
+        mbar_arrive_expect_tx(&full[it], 4 * kTcWTileBytes + (STACK ? 0 : 4 * Cfg::kXTileBytes));
+#pragma unroll
+        for (int p = 0; p < 4; ++p) tma_load_2d(w_tile(it, p), wmap[p], &full[it], k, o0);
+      } else {
+        const int r = (it - my_main) * kTcChunk;
+        mbar_arrive_expect_tx(&full[it], 4 * kTcWTileBytes + N_TOK * kTcChunk * 2);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) tma_load_3d(w_tile(it, a), &map_lb, &full[it], r, a, o0);
+      }
+    }
+  };
+  // Bias of this thread's output row as raw bits; converted in the epilogue,
+  // so the load latency hides under the main loop.  With a K split the bias
+  // is added by the reduction kernel instead.
+  auto load_bias = [&](T (&raw)[4]) {
+    const int ob = o0 + (int)threadIdx.x;
+    const T* __restrict__ bp = reinterpret_cast<const T*>(prm.bias);
+    const bool has = bp && prm.split_k == 1 && ob < prm.N_g;
+#pragma unroll
+    for (int a = 0; a < 4; ++a) raw[a] = has ? bp[4 * ob + a] : from_f32<T>(0.f);
+  };
 
+  // Set-up that touches no global memory, so it overlaps the tail of the
+  // previous kernel of the stream.
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], STACK ? 2 : 1);  // producer (+ builders)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -114,38 +197,61 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     tma_prefetch_desc(&map_wi);
     tma_prefetch_desc(&map_wj);
     tma_prefetch_desc(&map_wk);
-    tma_prefetch_desc(&map_x);
+    if (!STACK) tma_prefetch_desc(&map_x);
+    // With static weights the caller guarantees that no earlier work on the
+    // stream writes the weights, bias or LoRA B, so their first tiles are
+    // requested before waiting for that work.
+    if (prm.static_weights) issue_pre_weights();
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
+  T bias_raw[4];
+  if (prm.static_weights) load_bias(bias_raw);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything below may read what earlier kernels of the stream wrote (x,
+  // the prologue's outputs, the workspace) or write what they read (y).
+  pdl_wait_prior();
+  if (!prm.static_weights) load_bias(bias_raw);
 
   if (threadIdx.x == 0) {
     // ---------------- TMA producer ----------------
-    const CUtensorMap* wmap[4] = {&map_wr, &map_wi, &map_wj, &map_wk};
-    int it = 0;
+    if (!prm.static_weights) issue_pre_weights();
+    for (int it = 0; it < pre; ++it) {
+      if (it < my_main) {
+        if (!STACK) {
+          const int k = (c_begin + it) * kTcChunk;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tma_load_3d(x_tile(it, q), &map_x, &full[it], k, t0, q);
+        }
+      } else {
+        tma_load_2d(x_tile(it, 0), &map_t, &full[it], (it - my_main) * kTcChunk, t0);
+      }
+    }
+    int it = pre;
     for (; it < total; ++it) {
       const int s = it % S, n = it / S;
-      if (it >= S && !mbar_wait(&empty[s], (n - 1) & 1)) {
+      if (!mbar_wait(&empty[s], (n - 1) & 1)) {
         *abort_flag = 1;
         break;
       }
       if (*abort_flag) break;
       if (it < my_main) {
         const int k = (c_begin + it) * kTcChunk;
-        mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + 4 * Cfg::kXTileBytes);
+        mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + (STACK ? 0 : 4 * Cfg::kXTileBytes));
 #pragma unroll
         for (int p = 0; p < 4; ++p) tma_load_2d(w_tile(s, p), wmap[p], &full[s], k, o0);
+        if (!STACK) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) tma_load_3d(x_tile(s, q), &map_x, &full[s], k, t0, q);
+          for (int q = 0; q < 4; ++q) tma_load_3d(x_tile(s, q), &map_x, &full[s], k, t0, q);
+        }
       } else {
         const int r = (it - my_main) * kTcChunk;
-        mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + Cfg::kXTileBytes);
+        mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + N_TOK * kTcChunk * 2);
 #pragma unroll
         for (int a = 0; a < 4; ++a) tma_load_3d(w_tile(s, a), &map_lb, &full[s], r, a, o0);
         tma_load_2d(x_tile(s, 0), &map_t, &full[s], r, t0);
@@ -168,11 +274,14 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
             const uint64_t adesc = smem_desc_sw64(w_tile(s, p)) + 2 * kk;
+            const uint32_t accum = (it > 0 || kk > 0 || p > 0) ? 1u : 0u;
+            if (STACK) {
+              umma_f16(tmem_base, adesc, smem_desc_sw64(x_tile(s, p)) + 2 * kk, kIdescStack, accum);
+            } else {
 #pragma unroll
-            for (int a = 0; a < 4; ++a) {
-              const uint64_t bdesc = smem_desc_sw64(x_tile(s, p ^ a)) + 2 * kk;
-              umma_f16(tmem_base + a * N_TOK, adesc, bdesc, quat_neg(a, p) ? kIdescNeg : kIdescPos,
-                       (it > 0 || kk > 0 || p > 0) ? 1u : 0u);
+              for (int a = 0; a < 4; ++a)
+                umma_f16(tmem_base + a * N_TOK, adesc, smem_desc_sw64(x_tile(s, p ^ a)) + 2 * kk,
+                         quat_neg(a, p) ? kIdescNeg : kIdescPos, accum);
             }
           }
         }
@@ -189,6 +298,60 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     }
     *consumed_count = it;
     umma_commit(acc_full);  // fires once every UMMA issued above has completed
+  } else if (STACK && warp >= 2) {
+    // ---------------- Xhat builders (warps 2-3) ----------------
+    // Xhat_p row (a*N_TOK + token), 16-byte chunk c (input groups 8c..8c+7
+    // of the chunk) = s(a,p) * X_{p^a}: one work item moves 8 quaternions of
+    // one token (64 bytes of x) into 16 swizzled 16-byte slots (64-byte
+    // swizzle: chunk c of row r sits at chunk c ^ ((r >> 1) & 3)).  Every
+    // builder runs every iteration (and meets every named barrier) even after
+    // an abort, so no builder can be left waiting.
+    const int bt = threadIdx.x - 64;
+    const T* __restrict__ x = reinterpret_cast<const T*>(prm.x);
+    for (int it = 0; it < total; ++it) {
+      const int s = it % S, n = it / S;
+      if (it >= S && !*abort_flag && !mbar_wait(&empty[s], (n - 1) & 1)) *abort_flag = 1;
+      if (it < my_main && !*abort_flag) {
+        const int g0 = (c_begin + it) * kTcChunk;
+        for (int item = bt; item < N_TOK * 4; item += 64) {
+          const int tok = item >> 2, gb = item & 3;
+          const int m = t0 + tok, gbase = g0 + 8 * gb;
+          uint32_t w[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) w[j] = 0u;
+          if (m < prm.M && gbase < prm.K_g) {
+            const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)m * prm.ld_x + 4 * gbase);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint4 v = __ldg(src + c);
+              w[4 * c + 0] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+            }
+          }
+          // plane q of the 8 quaternions: word j = (X_q[2j], X_q[2j+1])
+          uint32_t pl[4][4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              pl[q][j] = __byte_perm(w[4 * j + (q >> 1)], w[4 * j + 2 + (q >> 1)], (q & 1) ? 0x7632 : 0x5410);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const uint32_t base = smem_u32(x_tile(s, p));
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int a = p ^ q;
+              const uint32_t sg = quat_neg(a, p) ? 0x80008000u : 0u;
+              const int row = a * N_TOK + tok;
+              const uint32_t addr = base + row * 64 + ((gb ^ ((row >> 1) & 3)) << 4);
+              st_shared_v4(addr, pl[q][0] ^ sg, pl[q][1] ^ sg, pl[q][2] ^ sg, pl[q][3] ^ sg);
+            }
+          }
+        }
+        fence_async_smem();
+      }
+      builder_bar_sync();
+      if (bt == 0) mbar_arrive(&full[s]);
+    }
   }
   __syncwarp();
 
@@ -199,17 +362,15 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   const int o_local = warp * 32 + lane;
   const uint32_t lane_addr = tmem_base + ((uint32_t)(warp * 32) << 16);
   T* __restrict__ y = reinterpret_cast<T*>(prm.y);
-  const T* __restrict__ bias = reinterpret_cast<const T*>(prm.bias);
+  const int jn = (m_tile + 15) / 16;  // 16-token column groups holding real tokens
 
   if (prm.split_k == 1) {
     const int o = o0 + o_local;
-    float b[4] = {0.f, 0.f, 0.f, 0.f};
-    if (ok && bias && o < prm.N_g) {
+    float b[4];
 #pragma unroll
-      for (int a = 0; a < 4; ++a) b[a] = to_f32(bias[4 * o + a]);
-    }
+    for (int a = 0; a < 4; ++a) b[a] = to_f32(bias_raw[a]);
 #pragma unroll 1
-    for (int j = 0; j < N_TOK / 16; ++j) {
+    for (int j = 0; j < jn; ++j) {
       float v[4][16];
 #pragma unroll
       for (int a = 0; a < 4; ++a) tmem_ld16(lane_addr + a * N_TOK + j * 16, v[a]);
@@ -226,47 +387,25 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
       }
     }
   } else {
-    // Partials -> own shared memory as red[(a*N_TOK + tok) * 128 + o_local].
-    float* red = reinterpret_cast<float*>(smem);
-    const bool smem_free = ok;  // all loads were consumed by completed UMMAs
+    // K split: fp32 partials of the real tokens go to this CTA's slot of the
+    // workspace as [token][row] float4 (a = 0..3), summed with the bias and
+    // rounded by qlin_splitk_reduce_kernel.
+    float4* part = prm.partials +
+                   ((size_t)(ks * gridDim.z + blockIdx.z) * gridDim.y + blockIdx.y) * (N_TOK * kTcBlockO);
 #pragma unroll 1
-    for (int j = 0; j < N_TOK / 16; ++j) {
+    for (int j = 0; j < jn; ++j) {
       float v[4][16];
 #pragma unroll
       for (int a = 0; a < 4; ++a) tmem_ld16(lane_addr + a * N_TOK + j * 16, v[a]);
       tmem_ld_wait();
-      if (smem_free) {
+      if (ok) {
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-          for (int t = 0; t < 16; ++t) red[(a * N_TOK + j * 16 + t) * 128 + o_local] = v[a][t];
-      }
-    }
-    cluster_sync_all();
-    // CTA `ks` finalises output rows [ks*rows, (ks+1)*rows) of the tile.
-    const int rows = kTcBlockO / prm.split_k;
-    const uint32_t red_addr = smem_u32(red);
-    int all_ok = ok ? 1 : 0;
-    for (int idx = threadIdx.x; idx < rows * N_TOK; idx += kTcThreads) {
-      const int ol = ks * rows + idx % rows, tok = idx / rows;
-      const int o = o0 + ol, m = t0 + tok;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int peer = 0; peer < prm.split_k; ++peer) {
-        const uint32_t base = map_peer_smem(red_addr, (uint32_t)peer);
-#pragma unroll
-        for (int a = 0; a < 4; ++a) acc[a] += ld_peer_f32(base + (uint32_t)(((a * N_TOK + tok) * 128 + ol) * 4));
-      }
-      if (all_ok && o < prm.N_g && m < prm.M) {
-        float b[4] = {0.f, 0.f, 0.f, 0.f};
-        if (bias) {
-#pragma unroll
-          for (int a = 0; a < 4; ++a) b[a] = to_f32(bias[4 * o + a]);
+        for (int t = 0; t < 16; ++t) {
+          const int tok = j * 16 + t;
+          if (tok < m_tile) part[tok * kTcBlockO + o_local] = make_float4(v[0][t], v[1][t], v[2][t], v[3][t]);
         }
-        *reinterpret_cast<uint2*>(y + (int64_t)m * prm.ld_y + 4 * o) =
-            pack4<T>(acc[0] + b[0], acc[1] + b[1], acc[2] + b[2], acc[3] + b[3]);
       }
     }
-    cluster_sync_all();  // peers may still read this CTA's partials until here
   }
 
   // ---------------- teardown ----------------
@@ -282,6 +421,57 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
+}
+
+// Split-K reduction: y[m, 4o..4o+3] = round(sum over the split of the fp32
+// partials + bias).  Launched as a programmatic dependent of the main kernel;
+// it waits for the main grid to finish before reading the partials (the bias
+// is read before that only when the caller declared the weights static).
+template <typename T>
+__global__ void __launch_bounds__(256)
+qlin_splitk_reduce_kernel(const float4* __restrict__ partials, int split, int t_blocks, int o_blocks,
+                          int n_tok, const T* __restrict__ bias, T* __restrict__ y, int64_t ld_y, int M,
+                          int N_g, int static_weights) {
+  pdl_launch_dependents();
+  const int64_t per_slot = (int64_t)t_blocks * o_blocks * n_tok * kTcBlockO;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool live = idx < per_slot;
+  // idx -> (t-block, o-block, token, row) in the partials' layout
+  const int row = (int)(idx % kTcBlockO);
+  const int tok = (int)((idx / kTcBlockO) % n_tok);
+  const int ob = (int)((idx / ((int64_t)kTcBlockO * n_tok)) % o_blocks);
+  const int tb = (int)(idx / ((int64_t)kTcBlockO * n_tok * o_blocks));
+  const int o = ob * kTcBlockO + row, m = tb * n_tok + tok;
+  const bool valid = live && o < N_g && m < M;
+  T braw[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) braw[a] = from_f32<T>(0.f);
+  if (static_weights && valid && bias) {
+#pragma unroll
+    for (int a = 0; a < 4; ++a) braw[a] = bias[4 * o + a];
+  }
+  pdl_wait_prior();
+  if (!valid) return;
+  if (!static_weights && bias) {
+#pragma unroll
+    for (int a = 0; a < 4; ++a) braw[a] = bias[4 * o + a];
+  }
+  // All slots are loaded before any is summed, so the loads are in flight
+  // together rather than one L2 round trip per slot.
+  float4 v[kTcMaxSplit];
+#pragma unroll
+  for (int s = 0; s < kTcMaxSplit; ++s)
+    v[s] = s < split ? partials[s * per_slot + idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int s = 0; s < kTcMaxSplit; ++s) {
+    acc.x += v[s].x; acc.y += v[s].y; acc.z += v[s].z; acc.w += v[s].w;
+  }
+  float b[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) b[a] = to_f32(braw[a]);
+  *reinterpret_cast<uint2*>(y + (int64_t)m * ld_y + 4 * o) =
+      pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]);
 }
 
 }  // namespace qlin

@@ -87,7 +87,7 @@ def _weights(ws):
 
 
 def _forward_impl(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=None, lora_scale=0.0,
-                  algo=_lib.ALGO_AUTO):
+                  algo=_lib.ALGO_AUTO, static_weights=False):
     in_groups, out_groups = _validate(x, wr, wi, wj, wk)
     if bias is not None and (bias.dim() != 1 or bias.shape[0] != 4 * out_groups):
         raise ValueError(f"bias must be [{4 * out_groups}], got {tuple(bias.shape)}")
@@ -122,7 +122,8 @@ def _forward_impl(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=None, lora_s
     if M:
         with torch.cuda.device(dev):
             _lib.forward_raw(x2, ld_x, ws, ld_w, b, la, lb, rank, lora_scale, y, 4 * out_groups,
-                             M, in_groups, out_groups, algo)
+                             M, in_groups, out_groups, algo,
+                             _lib.FLAG_STATIC_WEIGHTS if static_weights else 0)
     return y.reshape(*lead, 4 * out_groups)
 
 
@@ -188,13 +189,19 @@ class _QLinFn(torch.autograd.Function):
 
 
 def fused_quaternion_linear(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=None,
-                            lora_scale: float = 0.0):
-    """``quaternion_linear(x) + bias + lora_scale * (x A^T) B^T`` in one device call."""
+                            lora_scale: float = 0.0, static_weights: bool = False):
+    """``quaternion_linear(x) + bias + lora_scale * (x A^T) B^T`` in one device call.
+
+    ``static_weights=True`` declares that nothing queued earlier on the current
+    stream writes the weights, bias or LoRA B (inference with fixed weights):
+    the kernel may then stream them while the previous kernel finishes.
+    """
     if torch.is_grad_enabled() and any(
         t is not None and t.requires_grad for t in (x, wr, wi, wj, wk, bias, lora_a, lora_b)
     ):
         return _QLinFn.apply(x, wr, wi, wj, wk, bias, lora_a, lora_b, float(lora_scale))
-    return _forward_impl(x, wr, wi, wj, wk, bias, lora_a, lora_b, lora_scale)
+    return _forward_impl(x, wr, wi, wj, wk, bias, lora_a, lora_b, lora_scale,
+                         static_weights=static_weights)
 
 
 def quaternion_linear(x, wr, wi, wj, wk) -> torch.Tensor:
@@ -227,6 +234,10 @@ class QuaternionLinear(nn.Module):
             self.bias = nn.Parameter(torch.empty(out_features, **fk))
         else:
             self.register_parameter("bias", None)
+        # Inference hint (not part of the state dict): when True, forward
+        # declares the weights static for the duration of the call, letting
+        # the kernel stream them while the previous kernel of the stream ends.
+        self.static_weights = False
         self.reset_parameters()
 
     def reset_parameters(self) -> None:
@@ -239,7 +250,8 @@ class QuaternionLinear(nn.Module):
             nn.init.uniform_(self.bias, -bound, bound)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return fused_quaternion_linear(x, self.wr, self.wi, self.wj, self.wk, self.bias)
+        return fused_quaternion_linear(x, self.wr, self.wi, self.wj, self.wk, self.bias,
+                                       static_weights=self.static_weights)
 
     def real_block_matrix(self) -> torch.Tensor:
         """The equivalent real ``[out_features, in_features]`` matrix (verification only)."""

@@ -42,8 +42,11 @@ def test_status_strings(qb):
 def test_workspace_size(qb):
     import torch
     assert qb._lib.workspace_size(torch.float32, 128, 256, 256, 0) == 0
+    # decode-sized: LoRA t (bf16 and fp32 copies) + split-K partials, no planar x
     ws = qb._lib.workspace_size(torch.bfloat16, 16, 1024, 1024, 32)
-    assert ws >= 4 * 16 * 1024 * 2 + 16 * 32 * 2
+    assert ws >= 16 * 32 * 2 + 16 * 32 * 4 + 2 * 8 * 16 * 128 * 16
+    # prefill-sized: planar copy of x
+    assert qb._lib.workspace_size(torch.bfloat16, 2048, 1024, 2752, 0) >= 4 * 2048 * 1024 * 2
     with pytest.raises(ValueError):
         qb._lib.workspace_size(torch.bfloat16, -1, 1024, 1024, 0)
 
@@ -54,6 +57,9 @@ def test_shape_errors_are_reported_before_device_use(qb):
     # ld_x < 4*K_g -> QLIN_ERR_SHAPE, no CUDA call needed
     code = lib.qlin_forward(1, 1, 10, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, P)
     assert code == 1
+    # unknown flag bits are refused (after the shape checks, before any device use)
+    code = lib.qlin_forward_ex(1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 2, P)
+    assert code == 8
     # M == 0 is a no-op that succeeds without a device
     code = lib.qlin_forward(1, P, 16, P, P, P, P, 4, P, P, P, 0, 0.0, P, 16, 0, 4, 4, P, 0, P)
     assert code == 0
