@@ -90,7 +90,7 @@ int max_split_for(int64_t M, int64_t K_g, int64_t N_g, int64_t sms) {
   const int64_t n_tok = n_tok_for(M);
   const int64_t tiles = ((N_g + kTcBlockO - 1) / kTcBlockO) * ((M + n_tok - 1) / n_tok);
   const int64_t chunks = (K_g + kTcChunk - 1) / kTcChunk;
-  if (tiles * 2 > sms) return 1;
+  if (tiles == 0 || tiles * 2 > sms) return 1;
   const int64_t s = std::min<int64_t>({(int64_t)kTcMaxSplit, chunks, std::max<int64_t>(1, sms / tiles)});
   return (int)std::max<int64_t>(1, s);
 }

@@ -49,6 +49,8 @@ def test_workspace_size(qb):
     assert qb._lib.workspace_size(torch.bfloat16, 2048, 1024, 2752, 0) >= 4 * 2048 * 1024 * 2
     with pytest.raises(ValueError):
         qb._lib.workspace_size(torch.bfloat16, -1, 1024, 1024, 0)
+    # an empty batch needs no split-K partials (and must not divide by zero tiles)
+    assert qb._lib.workspace_size(torch.bfloat16, 0, 1024, 1024, 0) == 0
 
 
 def test_shape_errors_are_reported_before_device_use(qb):
