@@ -142,6 +142,40 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int* alg
 int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank);
 
 /*
+ * Allocation-free variant of qlin_forward (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory where they run the layer
+ * (code that must not call cudaMalloc mid-stream because it can synchronise
+ * the device, framework plugins that are handed only their input and output
+ * buffers, runtimes that forbid allocation after start-up).  Same arguments
+ * and kernels as qlin_forward, but no workspace: the scratch comes from a
+ * fixed buffer of QLIN_NOALLOC_SCRATCH_BYTES compiled into the library, which
+ * every GPU that loads the library holds until the process exits.
+ *
+ *  - Problems whose qlin_workspace_size exceeds QLIN_NOALLOC_SCRATCH_BYTES
+ *    (8 MiB: decode-sized layers; M * in_features up to about 4 Mi elements
+ *    when M > 64) are refused with QLIN_ERR_WORKSPACE before any device work.
+ *  - The first call on a device looks up the buffer's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - All calls on a device share the one buffer and it keeps the last call's
+ *    contents (nothing in it needs to start at zero).  Calls that overlap on
+ *    the GPU -- on different streams, or from different threads -- race on
+ *    it; serialise them (one stream, or events between streams).
+ * Nothing is allocated: no cudaMalloc, no cudaFree, no allocating library call.
+ */
+#define QLIN_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+int qlin_forward_noalloc(int dtype,
+                         const void* x, int64_t ld_x,
+                         const void* wr, const void* wi, const void* wj, const void* wk,
+                         int64_t ld_w,
+                         const void* bias,
+                         const void* lora_a, const void* lora_b, int rank, float lora_scale,
+                         void* y, int64_t ld_y,
+                         int64_t M, int64_t K_g, int64_t N_g,
+                         void* stream);
+
+/*
  * Device-side error word.  Every wait inside the kernels (TMA arrival, MMA
  * completion) is bounded; a wait that runs out records QLIN_ERR_TIMEOUT here
  * and the kernel returns without further work instead of hanging the GPU.

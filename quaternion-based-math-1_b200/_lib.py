@@ -42,6 +42,7 @@ EXPORTED = (
     "qlin_plan",
     "qlin_get_device_error",
     "qlin_gather_columns",
+    "qlin_forward_noalloc",
 )
 
 
@@ -77,6 +78,8 @@ def load(path: str | None = None):
         lib.qlin_plan.restype = I
         lib.qlin_get_device_error.argtypes = [P, I, ctypes.POINTER(I)]
         lib.qlin_get_device_error.restype = I
+        lib.qlin_forward_noalloc.argtypes = fwd[:-2] + [P]
+        lib.qlin_forward_noalloc.restype = I
         lib.qlin_gather_columns.argtypes = [I, P, P, I64, I64, I64, I64, P]
         lib.qlin_gather_columns.restype = I
         if path is None:

@@ -574,3 +574,63 @@ int qlin_gather_columns(int dtype, const void* src, void* dst, int64_t G, int64_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory at the point where they run
+// the layer: code that must not call cudaMalloc mid-stream (it can
+// synchronise the device), plugins of host frameworks that hand out only
+// input and output buffers, and runtimes that forbid allocation after
+// start-up.  qlin_forward_noalloc serves them with the same kernels as
+// qlin_forward, taking its scratch from a fixed buffer compiled into this
+// library instead of a caller-provided workspace.
+// ---------------------------------------------------------------------------
+
+// The fixed scratch buffer.  Every GPU that loads this library holds it until
+// the process exits; every call on a device shares it.  In host code the name
+// is only a stand-in: its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[QLIN_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch for the current device, looked up once
+// per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QLIN_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return QLIN_ERR_LAUNCH;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return QLIN_OK;
+}
+
+}  // namespace
+
+extern "C" int qlin_forward_noalloc(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi,
+                                    const void* wj, const void* wk, int64_t ld_w, const void* bias,
+                                    const void* lora_a, const void* lora_b, int rank, float lora_scale,
+                                    void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
+                                    void* stream) {
+  size_t need = 0;
+  int st = qlin_workspace_size(dtype, M, K_g, N_g, rank, &need);
+  if (st != QLIN_OK) return st;
+  // Problems whose scratch exceeds the fixed buffer are refused up front.
+  if (need > (size_t)QLIN_NOALLOC_SCRATCH_BYTES) return QLIN_ERR_WORKSPACE;
+  void* ws = nullptr;
+  if (need > 0 && M > 0) {
+    st = noalloc_scratch(&ws);
+    if (st != QLIN_OK) return st;
+  }
+  // The scratch needs no initial contents: every byte a call reads was
+  // written earlier in the same call.
+  return qlin_forward_ex(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
+                         ld_y, M, K_g, N_g, ws, ws ? (size_t)QLIN_NOALLOC_SCRATCH_BYTES : 0,
+                         QLIN_ALGO_AUTO, 0, stream);
+}
