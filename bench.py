@@ -196,7 +196,10 @@ def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES, flags=0):
     rank = 0 if lay.lora_a is None else lay.lora_a.shape[0]
     ys = [torch.empty(M, 4 * N_g, dtype=dt, device=dev) for _ in range(ncopy)]
     ws_bytes = qb._lib.workspace_size(dt, M, K_g, N_g, rank)
-    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    # a zero-filled workspace reused by every call (QLIN_FLAG_ZEROED_WORKSPACE):
+    # decode-sized K splits are then summed inside the main kernel
+    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    flags |= qb._lib.FLAG_ZEROED_WORKSPACE
     lib = qb._lib.load()
     code = qb._lib.dtype_code(dt)
     stream_of = qb._lib.stream_handle
@@ -214,7 +217,7 @@ def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES, flags=0):
             qb._lib.check(st, "qlin_forward")
 
     with torch.cuda.device(dev):
-        plan = qb._lib.plan(dt, M, K_g, N_g, rank)
+        plan = qb._lib.plan(dt, M, K_g, N_g, rank, flags=flags)
     return call, ncopy, copies, ys, plan
 
 

@@ -60,8 +60,20 @@ enum {
  * x, the workspace and y are still only touched after it completed.
  * Without the flag every kernel waits for its predecessor before reading
  * any memory (plain stream order), overlapping only its launch and set-up.
+ *
+ * QLIN_FLAG_ZEROED_WORKSPACE: the workspace was zero-filled before its first
+ * use and is only passed to calls of this library that are ordered with one
+ * another (one stream).  Its first QLIN_WORKSPACE_COUNTER_BYTES bytes then
+ * hold per-tile arrival counters that every call leaves at zero again, and a
+ * K-split problem of at most 4 tokens sums its partial products inside the
+ * main kernel (the last CTA of each tile to arrive) instead of in a separate
+ * reduction kernel: one launch and one kernel hand-off fewer per call.  One
+ * zeroed workspace may serve problems of any size: every non-zero
+ * qlin_workspace_size() includes the counter bytes at its start, which no
+ * other use of the workspace touches.
  */
-enum { QLIN_FLAG_STATIC_WEIGHTS = 1 };
+enum { QLIN_FLAG_STATIC_WEIGHTS = 1, QLIN_FLAG_ZEROED_WORKSPACE = 2 };
+#define QLIN_WORKSPACE_COUNTER_BYTES 4096u
 
 /* Human-readable name of a status code (static storage). */
 const char* qlin_status_string(int status);
@@ -129,13 +141,14 @@ int qlin_forward_ex(int dtype,
                     int algo, int flags, void* stream);
 
 /*
- * Launch plan qlin_forward uses for this problem on the current device
- * (diagnostics; no reference counterpart).  Fills every non-null output:
+ * Launch plan qlin_forward_ex uses for this problem with these flags on the
+ * current device (diagnostics; no reference counterpart; flags 0 is
+ * qlin_forward's plan).  Fills every non-null output:
  * algo (QLIN_ALGO_*, assuming aligned pointers), tokens per tensor-core tile,
  * K split (CTAs sharing one output tile), kernel launches per call, and how
  * many CTAs of the tensor-core kernel the device keeps resident at once.
  */
-int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int* algo,
+int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flags, int* algo,
               int* tile_tokens, int* split_k, int* launches, int* resident_ctas);
 
 /* Which algorithm qlin_forward would pick for this problem (QLIN_ALGO_*). */

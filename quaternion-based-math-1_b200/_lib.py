@@ -22,6 +22,7 @@ LIB_PATH = os.path.join(PKG_DIR, "lib", "libqlin_b200.so")
 F32, BF16, F16 = 0, 1, 2
 ALGO_AUTO, ALGO_SIMT, ALGO_TC = 0, 1, 2
 FLAG_STATIC_WEIGHTS = 1
+FLAG_ZEROED_WORKSPACE = 2
 
 OK = 0
 ERR_SHAPE = 1
@@ -74,7 +75,7 @@ def load(path: str | None = None):
         lib.qlin_select_algo.argtypes = [I, I64, I64, I64, I]
         lib.qlin_select_algo.restype = I
         IP = ctypes.POINTER(I)
-        lib.qlin_plan.argtypes = [I, I64, I64, I64, I, IP, IP, IP, IP, IP]
+        lib.qlin_plan.argtypes = [I, I64, I64, I64, I, I, IP, IP, IP, IP, IP]
         lib.qlin_plan.restype = I
         lib.qlin_get_device_error.argtypes = [P, I, ctypes.POINTER(I)]
         lib.qlin_get_device_error.restype = I
@@ -131,10 +132,14 @@ def device_error(device: torch.device | None = None, clear: bool = True) -> int:
     return int(st.value)
 
 
-def plan(dtype: torch.dtype, M: int, K_g: int, N_g: int, rank: int) -> dict:
-    """Launch plan of qlin_forward on the current device (see qlin_plan)."""
+def plan(dtype: torch.dtype, M: int, K_g: int, N_g: int, rank: int, flags: int | None = None) -> dict:
+    """Launch plan on the current device (see qlin_plan).  ``flags`` defaults
+    to the flags :func:`forward_raw` passes for this problem."""
+    if flags is None:
+        flags = FLAG_ZEROED_WORKSPACE if _uses_zeroed_workspace(dtype, M) else 0
     outs = [ctypes.c_int(0) for _ in range(5)]
-    check(load().qlin_plan(dtype_code(dtype), M, K_g, N_g, rank, *(ctypes.byref(o) for o in outs)),
+    check(load().qlin_plan(dtype_code(dtype), M, K_g, N_g, rank, int(flags),
+                           *(ctypes.byref(o) for o in outs)),
           "qlin_plan")
     algo, tok, split, launches, resident = (o.value for o in outs)
     return {"algo": {ALGO_SIMT: "simt", ALGO_TC: "tcgen05"}.get(algo, str(algo)),
@@ -145,13 +150,47 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
+# Decode-sized calls (few tokens) run on a zero-filled workspace kept per
+# (device, stream): with QLIN_FLAG_ZEROED_WORKSPACE their K split is summed
+# inside the main kernel, one launch fewer.  Calls on one stream are ordered,
+# so they may share it; each call leaves its counter bytes at zero.
+_ZEROED_MAX_TOKENS = 4
+_zeroed_ws: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _uses_zeroed_workspace(dtype: torch.dtype, M: int) -> bool:
+    return dtype in (torch.bfloat16, torch.float16) and 0 < M <= _ZEROED_MAX_TOKENS
+
+
+def zeroed_workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    """The zero-filled workspace of the current stream of ``device``, grown to
+    ``nbytes`` if needed; None while a CUDA graph is being captured and the
+    cached buffer is too small (the caller then uses a plain workspace)."""
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    buf = _zeroed_ws.get(key)
+    if buf is not None and buf.numel() >= nbytes:
+        return buf
+    if torch.cuda.is_current_stream_capturing():
+        return None
+    buf = torch.zeros(max(nbytes, 64 * 1024), dtype=torch.uint8, device=device)
+    _zeroed_ws[key] = buf
+    return buf
+
+
 def forward_raw(x2, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y2, ld_y,
                 M, K_g, N_g, algo=ALGO_AUTO, flags=0):
     """Call ``qlin_forward_ex`` on prepared 2-D device tensors (see linear.py)."""
     lib = load()
     dev = x2.device
     ws_bytes = workspace_size(x2.dtype, M, K_g, N_g, rank)
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev) if ws_bytes else None
+    ws = None
+    if ws_bytes and _uses_zeroed_workspace(x2.dtype, M):
+        ws = zeroed_workspace(dev, ws_bytes)
+        if ws is not None:
+            flags |= FLAG_ZEROED_WORKSPACE
+    if ws is None and ws_bytes:
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     code = lib.qlin_forward_ex(
         dtype_code(x2.dtype), _ptr(x2), ld_x, _ptr(w[0]), _ptr(w[1]), _ptr(w[2]), _ptr(w[3]), ld_w,
         _ptr(bias), _ptr(lora_a), _ptr(lora_b), int(rank), float(lora_scale),

@@ -100,13 +100,23 @@ int max_split_for(int64_t M, int64_t K_g, int64_t N_g, int64_t sms) {
 // split, tile, token and row).  CUDA-core path: LoRA t ([M, rank] fp32).
 struct WsLayout {
   size_t xp_off = 0, xp_bytes = 0, t_off = 0, t_bytes = 0, tf_off = 0, tf_bytes = 0;
-  size_t part_off = 0, part_bytes = 0, total = 0;
+  size_t part_off = 0, part_bytes = 0, cnt_off = 0, cnt_bytes = 0, total = 0;
   int64_t ld_t = 0;
 };
 
+// Tokens up to which a K split sums its partials inside the main kernel (the
+// last CTA of each tile to arrive reads every slot); above, a separate
+// reduction kernel spreads that work over the device.
+constexpr int64_t kFusedReduceMaxTokens = 4;
+
 WsLayout ws_layout(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
   WsLayout w;
-  size_t off = 0;
+  // The first QLIN_WORKSPACE_COUNTER_BYTES of every non-empty workspace are
+  // the arrival counters of the fused split-K reduction (used only under
+  // QLIN_FLAG_ZEROED_WORKSPACE); nothing else is ever placed there.
+  w.cnt_off = 0;
+  w.cnt_bytes = QLIN_WORKSPACE_COUNTER_BYTES;
+  size_t off = w.cnt_bytes;
   if (dtype != QLIN_F32) {
     w.xp_off = off;
     w.xp_bytes = M > kStackMaxTokens ? (size_t)(4 * M * K_g * 2) : 0;
@@ -131,7 +141,8 @@ WsLayout ws_layout(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
     w.tf_bytes = (size_t)(M * rank * 4);
     off = (size_t)round_up((int64_t)(off + w.tf_bytes), 256);
   }
-  w.total = off;
+  // A problem that needs no scratch needs no counters either.
+  w.total = (M == 0 || off == w.cnt_bytes) ? 0 : off;
   return w;
 }
 
@@ -221,6 +232,9 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
   prm.split_k = split;
   prm.partials = split > 1 ? partials : nullptr;
   if (split > 1 && !partials) return QLIN_ERR_WORKSPACE;
+  prm.fuse_reduce = (split > 1 && M <= kFusedReduceMaxTokens && prm.counters) ? 1 : 0;
+  // one counter per output tile, all inside the counter bytes
+  if (prm.fuse_reduce && o_blocks * t_blocks * 4 > (int64_t)QLIN_WORKSPACE_COUNTER_BYTES) prm.fuse_reduce = 0;
 
   // Programmatic dependent launch: the kernel's set-up overlaps the tail of
   // the previous kernel of the stream; it waits for that kernel
@@ -238,7 +252,7 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], maps[3], maps[4],
                                      maps[5], maps[6], prm);
   if (e != cudaSuccess) return QLIN_ERR_LAUNCH;
-  if (split > 1) {
+  if (split > 1 && !prm.fuse_reduce) {
     // The reduction is a programmatic dependent of the main kernel, which
     // lets it launch at once; it waits for the main grid before reading.
     const int64_t threads = t_blocks * o_blocks * N_TOK * kTcBlockO;
@@ -272,6 +286,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
 
   // 1. prologue: component planes of x (plane mode) and the scaled LoRA down
   //    projection; none for stacked mode without LoRA
+  int after_prologue = 0;
   {
     const int64_t planar_blocks = stack ? 0 : (M * (K_g / 8) + 255) / 256;
     const int rr = stack ? 1 : 8;
@@ -293,6 +308,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
                             : cudaLaunchKernelEx(&pc, qlin_prologue_kernel<T, 8>, x, ld_x, xp, M, K_g,
                                                  planar_blocks, lora_a, rank, lora_scale, t, L.ld_t);
       if (e != cudaSuccess) return QLIN_ERR_LAUNCH;
+      after_prologue = 1;
     }
   }
   // 2. tensor maps
@@ -339,6 +355,10 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
   prm.split_k = 1;
   prm.partials = nullptr;
   prm.static_weights = (flags & QLIN_FLAG_STATIC_WEIGHTS) ? 1 : 0;
+  prm.counters = (flags & QLIN_FLAG_ZEROED_WORKSPACE) ? reinterpret_cast<unsigned*>(ws + L.cnt_off)
+                                                       : nullptr;
+  prm.fuse_reduce = 0;
+  prm.after_prologue = after_prologue;
   float4* partials = L.part_bytes ? reinterpret_cast<float4*>(ws + L.part_off) : nullptr;
   switch (n_tok) {
     case 16: return launch_tc_impl<T, 16>(dev, maps, prm, M, K_g, N_g, partials, stream);
@@ -431,7 +451,7 @@ const char* qlin_status_string(int status) {
   }
 }
 
-int qlin_abi_version(void) { return 100; }
+int qlin_abi_version(void) { return 101; }
 
 int qlin_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, size_t* bytes) {
   if (!bytes) return QLIN_ERR_ARG;
@@ -446,9 +466,10 @@ int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
   return select_algo(dtype);
 }
 
-int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int* algo, int* tile_tokens,
-              int* split_k, int* launches, int* resident_ctas) {
+int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flags, int* algo,
+              int* tile_tokens, int* split_k, int* launches, int* resident_ctas) {
   if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
+  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE)) return QLIN_ERR_ARG;
   if (M <= 0 || K_g <= 0 || N_g <= 0 || rank < 0) return QLIN_ERR_SHAPE;
   DeviceInfo* dev = nullptr;
   int st = device_info(&dev);
@@ -470,7 +491,8 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int* alg
                        : plan_tc<__half, 128>(dev, M, K_g, N_g, &sp, &res); break;
     }
     if (st != QLIN_OK) return st;
-    nl = 1 + ((M > kStackMaxTokens || rank > 0) ? 1 : 0) + (sp > 1 ? 1 : 0);
+    const bool fused = (flags & QLIN_FLAG_ZEROED_WORKSPACE) && M <= kFusedReduceMaxTokens;
+    nl = 1 + ((M > kStackMaxTokens || rank > 0) ? 1 : 0) + ((sp > 1 && !fused) ? 1 : 0);
   } else {
     nl = rank > 0 ? 2 : 1;
   }
@@ -490,7 +512,7 @@ int qlin_forward_ex(int dtype, const void* x, int64_t ld_x, const void* wr, cons
   if (st != QLIN_OK) return st;
   if (M == 0) return QLIN_OK;
   if (algo < QLIN_ALGO_AUTO || algo > QLIN_ALGO_TC) return QLIN_ERR_ARG;
-  if (flags & ~QLIN_FLAG_STATIC_WEIGHTS) return QLIN_ERR_ARG;
+  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE)) return QLIN_ERR_ARG;
   if (rank == 0) lora_a = lora_b = nullptr;
   DeviceInfo* dev = nullptr;
   st = device_info(&dev);
@@ -628,9 +650,11 @@ extern "C" int qlin_forward_noalloc(int dtype, const void* x, int64_t ld_x, cons
     st = noalloc_scratch(&ws);
     if (st != QLIN_OK) return st;
   }
-  // The scratch needs no initial contents: every byte a call reads was
-  // written earlier in the same call.
+  // The scratch starts zero-filled (a device global) and only calls of this
+  // entry point use it, so it meets QLIN_FLAG_ZEROED_WORKSPACE: its counter
+  // bytes are zero between calls.  Every other byte a call reads was written
+  // earlier in the same call.
   return qlin_forward_ex(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
                          ld_y, M, K_g, N_g, ws, ws ? (size_t)QLIN_NOALLOC_SCRATCH_BYTES : 0,
-                         QLIN_ALGO_AUTO, 0, stream);
+                         QLIN_ALGO_AUTO, ws ? QLIN_FLAG_ZEROED_WORKSPACE : 0, stream);
 }

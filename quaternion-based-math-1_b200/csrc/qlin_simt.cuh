@@ -198,17 +198,18 @@ qlin_planarize_kernel(const T* __restrict__ x, int64_t ld_x, T* __restrict__ xp,
 //    (16-byte) vectors, fp32 accumulation, rounded to T once.  RR = 1 spreads
 //    a few tokens over many blocks; RR = 8 reuses each x row for 8 ranks.
 // Launched as a programmatic dependent of the previous kernel of the stream:
-// it lets the next kernel launch, then waits for the previous one before
-// touching memory.  Requires K % 8 == 0 and 16-byte aligned x, lora_a and
-// rows (ld_x % 8 == 0).
+// it waits for that kernel, then lets the next kernel (this call's main
+// kernel) launch, so that the main kernel's launch implies that all earlier
+// work of the stream is complete.  Requires K % 8 == 0 and 16-byte aligned x,
+// lora_a and rows (ld_x % 8 == 0).
 template <typename T, int RR>
 __global__ void __launch_bounds__(256)
 qlin_prologue_kernel(const T* __restrict__ x, int64_t ld_x, T* __restrict__ xp, int64_t M, int64_t K_g,
                      int64_t planar_blocks, const T* __restrict__ lora_a, int rank, float lora_scale,
                      T* __restrict__ t_tc, int64_t ld_t) {
   static_assert(sizeof(T) == 2, "16-bit elements");
-  pdl_launch_dependents();
   pdl_wait_prior();
+  pdl_launch_dependents();
   if ((int64_t)blockIdx.x < planar_blocks) {
     const int64_t groups = K_g / 8;
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

@@ -29,7 +29,9 @@
 // quaternions (64-byte rows, 64-byte TMA/UMMA swizzle).  With few tiles
 // (decode) the chunks of one tile are split over several CTAs so that every
 // SM streams weights; their fp32 partials of the real tokens go to the
-// workspace and a small dependent kernel sums them.  LoRA: the scaled down
+// workspace and are summed by a small dependent kernel or, for at most four
+// tokens on a zero-filled workspace, by the last CTA of the tile to finish
+// (arrival counter).  LoRA: the scaled down
 // projection t (prologue kernel) is the B operand of four extra UMMAs per 32
 // ranks whose A operands are the [o, a]-strided rows of LoRA B, accumulated
 // before the single rounding.
@@ -39,7 +41,11 @@
 // TMEM, descriptor prefetch) overlaps that kernel's tail, and it waits
 // (griddepcontrol.wait) before it reads or writes memory -- except that with
 // static weights (the caller's promise that earlier work does not write the
-// weights) the first weight tiles are requested before the wait.
+// weights) the first weight tiles are requested before the wait, and that
+// after this call's prologue (which lets the main kernel launch only once it
+// has itself waited for all earlier work) the main kernel streams weights and
+// builds x operands while the prologue runs, waiting only before it loads
+// the prologue's outputs.
 //
 // Roles (128 threads): thread 0 issues TMA, warp 1 owns TMEM and its lane 0
 // issues UMMA, warps 2-3 build Xhat (stacked mode), all four warps run the
@@ -93,7 +99,10 @@ struct TcParams {
   int lora_chunks;     // ceil(rank / 32), 0 without LoRA
   int split_k;         // CTAs sharing one output tile along K (1 = no split)
   float4* partials;    // split_k > 1: [split][t_blocks][o_blocks][N_TOK][128] fp32 x4
+  unsigned* counters;  // fused reduction: one arrival counter per output tile, zero between calls
+  int fuse_reduce;     // split_k > 1: the last CTA of a tile to arrive sums the partials
   int static_weights;  // weights/bias/LoRA B are not written by earlier work on the stream
+  int after_prologue;  // launched right after this call's prologue kernel (see below)
 };
 
 __device__ __forceinline__ void builder_bar_sync() {
@@ -106,6 +115,13 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                                              uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
                : "memory");
+}
+
+// Bias element of output row o, component a (zero without a bias or past N_g).
+template <typename T>
+__device__ __forceinline__ T bias_raw_split(const TcParams& prm, int o, int a) {
+  const T* __restrict__ bp = reinterpret_cast<const T*>(prm.bias);
+  return (bp && o < prm.N_g) ? bp[4 * o + a] : from_f32<T>(0.f);
 }
 
 template <typename T, int N_TOK, bool STACK>
@@ -147,6 +163,12 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   // waits (griddepcontrol.wait) for its predecessor to complete before it
   // reads or writes memory the predecessor may use.
   pdl_launch_dependents();
+  // After a prologue, this grid only launches once every prologue CTA has
+  // passed its own griddepcontrol.wait, i.e. once all work queued before
+  // this call has completed.  Weights, bias, x and y are then safe to touch
+  // at once; only the prologue's outputs (x planes, LoRA t) are waited for,
+  // by the TMA producer, before its first load of them.
+  const bool early = prm.static_weights || prm.after_prologue;
 
   auto w_tile = [&](int s, int p) { return smem + s * Cfg::kStageBytes + p * kTcWTileBytes; };
   auto x_tile = [&](int s, int q) {
@@ -201,26 +223,27 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     // With static weights the caller guarantees that no earlier work on the
     // stream writes the weights, bias or LoRA B, so their first tiles are
     // requested before waiting for that work.
-    if (prm.static_weights) issue_pre_weights();
+    if (early) issue_pre_weights();
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
   T bias_raw[4];
-  if (prm.static_weights) load_bias(bias_raw);
+  if (early) load_bias(bias_raw);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Everything below may read what earlier kernels of the stream wrote (x,
   // the prologue's outputs, the workspace) or write what they read (y).
-  pdl_wait_prior();
-  if (!prm.static_weights) load_bias(bias_raw);
+  if (!prm.after_prologue) pdl_wait_prior();
+  if (!early) load_bias(bias_raw);
 
   if (threadIdx.x == 0) {
     // ---------------- TMA producer ----------------
-    if (!prm.static_weights) issue_pre_weights();
+    if (!early) issue_pre_weights();
+    if (prm.after_prologue && (!STACK || my_lora > 0)) pdl_wait_prior();  // x planes / LoRA t
     for (int it = 0; it < pre; ++it) {
       if (it < my_main) {
         if (!STACK) {
@@ -388,10 +411,13 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     }
   } else {
     // K split: fp32 partials of the real tokens go to this CTA's slot of the
-    // workspace as [token][row] float4 (a = 0..3), summed with the bias and
-    // rounded by qlin_splitk_reduce_kernel.
-    float4* part = prm.partials +
-                   ((size_t)(ks * gridDim.z + blockIdx.z) * gridDim.y + blockIdx.y) * (N_TOK * kTcBlockO);
+    // workspace as [token][row] float4 (a = 0..3).  They are summed with the
+    // bias and rounded either by qlin_splitk_reduce_kernel or, for a few
+    // tokens, here: the last CTA of the tile to arrive (arrival counter in the
+    // workspace, reset to zero by that CTA) reads all slots in split order.
+    const size_t slot_stride = (size_t)gridDim.z * gridDim.y * (N_TOK * kTcBlockO);
+    const size_t tile_off = ((size_t)blockIdx.z * gridDim.y + blockIdx.y) * (N_TOK * kTcBlockO);
+    float4* part = prm.partials + (size_t)ks * slot_stride + tile_off;
 #pragma unroll 1
     for (int j = 0; j < jn; ++j) {
       float v[4][16];
@@ -404,6 +430,39 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
           const int tok = j * 16 + t;
           if (tok < m_tile) part[tok * kTcBlockO + o_local] = make_float4(v[0][t], v[1][t], v[2][t], v[3][t]);
         }
+      }
+    }
+    if (prm.fuse_reduce) {
+      __shared__ int s_last;
+      __threadfence();  // this thread's partials are visible device-wide
+      __syncthreads();
+      const unsigned tile_id = blockIdx.z * gridDim.y + blockIdx.y;
+      if (threadIdx.x == 0) s_last = (atomicAdd(&prm.counters[tile_id], 1u) == (unsigned)(prm.split_k - 1));
+      __syncthreads();
+      if (s_last) {
+        __threadfence();
+        const int o = o0 + o_local;
+        float b[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) b[a] = to_f32(bias_raw_split<T>(prm, o, a));
+        for (int tok = 0; tok < m_tile; ++tok) {
+          float4 vs[kTcMaxSplit];
+#pragma unroll
+          for (int sp = 0; sp < kTcMaxSplit; ++sp)
+            vs[sp] = sp < prm.split_k ? __ldcg(prm.partials + (size_t)sp * slot_stride + tile_off +
+                                               tok * kTcBlockO + o_local)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int sp = 0; sp < kTcMaxSplit; ++sp) {
+            acc.x += vs[sp].x; acc.y += vs[sp].y; acc.z += vs[sp].z; acc.w += vs[sp].w;
+          }
+          if (ok && o < prm.N_g) {
+            *reinterpret_cast<uint2*>(y + (int64_t)(t0 + tok) * prm.ld_y + 4 * o) =
+                pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]);
+          }
+        }
+        if (threadIdx.x == 0) prm.counters[tile_id] = 0u;
       }
     }
   }

@@ -51,6 +51,10 @@ def test_workspace_size(qb):
         qb._lib.workspace_size(torch.bfloat16, -1, 1024, 1024, 0)
     # an empty batch needs no split-K partials (and must not divide by zero tiles)
     assert qb._lib.workspace_size(torch.bfloat16, 0, 1024, 1024, 0) == 0
+    # every non-empty workspace starts with the 4096 counter bytes of the
+    # fused split-K reduction, which nothing else uses
+    assert qb._lib.workspace_size(torch.bfloat16, 1, 1024, 1024, 0) >= 4096 + 16 * 16 * 8 * 128 * 16
+    assert qb._lib.workspace_size(torch.float32, 1, 1024, 1024, 8) == 4096 + 256
 
 
 def test_shape_errors_are_reported_before_device_use(qb):
@@ -60,7 +64,7 @@ def test_shape_errors_are_reported_before_device_use(qb):
     code = lib.qlin_forward(1, 1, 10, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, P)
     assert code == 1
     # unknown flag bits are refused (after the shape checks, before any device use)
-    code = lib.qlin_forward_ex(1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 2, P)
+    code = lib.qlin_forward_ex(1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 4, P)
     assert code == 8
     # M == 0 is a no-op that succeeds without a device
     code = lib.qlin_forward(1, P, 16, P, P, P, P, 4, P, P, P, 0, 0.0, P, 16, 0, 4, 4, P, 0, P)

@@ -1,0 +1,119 @@
+"""The K-split reduction fused into the main kernel (QLIN_FLAG_ZEROED_WORKSPACE).
+
+Decode-sized problems split K over several CTAs per output tile.  On a
+zero-filled workspace the last CTA of each tile to finish sums the fp32
+partials (an arrival counter in the workspace's first 4096 bytes, reset by
+that CTA) instead of a separate reduction kernel.  The sum runs over the same
+slots in the same order as the reduction kernel, so results must be
+bit-identical with and without the flag; the counters must be back at zero
+after every call, whatever sequence of problems shares the workspace."""
+
+import pytest
+import torch
+
+from gpu_helpers import rel_err, to_device
+
+pytestmark = pytest.mark.gpu
+
+FLAG_ZEROED = 2
+COUNTER_BYTES = 4096
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+def _call(qb, d, y, M, K_g, N_g, rank, ws, flags):
+    lib = qb._lib.load()
+    n = qb._lib.workspace_size(d["x"].dtype, M, K_g, N_g, rank)
+    assert ws is None or ws.numel() >= n
+    return lib.qlin_forward_ex(qb._lib.dtype_code(d["x"].dtype), _ptr(d["x"]), 4 * K_g,
+                               *(_ptr(w) for w in d["w"]), K_g, _ptr(d["bias"]), _ptr(d["lora_a"]),
+                               _ptr(d["lora_b"]), rank, float(d["scale"]), _ptr(y), 4 * N_g, M, K_g,
+                               N_g, _ptr(ws), n, 0, flags, qb._lib.stream_handle(d["x"].device))
+
+def _both(qb, workloads, cuda, dtype, M, K, N, seed, rank, bias, zeroed_ws):
+    lay = workloads.make_layer(dtype, M, K, N, seed, bias=bias, lora_rank=rank, lora_std=0.02)
+    d = to_device(lay, cuda)
+    K_g, N_g = K // 4, N // 4
+    y_f = torch.empty(M, N, dtype=d["x"].dtype, device=cuda)
+    y_r = torch.empty_like(y_f)
+    ws_plain = torch.empty(max(qb._lib.workspace_size(d["x"].dtype, M, K_g, N_g, rank), 1),
+                           dtype=torch.uint8, device=cuda)
+    assert _call(qb, d, y_f, M, K_g, N_g, rank, zeroed_ws, FLAG_ZEROED) == 0
+    assert _call(qb, d, y_r, M, K_g, N_g, rank, ws_plain, 0) == 0
+    torch.cuda.synchronize()
+    return lay, y_f, y_r
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("rank,bias", [(0, None), (32, "normal")])
+def test_fused_reduction_is_bit_identical(qb, oracle, workloads, cuda, dtype, M, rank, bias):
+    K, N = 2048, 1024
+    ws = torch.zeros(8 << 20, dtype=torch.uint8, device=cuda)
+    lay, y_f, y_r = _both(qb, workloads, cuda, dtype, M, K, N, 100 + M, rank, bias, ws)
+    assert torch.equal(y_f, y_r)
+    want = oracle.forward_rows(lay.x, *lay.weights, bias=lay.bias, lora_a=lay.lora_a,
+                               lora_b=lay.lora_b, lora_scale=lay.lora_scale)
+    assert rel_err(oracle, y_f.float().cpu().numpy(), want) <= 1e-2
+    assert int(ws[:COUNTER_BYTES].count_nonzero()) == 0
+    assert qb.device_error(cuda) == 0
+
+def test_one_zeroed_workspace_serves_a_sequence_of_problems(qb, workloads, cuda):
+    # decode, prefill-like and LoRA problems interleaved on one workspace: the
+    # larger problems write their scratch past the counter bytes, the small
+    # ones keep finding zero counters
+    ws = torch.zeros(8 << 20, dtype=torch.uint8, device=cuda)
+    seq = [(1, 1024, 1024, 0), (100, 512, 512, 16), (2, 4096, 512, 0), (4, 1024, 4096, 32),
+           (1, 1024, 1024, 0), (70, 1024, 256, 0), (3, 2048, 2048, 8), (1, 1024, 1024, 0)]
+    for i, (M, K, N, rank) in enumerate(seq):
+        _, y_f, y_r = _both(qb, workloads, cuda, "bf16", M, K, N, 200 + i, rank, "normal", ws)
+        assert torch.equal(y_f, y_r), (M, K, N, rank)
+        assert int(ws[:COUNTER_BYTES].count_nonzero()) == 0
+    assert qb.device_error(cuda) == 0
+
+def test_fused_reduction_in_a_graph_and_back_to_back(qb, workloads, cuda):
+    lay = workloads.make_layer("bf16", 1, 4096, 4096, 5, bias="normal", lora_rank=0)
+    d = to_device(lay, cuda)
+    K_g = N_g = 1024
+    ws = torch.zeros(qb._lib.workspace_size(torch.bfloat16, 1, K_g, N_g, 0), dtype=torch.uint8,
+                     device=cuda)
+    want = torch.empty(1, 4096, dtype=torch.bfloat16, device=cuda)
+    assert _call(qb, d, want, 1, K_g, N_g, 0, torch.empty_like(ws), 0) == 0
+    outs = [torch.empty_like(want) for _ in range(8)]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        for o in outs:  # eight calls back to back on one workspace
+            assert _call(qb, d, o, 1, K_g, N_g, 0, ws, FLAG_ZEROED) == 0
+    for _ in range(5):
+        graph.replay()
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, want)
+    assert int(ws[:COUNTER_BYTES].count_nonzero()) == 0
+    del graph
+    assert qb.device_error(cuda) == 0
+
+def test_plan_counts_the_fused_reduction(qb, cuda):
+    p0 = qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 0, flags=0)
+    p1 = qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 0, flags=FLAG_ZEROED)
+    assert p0["split_k"] > 1
+    assert p1["launches"] == p0["launches"] - 1 == 1
+    # above four tokens the separate reduction kernel stays
+    p5 = qb._lib.plan(torch.bfloat16, 5, 1024, 1024, 0, flags=FLAG_ZEROED)
+    assert p5["launches"] == 2
+    # the module path uses the zeroed workspace for decode-sized calls
+    assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 32)["launches"] == 2
+
+def test_module_path_keeps_its_workspace_counters_zero(qb, cuda):
+    g = torch.Generator().manual_seed(11)
+    w = [(torch.randn(256, 256, generator=g) / 32).to(cuda, torch.bfloat16) for _ in range(4)]
+    for M in (1, 3, 4, 1):
+        x = torch.randn(M, 1024, generator=g).to(cuda, torch.bfloat16)
+        y = qb.quaternion_linear(x, *w)
+        ref = qb.linear._forward_impl(x, *w, None, None, None, 0.0, algo=qb._lib.ALGO_SIMT)
+        torch.cuda.synchronize()
+        assert (y.float() - ref.float()).abs().max().item() <= 2e-2 * ref.float().abs().max().item()
+    for buf in qb._lib._zeroed_ws.values():
+        assert int(buf[:COUNTER_BYTES].count_nonzero()) == 0
+    assert qb.device_error(cuda) == 0

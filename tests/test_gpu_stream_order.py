@@ -85,6 +85,9 @@ def test_weight_update_right_before_call_is_seen(qb, cuda, M):
 
 
 def test_plan_reports_the_decode_split(qb, cuda):
-    plan = qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 32)
+    # LoRA prologue + main kernel (+ the split-K reduction kernel unless the
+    # workspace is zero-filled, as the module path's decode workspace is)
+    plan = qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 32, flags=0)
     assert plan["algo"] == "tcgen05" and plan["tile_tokens"] == 16
     assert plan["split_k"] > 1 and plan["launches"] == 3
+    assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 32)["launches"] == 2
