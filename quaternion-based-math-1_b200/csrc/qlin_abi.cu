@@ -28,10 +28,10 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   bool init = false;
   int cc_major = 0, cc_minor = 0, num_sms = 0;
-  // per (element type, N_TOK) kernel instance: attributes set, and how many
-  // CTAs of it the device keeps resident at once
-  bool tc_attr_set[2][4] = {{false, false, false, false}, {false, false, false, false}};
-  int resident[2][4] = {};
+  // per (element type, N_TOK, in-kernel LoRA) kernel instance: attributes
+  // set, and how many CTAs of it the device keeps resident at once
+  bool tc_attr_set[2][4][3] = {};
+  int resident[2][4][3] = {};
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mutex;
@@ -174,10 +174,11 @@ bool tc_eligible(int dtype, const void* x, int64_t ld_x, const void* const w[4],
 int select_algo(int dtype) { return dtype == QLIN_F32 ? QLIN_ALGO_SIMT : QLIN_ALGO_TC; }
 
 CUresult encode(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* base, const cuuint64_t* dims,
-                const cuuint64_t* strides, const cuuint32_t* box) {
+                const cuuint64_t* strides, const cuuint32_t* box,
+                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_64B) {
   cuuint32_t estr[3] = {1, 1, 1};
   return g_encode(map, dt, (cuuint32_t)rank, base, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
@@ -185,14 +186,32 @@ CUresult encode(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* base, 
 template <int N_TOK>
 constexpr bool kStackFor = N_TOK <= kStackMaxTokens;
 
-template <typename T, int N_TOK>
+// Where the LoRA down projection runs (kLora*), for ranks up to
+// kTcLoraInRank: on the builder warps' CUDA cores for at most
+// kTcLoraSimtTokens tokens when each split covers at most 4 K chunks (a few
+// hundred multiply-adds per thread, hidden under the weight stream); on the
+// tensor cores inside the main kernel for stacked tiles of at most 32 tokens
+// (their TMEM lanes 64..95 belong to builder warp 2); else in the prologue.
+int lora_mode(int64_t M, int rank, int64_t K_g, int split) {
+  if (rank <= 0 || rank > kTcLoraInRank) return kLoraPrologue;
+  const int64_t chunks = (K_g + kTcChunk - 1) / kTcChunk;
+  if (M <= kTcLoraSimtTokens && (chunks + split - 1) / split <= 4) return kLoraSimt;
+  if (n_tok_for(M) <= 32) return kLoraTc;
+  return kLoraPrologue;
+}
+
+// Threads of a tensor-core CTA: 128, plus two LoRA warps in the CUDA-core mode.
+constexpr int tc_block_threads(int lora) { return lora == kLoraSimt ? kTcMaxThreads : kTcThreads; }
+
+template <typename T, int N_TOK, int LORA>
 int ensure_tc_attrs(DeviceInfo* dev) {
-  using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>>;
-  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>>;
+  using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>, LORA>;
+  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA>;
   const int ti = n_tok_index(N_TOK);
   const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
+  const int li = LORA;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (dev->tc_attr_set[di][ti]) return QLIN_OK;
+  if (dev->tc_attr_set[di][ti][li]) return QLIN_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
       cudaSuccess)
     return QLIN_ERR_LAUNCH;
@@ -209,20 +228,20 @@ int ensure_tc_attrs(DeviceInfo* dev) {
                            cudaSharedmemCarveoutMaxShared) != cudaSuccess)
     return QLIN_ERR_LAUNCH;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kTcThreads, Cfg::kSmemBytes) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, tc_block_threads(LORA), Cfg::kSmemBytes) !=
       cudaSuccess)
     return QLIN_ERR_LAUNCH;
-  dev->resident[di][ti] = per_sm * dev->num_sms;
-  dev->tc_attr_set[di][ti] = true;
+  dev->resident[di][ti][li] = per_sm * dev->num_sms;
+  dev->tc_attr_set[di][ti][li] = true;
   return QLIN_OK;
 }
 
-template <typename T, int N_TOK>
+template <typename T, int N_TOK, int LORA>
 int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& base_prm, int64_t M,
                    int64_t K_g, int64_t N_g, float4* partials, cudaStream_t stream) {
-  using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>>;
-  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>>;
-  int st = ensure_tc_attrs<T, N_TOK>(dev);
+  using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>, LORA>;
+  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA>;
+  int st = ensure_tc_attrs<T, N_TOK, LORA>(dev);
   if (st != QLIN_OK) return st;
   TcParams prm = base_prm;
   const int64_t o_blocks = (N_g + kTcBlockO - 1) / kTcBlockO;
@@ -244,13 +263,13 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
   attr.val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)split, (unsigned)o_blocks, (unsigned)t_blocks);
-  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.blockDim = dim3(tc_block_threads(LORA), 1, 1);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], maps[3], maps[4],
-                                     maps[5], maps[6], prm);
+                                     maps[5], maps[6], maps[7], prm);
   if (e != cudaSuccess) return QLIN_ERR_LAUNCH;
   if (split > 1 && !prm.fuse_reduce) {
     // The reduction is a programmatic dependent of the main kernel, which
@@ -283,14 +302,17 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
   T* t = rank > 0 ? reinterpret_cast<T*>(ws + L.t_off) : nullptr;
   const int n_tok = n_tok_for(M);
   const bool stack = M <= kStackMaxTokens;
+  const int lmode = lora_mode(M, rank, K_g, max_split_for(M, K_g, N_g, dev->num_sms));
+  const bool lora_in = lmode != kLoraPrologue;
 
   // 1. prologue: component planes of x (plane mode) and the scaled LoRA down
-  //    projection; none for stacked mode without LoRA
+  //    projection; none for stacked mode whose LoRA (if any) runs in the
+  //    main kernel
   int after_prologue = 0;
   {
     const int64_t planar_blocks = stack ? 0 : (M * (K_g / 8) + 255) / 256;
     const int rr = stack ? 1 : 8;
-    const int64_t lora_blocks = rank > 0 ? ((M + 7) / 8) * ((rank + rr - 1) / rr) : 0;
+    const int64_t lora_blocks = (rank > 0 && !lora_in) ? ((M + 7) / 8) * ((rank + rr - 1) / rr) : 0;
     const int64_t blocks = planar_blocks + lora_blocks;
     if (blocks > INT32_MAX) return QLIN_ERR_SHAPE;
     if (blocks > 0) {
@@ -312,7 +334,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
     }
   }
   // 2. tensor maps
-  CUtensorMap maps[7];
+  CUtensorMap maps[8];
   std::memset(maps, 0, sizeof(maps));
   for (int p = 0; p < 4; ++p) {
     cuuint64_t dims[2] = {(cuuint64_t)K_g, (cuuint64_t)N_g};
@@ -339,6 +361,18 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
     cuuint32_t tbox[2] = {kTcChunk, (cuuint32_t)n_tok};
     if (encode(&maps[6], dt, 2, t, tdims, tstrides, tbox) != CUDA_SUCCESS) return QLIN_ERR_ALIGN;
     lora_chunks = (int)((rank + kTcChunk - 1) / kTcChunk);
+    if (lmode == kLoraTc || lmode == kLoraSimt) {
+      // lora_a [rank, 4*K_g], rows past rank read as zero: 32-element
+      // swizzled columns (tensor-core operand), or plain 256-element row
+      // pieces (the CUDA-core mode's slice)
+      cuuint64_t adims[2] = {(cuuint64_t)(4 * K_g), (cuuint64_t)rank};
+      cuuint64_t astrides[1] = {(cuuint64_t)(4 * K_g * 2)};
+      const bool tc = lmode == kLoraTc;
+      cuuint32_t abox[2] = {tc ? 32u : (cuuint32_t)kTcLoraSliceBox, (cuuint32_t)kTcLoraInRank};
+      if (encode(&maps[7], dt, 2, const_cast<T*>(lora_a), adims, astrides, abox,
+                 tc ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
+        return QLIN_ERR_ALIGN;
+    }
   }
   // 3. main kernel (+ split-K reduction)
   TcParams prm;
@@ -359,12 +393,21 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
                                                        : nullptr;
   prm.fuse_reduce = 0;
   prm.after_prologue = after_prologue;
+  prm.rank = rank;
+  prm.lora_scale = lora_scale;
+  prm.lora_a = lora_a;
+  prm.ld_a = 4 * K_g;
   float4* partials = L.part_bytes ? reinterpret_cast<float4*>(ws + L.part_off) : nullptr;
   switch (n_tok) {
-    case 16: return launch_tc_impl<T, 16>(dev, maps, prm, M, K_g, N_g, partials, stream);
-    case 32: return launch_tc_impl<T, 32>(dev, maps, prm, M, K_g, N_g, partials, stream);
-    case 64: return launch_tc_impl<T, 64>(dev, maps, prm, M, K_g, N_g, partials, stream);
-    default: return launch_tc_impl<T, 128>(dev, maps, prm, M, K_g, N_g, partials, stream);
+    case 16:
+      if (lmode == kLoraSimt) return launch_tc_impl<T, 16, kLoraSimt>(dev, maps, prm, M, K_g, N_g, partials, stream);
+      if (lmode == kLoraTc) return launch_tc_impl<T, 16, kLoraTc>(dev, maps, prm, M, K_g, N_g, partials, stream);
+      return launch_tc_impl<T, 16, kLoraPrologue>(dev, maps, prm, M, K_g, N_g, partials, stream);
+    case 32:
+      if (lmode == kLoraTc) return launch_tc_impl<T, 32, kLoraTc>(dev, maps, prm, M, K_g, N_g, partials, stream);
+      return launch_tc_impl<T, 32, kLoraPrologue>(dev, maps, prm, M, K_g, N_g, partials, stream);
+    case 64: return launch_tc_impl<T, 64, kLoraPrologue>(dev, maps, prm, M, K_g, N_g, partials, stream);
+    default: return launch_tc_impl<T, 128, kLoraPrologue>(dev, maps, prm, M, K_g, N_g, partials, stream);
   }
 }
 
@@ -422,13 +465,23 @@ int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void*
 }
 
 template <typename T, int N_TOK>
-int plan_tc(DeviceInfo* dev, int64_t M, int64_t K_g, int64_t N_g, int* split, int* resident) {
-  int st = ensure_tc_attrs<T, N_TOK>(dev);
+int plan_tc(DeviceInfo* dev, int64_t M, int64_t K_g, int64_t N_g, int rank, int* split, int* resident) {
+  *split = max_split_for(M, K_g, N_g, dev->num_sms);
+  const int li = lora_mode(M, rank, K_g, *split);
+  int st = QLIN_OK;
+  if constexpr (N_TOK == 16) {
+    st = li == kLoraSimt ? ensure_tc_attrs<T, N_TOK, kLoraSimt>(dev)
+                         : (li == kLoraTc ? ensure_tc_attrs<T, N_TOK, kLoraTc>(dev)
+                                          : ensure_tc_attrs<T, N_TOK, kLoraPrologue>(dev));
+  } else if constexpr (N_TOK == 32) {
+    st = li == kLoraTc ? ensure_tc_attrs<T, N_TOK, kLoraTc>(dev) : ensure_tc_attrs<T, N_TOK, kLoraPrologue>(dev);
+  } else {
+    st = ensure_tc_attrs<T, N_TOK, kLoraPrologue>(dev);
+  }
   if (st != QLIN_OK) return st;
   const int ti = n_tok_index(N_TOK);
   const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
-  *split = max_split_for(M, K_g, N_g, dev->num_sms);
-  *resident = dev->resident[di][ti];
+  *resident = dev->resident[di][ti][li];
   return QLIN_OK;
 }
 
@@ -481,18 +534,19 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flag
     nt = n_tok_for(M);
     const bool bf = dtype == QLIN_BF16;
     switch (nt) {
-      case 16: st = bf ? plan_tc<__nv_bfloat16, 16>(dev, M, K_g, N_g, &sp, &res)
-                       : plan_tc<__half, 16>(dev, M, K_g, N_g, &sp, &res); break;
-      case 32: st = bf ? plan_tc<__nv_bfloat16, 32>(dev, M, K_g, N_g, &sp, &res)
-                       : plan_tc<__half, 32>(dev, M, K_g, N_g, &sp, &res); break;
-      case 64: st = bf ? plan_tc<__nv_bfloat16, 64>(dev, M, K_g, N_g, &sp, &res)
-                       : plan_tc<__half, 64>(dev, M, K_g, N_g, &sp, &res); break;
-      default: st = bf ? plan_tc<__nv_bfloat16, 128>(dev, M, K_g, N_g, &sp, &res)
-                       : plan_tc<__half, 128>(dev, M, K_g, N_g, &sp, &res); break;
+      case 16: st = bf ? plan_tc<__nv_bfloat16, 16>(dev, M, K_g, N_g, rank, &sp, &res)
+                       : plan_tc<__half, 16>(dev, M, K_g, N_g, rank, &sp, &res); break;
+      case 32: st = bf ? plan_tc<__nv_bfloat16, 32>(dev, M, K_g, N_g, rank, &sp, &res)
+                       : plan_tc<__half, 32>(dev, M, K_g, N_g, rank, &sp, &res); break;
+      case 64: st = bf ? plan_tc<__nv_bfloat16, 64>(dev, M, K_g, N_g, rank, &sp, &res)
+                       : plan_tc<__half, 64>(dev, M, K_g, N_g, rank, &sp, &res); break;
+      default: st = bf ? plan_tc<__nv_bfloat16, 128>(dev, M, K_g, N_g, rank, &sp, &res)
+                       : plan_tc<__half, 128>(dev, M, K_g, N_g, rank, &sp, &res); break;
     }
     if (st != QLIN_OK) return st;
     const bool fused = (flags & QLIN_FLAG_ZEROED_WORKSPACE) && M <= kFusedReduceMaxTokens;
-    nl = 1 + ((M > kStackMaxTokens || rank > 0) ? 1 : 0) + ((sp > 1 && !fused) ? 1 : 0);
+    const bool prologue = M > kStackMaxTokens || (rank > 0 && lora_mode(M, rank, K_g, sp) == kLoraPrologue);
+    nl = 1 + (prologue ? 1 : 0) + ((sp > 1 && !fused) ? 1 : 0);
   } else {
     nl = rank > 0 ? 2 : 1;
   }

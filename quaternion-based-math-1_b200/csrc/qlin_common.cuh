@@ -29,6 +29,20 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
 // Four fp32 values -> four 16-bit values packed in 8 bytes (round to nearest even).
+// Dot product of two vectors of eight 16-bit elements (16 bytes each), fp32.
+template <typename T>
+__device__ __forceinline__ float dot8(uint4 a, uint4 b) {
+  const T* pa = reinterpret_cast<const T*>(&a);
+  const T* pb = reinterpret_cast<const T*>(&b);
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    s0 = fmaf(to_f32(pa[i]), to_f32(pb[i]), s0);
+    s1 = fmaf(to_f32(pa[i + 1]), to_f32(pb[i + 1]), s1);
+  }
+  return s0 + s1;
+}
+
 template <typename T> __device__ __forceinline__ uint2 pack4(float a, float b, float c, float d);
 template <> __device__ __forceinline__ uint2 pack4<__nv_bfloat16>(float a, float b, float c, float d) {
   __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
@@ -113,6 +127,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Plain bulk copy global -> this CTA's shared memory (16-byte aligned
+// addresses, size a multiple of 16), completing on an mbarrier.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,

@@ -62,24 +62,60 @@ namespace qlin {
 
 constexpr int kTcBlockO = 128;   // output quaternions per CTA tile (UMMA M)
 constexpr int kTcChunk = 32;     // input quaternions per K chunk (64-byte rows)
-constexpr int kTcThreads = 128;
+constexpr int kTcThreads = 128;      // TMA, UMMA, two builder warps; all four run the epilogue
+constexpr int kTcLoraThreads = 64;   // CUDA-core LoRA: two more warps for the down projection
+constexpr int kTcMaxThreads = kTcThreads + kTcLoraThreads;
+constexpr int kTcEpiBar = 2;         // named barrier of the four epilogue warps
+constexpr int kTcLoraBar = 3;        // named barrier of the two LoRA warps
 constexpr int kTcWTileBytes = kTcBlockO * kTcChunk * 2;  // 8 KB
 constexpr int kTcMaxSplit = 16;  // largest K split of one output tile
 constexpr int kTcBuilderBar = 1; // named barrier of the two builder warps
+constexpr int kTcLoraInRank = 32; // largest LoRA rank whose down projection runs in the main kernel
+constexpr int kTcLoraSimtTokens = 4;  // largest M of the CUDA-core in-kernel down projection
+constexpr int kTcLoraSliceBox = 256;  // elements per row of one lora_a slice load (CUDA-core mode)
+constexpr int kTcLoraSliceMax = 512;  // elements of lora_a rows one split covers (4 chunks)
+// LoRA down projection t = lora_scale * x A^T of the tensor-core kernel:
+enum { kLoraPrologue = 0,  // none, or t from the prologue kernel (TMA-loaded)
+       kLoraTc = 1,        // per split, on the tensor cores (extra UMMA per K step)
+       kLoraSimt = 2 };    // per split, on the builder warps' CUDA cores
+constexpr int kTcTLane = 64;      // TMEM lane of token 0 in the in-kernel LoRA accumulator
 
-template <int N_TOK, bool STACK>
+__host__ __device__ constexpr int tmem_cols_for(int n) {
+  return n <= 32 ? 32 : (n <= 64 ? 64 : (n <= 128 ? 128 : (n <= 256 ? 256 : 512)));
+}
+
+template <int N_TOK, bool STACK, int LORA = kLoraPrologue>
 struct TcCfg {
   // Activation operand per weight component and stage: stacked [4*N_TOK rows]
   // or one plane [N_TOK rows], 64 bytes per row either way.
   static constexpr int kXTileBytes = (STACK ? 4 : 1) * N_TOK * kTcChunk * 2;
-  static constexpr int kStageBytes = 4 * kTcWTileBytes + 4 * kXTileBytes;
-  static constexpr int kFit = (200 * 1024) / kStageBytes;
+  // In-kernel LoRA down projection: the chunk's raw x rows (4 sub-tiles of
+  // 32 elements x N_TOK rows) and the matching 32-element columns of lora_a
+  // (4 sub-tiles x kTcLoraInRank rows).
+  static constexpr int kRawXBytes = LORA == kLoraTc ? 4 * N_TOK * 64 : 0;
+  static constexpr int kLoraABytes = LORA == kLoraTc ? 4 * kTcLoraInRank * 64 : 0;
+  static constexpr int kStageBytes = 4 * kTcWTileBytes + 4 * kXTileBytes + kRawXBytes + kLoraABytes;
+  // CUDA-core LoRA: the split's lora_a slice [32 rows][<= 512 elements],
+  // loaded once, ahead of the weights, as row pieces of kTcLoraSliceBox
+  static constexpr int kSliceBytes = LORA == kLoraSimt ? kTcLoraInRank * kTcLoraSliceMax * 2 : 0;
+  static constexpr int kFit = (200 * 1024 - kSliceBytes) / kStageBytes;
   static constexpr int kStages = kFit > 6 ? 6 : (kFit < 2 ? 2 : kFit);
-  static constexpr int kTmemCols = 4 * N_TOK;  // 64 .. 512, power of two
-  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kSliceOffset = kStages * kStageBytes;
+  // accumulators: 4*N_TOK columns of Y (+ kTcLoraInRank columns of t)
+  static constexpr int kTmemCols = tmem_cols_for(4 * N_TOK + (LORA == kLoraTc ? kTcLoraInRank : 0));
+  static constexpr int kBarOffset = kSliceOffset + kSliceBytes;
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
   static_assert(N_TOK == 16 || N_TOK == 32 || N_TOK == 64 || N_TOK == 128, "UMMA N");
   static_assert(!STACK || N_TOK <= 64, "stacked operand has 4*N_TOK <= 256 rows");
+  static_assert(LORA != kLoraTc || (STACK && N_TOK <= 32), "tensor-core LoRA: stacked, tokens in lanes 64..95");
+  static_assert(LORA != kLoraSimt || (STACK && N_TOK == 16), "CUDA-core LoRA: stacked, at most 4 tokens");
+  // The LoRA down projection's A operand (128 rows from kTcTLane rows before
+  // a raw x sub-tile) stays inside the stage: 4 KB of x operands before the
+  // raw rows, at least 4 KB (raw rows + lora_a) after the last sub-tile.
+  static_assert(LORA != kLoraTc || (4 * kTcWTileBytes + 4 * kXTileBytes >= kTcTLane * 64 &&
+                             kRawXBytes / 4 + kLoraABytes >= (128 - kTcTLane) * 64),
+                "LoRA A-operand window inside the stage");
+  static_assert(kStageBytes % 1024 == 0, "stages keep 1024-byte alignment");
   static_assert(kSmemBytes <= 232448, "fits the 227 KB opt-in shared memory");
 };
 
@@ -103,10 +139,20 @@ struct TcParams {
   int fuse_reduce;     // split_k > 1: the last CTA of a tile to arrive sums the partials
   int static_weights;  // weights/bias/LoRA B are not written by earlier work on the stream
   int after_prologue;  // launched right after this call's prologue kernel (see below)
+  int rank;            // LoRA rank (in-kernel LoRA: ranks >= rank are zero)
+  float lora_scale;    // in-kernel LoRA: t = lora_scale * x A^T
+  const void* lora_a;  // CUDA-core in-kernel LoRA: A [rank, ld_a]
+  int64_t ld_a;
 };
 
 __device__ __forceinline__ void builder_bar_sync() {
   asm volatile("bar.sync %0, %1;" ::"n"(kTcBuilderBar), "n"(64) : "memory");
+}
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kTcEpiBar), "n"(kTcThreads) : "memory");
+}
+__device__ __forceinline__ void lora_bar_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kTcLoraBar), "n"(kTcLoraThreads) : "memory");
 }
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -117,25 +163,29 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
-// Bias element of output row o, component a (zero without a bias or past N_g).
-template <typename T>
-__device__ __forceinline__ T bias_raw_split(const TcParams& prm, int o, int a) {
-  const T* __restrict__ bp = reinterpret_cast<const T*>(prm.bias);
-  return (bp && o < prm.N_g) ? bp[4 * o + a] : from_f32<T>(0.f);
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// fence.acq_rel.gpu, then a relaxed gpu-scope atomic add; returns the old value.
+__device__ __forceinline__ unsigned atomic_add_release_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("fence.acq_rel.gpu;\n\tatom.relaxed.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
-template <typename T, int N_TOK, bool STACK>
-__global__ void __launch_bounds__(kTcThreads, 1)
+template <typename T, int N_TOK, bool STACK, int LORA>
+__global__ void __launch_bounds__(kTcMaxThreads, 1)
 qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant__ CUtensorMap map_wi,
                const __grid_constant__ CUtensorMap map_wj, const __grid_constant__ CUtensorMap map_wk,
                const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_lb,
-               const __grid_constant__ CUtensorMap map_t, const TcParams prm) {
-  using Cfg = TcCfg<N_TOK, STACK>;
+               const __grid_constant__ CUtensorMap map_t, const __grid_constant__ CUtensorMap map_la,
+               const TcParams prm) {
+  using Cfg = TcCfg<N_TOK, STACK, LORA>;
   constexpr int S = Cfg::kStages;
   constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   constexpr uint32_t kIdescPos = make_idesc_f16(128, N_TOK, kFmt, false);
   constexpr uint32_t kIdescNeg = make_idesc_f16(128, N_TOK, kFmt, true);
   constexpr uint32_t kIdescStack = make_idesc_f16(128, STACK ? 4 * N_TOK : N_TOK, kFmt, false);
+  constexpr uint32_t kIdescLoraDown = make_idesc_f16(128, kTcLoraInRank, kFmt, false);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -143,7 +193,9 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* t_full = acc_full + 1;  // LoRA: down projection complete (tensor cores) / lora_a slice loaded (CUDA cores)
+  uint64_t* red_full = t_full + 1;  // fused K-split reduction: all partials are in shared memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued_count = const_cast<int*>(abort_flag) + 1;
   int* consumed_count = issued_count + 1;
@@ -155,7 +207,10 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   const int c_begin = (int)((int64_t)ks * prm.num_chunks / prm.split_k);
   const int c_end = (int)((int64_t)(ks + 1) * prm.num_chunks / prm.split_k);
   const int my_main = c_end - c_begin;
-  const int my_lora = (ks == prm.split_k - 1) ? prm.lora_chunks : 0;
+  // With the down projection in this kernel every split applies the LoRA up
+  // projection to its own partial t (a linear term, summed with the split);
+  // otherwise the last split applies it to the prologue's full t.
+  const int my_lora = (LORA != kLoraPrologue || ks == prm.split_k - 1) ? prm.lora_chunks : 0;
   const int total = my_main + my_lora;
   const int m_tile = (prm.M - t0) < N_TOK ? (prm.M - t0) : N_TOK;  // real tokens in the tile
 
@@ -174,19 +229,39 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   auto x_tile = [&](int s, int q) {
     return smem + s * Cfg::kStageBytes + 4 * kTcWTileBytes + q * Cfg::kXTileBytes;
   };
+  auto raw_tile = [&](int s, int j) {  // raw x rows, elements 32j..32j+31 of the chunk
+    return smem + s * Cfg::kStageBytes + 4 * kTcWTileBytes + 4 * Cfg::kXTileBytes + j * N_TOK * 64;
+  };
+  auto la_tile = [&](int s, int j) {  // lora_a rows, the same 32 elements
+    return smem + s * Cfg::kStageBytes + 4 * kTcWTileBytes + 4 * Cfg::kXTileBytes + Cfg::kRawXBytes +
+           j * kTcLoraInRank * 64;
+  };
   const CUtensorMap* wmap[4] = {&map_wr, &map_wi, &map_wj, &map_wk};
   const int pre = total < S ? total : S;
-  // Weight (and LoRA B) tiles of the first stages.
+  // Weight (and LoRA B) tiles of the first stages; in the CUDA-core LoRA mode
+  // preceded by this split's lora_a slice, so that it arrives first.
   auto issue_pre_weights = [&]() {
+    if (LORA == kLoraSimt) {
+      const int pieces = (4 * kTcChunk * my_main + kTcLoraSliceBox - 1) / kTcLoraSliceBox;
+      mbar_arrive_expect_tx(t_full, pieces * kTcLoraInRank * kTcLoraSliceBox * 2);
+      for (int j = 0; j < pieces; ++j)
+        tma_load_2d(smem + Cfg::kSliceOffset + j * kTcLoraInRank * kTcLoraSliceBox * 2, &map_la, t_full,
+                    4 * kTcChunk * c_begin + kTcLoraSliceBox * j, 0);
+    }
     for (int it = 0; it < pre; ++it) {
       if (it < my_main) {
         const int k = (c_begin + it) * kTcChunk;
-        mbar_arrive_expect_tx(&full[it], 4 * kTcWTileBytes + (STACK ? 0 : 4 * Cfg::kXTileBytes));
+        mbar_arrive_expect_tx(&full[it], 4 * kTcWTileBytes + (STACK ? 0 : 4 * Cfg::kXTileBytes) +
+                                             Cfg::kLoraABytes);
 #pragma unroll
         for (int p = 0; p < 4; ++p) tma_load_2d(w_tile(it, p), wmap[p], &full[it], k, o0);
+        if (LORA == kLoraTc) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tma_load_2d(la_tile(it, j), &map_la, &full[it], 4 * k + 32 * j, 0);
+        }
       } else {
         const int r = (it - my_main) * kTcChunk;
-        mbar_arrive_expect_tx(&full[it], 4 * kTcWTileBytes + N_TOK * kTcChunk * 2);
+        mbar_arrive_expect_tx(&full[it], 4 * kTcWTileBytes + (LORA != kLoraPrologue ? 0 : N_TOK * kTcChunk * 2));
 #pragma unroll
         for (int a = 0; a < 4; ++a) tma_load_3d(w_tile(it, a), &map_lb, &full[it], r, a, o0);
       }
@@ -194,11 +269,12 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   };
   // Bias of this thread's output row as raw bits; converted in the epilogue,
   // so the load latency hides under the main loop.  With a K split the bias
-  // is added by the reduction kernel instead.
+  // is added by the reduction kernel, or by the last CTA of the tile to
+  // arrive when the reduction is fused.
   auto load_bias = [&](T (&raw)[4]) {
     const int ob = o0 + (int)threadIdx.x;
     const T* __restrict__ bp = reinterpret_cast<const T*>(prm.bias);
-    const bool has = bp && prm.split_k == 1 && ob < prm.N_g;
+    const bool has = bp && (prm.split_k == 1 || prm.fuse_reduce) && ob < prm.N_g && threadIdx.x < kTcBlockO;
 #pragma unroll
     for (int a = 0; a < 4; ++a) raw[a] = has ? bp[4 * ob + a] : from_f32<T>(0.f);
   };
@@ -211,6 +287,8 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
+    mbar_init(t_full, 1);
+    mbar_init(red_full, 1);
     *abort_flag = 0;
     *issued_count = 0;
     *consumed_count = 0;
@@ -220,6 +298,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     tma_prefetch_desc(&map_wj);
     tma_prefetch_desc(&map_wk);
     if (!STACK) tma_prefetch_desc(&map_x);
+    if (LORA != kLoraPrologue) tma_prefetch_desc(&map_la);
     // With static weights the caller guarantees that no earlier work on the
     // stream writes the weights, bias or LoRA B, so their first tiles are
     // requested before waiting for that work.
@@ -237,7 +316,8 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   const uint32_t tmem_base = *tmem_slot;
   // Everything below may read what earlier kernels of the stream wrote (x,
   // the prologue's outputs, the workspace) or write what they read (y).
-  if (!prm.after_prologue) pdl_wait_prior();
+  // (the CUDA-core LoRA warps wait on their own, after their first loads)
+  if (!prm.after_prologue && !(LORA == kLoraSimt && warp >= 4)) pdl_wait_prior();
   if (!early) load_bias(bias_raw);
 
   if (threadIdx.x == 0) {
@@ -251,7 +331,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
 #pragma unroll
           for (int q = 0; q < 4; ++q) tma_load_3d(x_tile(it, q), &map_x, &full[it], k, t0, q);
         }
-      } else {
+      } else if (LORA == kLoraPrologue) {
         tma_load_2d(x_tile(it, 0), &map_t, &full[it], (it - my_main) * kTcChunk, t0);
       }
     }
@@ -265,19 +345,24 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
       if (*abort_flag) break;
       if (it < my_main) {
         const int k = (c_begin + it) * kTcChunk;
-        mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + (STACK ? 0 : 4 * Cfg::kXTileBytes));
+        mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + (STACK ? 0 : 4 * Cfg::kXTileBytes) +
+                                            Cfg::kLoraABytes);
 #pragma unroll
         for (int p = 0; p < 4; ++p) tma_load_2d(w_tile(s, p), wmap[p], &full[s], k, o0);
         if (!STACK) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) tma_load_3d(x_tile(s, q), &map_x, &full[s], k, t0, q);
         }
+        if (LORA == kLoraTc) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tma_load_2d(la_tile(s, j), &map_la, &full[s], 4 * k + 32 * j, 0);
+        }
       } else {
         const int r = (it - my_main) * kTcChunk;
-        mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + N_TOK * kTcChunk * 2);
+        mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + (LORA != kLoraPrologue ? 0 : N_TOK * kTcChunk * 2));
 #pragma unroll
         for (int a = 0; a < 4; ++a) tma_load_3d(w_tile(s, a), &map_lb, &full[s], r, a, o0);
-        tma_load_2d(x_tile(s, 0), &map_t, &full[s], r, t0);
+        if (LORA == kLoraPrologue) tma_load_2d(x_tile(s, 0), &map_t, &full[s], r, t0);
       }
     }
     *issued_count = it;
@@ -308,6 +393,18 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
             }
           }
         }
+        if (LORA == kLoraTc) {
+          // t^T partial: D[lane kTcTLane + token][rank] += x[token, k] * A[rank, k]
+          // over the chunk's four 32-element sub-tiles.  The A operand starts
+          // kTcTLane rows before the raw rows; the other rows' lanes are never read.
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk)
+              umma_f16(tmem_base + 4 * N_TOK, smem_desc_sw64(raw_tile(s, j) - kTcTLane * 64) + 2 * kk,
+                       smem_desc_sw64(la_tile(s, j)) + 2 * kk, kIdescLoraDown,
+                       (it > 0 || j > 0 || kk > 0) ? 1u : 0u);
+        }
       } else {
 #pragma unroll
         for (int kk = 0; kk < kTcChunk / 16; ++kk) {
@@ -318,10 +415,11 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
         }
       }
       umma_commit(&empty[s]);
+      if (LORA == kLoraTc && it == my_main - 1) umma_commit(t_full);
     }
     *consumed_count = it;
     umma_commit(acc_full);  // fires once every UMMA issued above has completed
-  } else if (STACK && warp >= 2) {
+  } else if (STACK && (warp == 2 || warp == 3)) {
     // ---------------- Xhat builders (warps 2-3) ----------------
     // Xhat_p row (a*N_TOK + token), 16-byte chunk c (input groups 8c..8c+7
     // of the chunk) = s(a,p) * X_{p^a}: one work item moves 8 quaternions of
@@ -331,7 +429,10 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     // an abort, so no builder can be left waiting.
     const int bt = threadIdx.x - 64;
     const T* __restrict__ x = reinterpret_cast<const T*>(prm.x);
-    for (int it = 0; it < total; ++it) {
+    bool t_seen = false;
+    // With the CUDA-core LoRA the LoRA stages belong to warps 4-5.
+    const int b_total = LORA == kLoraSimt ? my_main : total;
+    for (int it = 0; it < b_total; ++it) {
       const int s = it % S, n = it / S;
       if (it >= S && !*abort_flag && !mbar_wait(&empty[s], (n - 1) & 1)) *abort_flag = 1;
       if (it < my_main && !*abort_flag) {
@@ -369,100 +470,270 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
               st_shared_v4(addr, pl[q][0] ^ sg, pl[q][1] ^ sg, pl[q][2] ^ sg, pl[q][3] ^ sg);
             }
           }
+          if (LORA == kLoraTc) {
+            // the same 64 bytes unchanged: row tok of raw sub-tile gb
+            const uint32_t rbase = smem_u32(raw_tile(s, gb)) + tok * 64;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              st_shared_v4(rbase + ((c ^ ((tok >> 1) & 3)) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2],
+                           w[4 * c + 3]);
+          }
         }
         fence_async_smem();
+      } else if (LORA == kLoraTc && it >= my_main && !*abort_flag) {
+        // LoRA up projection operand: t = lora_scale * (this split's t^T
+        // partial), rounded once; warp 2 reads TMEM lanes 64..95 (tokens).
+        if (!t_seen) {
+          if (!mbar_wait(t_full, 0)) *abort_flag = 1;
+          tc_fence_after();
+          t_seen = true;
+        }
+        if (warp == 2) {
+          float v0[16], v1[16];
+          const uint32_t taddr = tmem_base + ((uint32_t)kTcTLane << 16) + 4 * N_TOK;
+          __syncwarp();  // tcgen05.ld is warp-collective
+          tmem_ld16(taddr, v0);
+          tmem_ld16(taddr + 16, v1);
+          tmem_ld_wait();
+          const int tok = lane;
+          if (tok < N_TOK && !*abort_flag) {
+            const uint32_t tb = smem_u32(x_tile(s, 0)) + tok * 64;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              float f[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int r = 8 * c + e;
+                f[e] = r < prm.rank ? prm.lora_scale * (r < 16 ? v0[r] : v1[r - 16]) : 0.f;
+              }
+              const uint2 lo = pack4<T>(f[0], f[1], f[2], f[3]);
+              const uint2 hi = pack4<T>(f[4], f[5], f[6], f[7]);
+              st_shared_v4(tb + ((c ^ ((tok >> 1) & 3)) << 4), lo.x, lo.y, hi.x, hi.y);
+            }
+          }
+          fence_async_smem();
+        }
       }
       builder_bar_sync();
       if (bt == 0) mbar_arrive(&full[s]);
+    }
+  } else if (LORA == kLoraSimt && warp >= 4) {
+    // ---------------- LoRA down projection (warps 4-5, CUDA cores) ----------------
+    // Warp lw owns ranks 16lw..16lw+15; lane l takes elements 8l..8l+7
+    // (+256j) of this split's slice: x from global memory (512 contiguous
+    // bytes per warp load), lora_a from the shared slice the producer loaded
+    // ahead of the weights (conflict-free 16-byte reads).  The per-lane
+    // partial dot products are summed by a transposing butterfly after which
+    // lane pair (2k, 2k+1) holds rank 16lw+k, for every token.
+    const int lt = threadIdx.x - kTcThreads;
+    const int lw = lt >> 5;
+    const int r = 16 * lw + (lane >> 1), h = lane & 1;  // rank and row parity this lane writes
+    const T* __restrict__ x = reinterpret_cast<const T*>(prm.x);
+    const int E = 4 * kTcChunk * my_main;  // elements of this split, at most 512
+    const int ebase = 4 * kTcChunk * c_begin;
+    const int lim = 4 * prm.K_g;
+    if (!prm.after_prologue) pdl_wait_prior();
+    // x pieces of this lane (each token, each 256-element piece)
+    uint4 xv[kTcLoraSimtTokens][2];
+#pragma unroll
+    for (int m = 0; m < kTcLoraSimtTokens; ++m)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int eo = 256 * j + 8 * lane, e = ebase + eo;
+        xv[m][j] = (m < m_tile && eo < E && e < lim)
+                       ? __ldg(reinterpret_cast<const uint4*>(x + (int64_t)(t0 + m) * prm.ld_x + e))
+                       : make_uint4(0u, 0u, 0u, 0u);
+      }
+    // the lora_a slice: [piece j][rank][256 elements], rows past rank zero
+    const bool a_ok = mbar_wait(t_full, 0);
+    if (!a_ok) *abort_flag = 1;
+    const uint4* slice = reinterpret_cast<const uint4*>(smem + Cfg::kSliceOffset);
+    float tacc[kTcLoraSimtTokens];
+#pragma unroll
+    for (int m = 0; m < kTcLoraSimtTokens; ++m) {
+      float vals[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) vals[k] = 0.f;
+      if (m < m_tile && a_ok) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          if (256 * j < E) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+              vals[k] += dot8<T>(slice[(j * kTcLoraInRank + 16 * lw + k) * (kTcLoraSliceBox / 8) + lane], xv[m][j]);
+          }
+        }
+      }
+      // butterfly over lane bits 4..1: keep the half of the values selected
+      // by the lane bit, add the partner's other half
+#pragma unroll
+      for (int o = 16, n = 16; o >= 2; o >>= 1, n >>= 1) {
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+          const float send = upper ? vals[i] : vals[i + n / 2];
+          const float keep = upper ? vals[i + n / 2] : vals[i];
+          vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      tacc[m] = vals[0] + __shfl_xor_sync(0xffffffffu, vals[0], 1);
+    }
+    for (int it = my_main; it < total; ++it) {
+      const int s = it % S, n = it / S;
+      if (it >= S && !*abort_flag && !mbar_wait(&empty[s], (n - 1) & 1)) *abort_flag = 1;
+      if (!*abort_flag) {
+        const uint32_t tb = smem_u32(x_tile(s, 0));
+#pragma unroll
+        for (int m = h; m < N_TOK; m += 2) {
+          float v = 0.f;
+#pragma unroll
+          for (int mm = 0; mm < kTcLoraSimtTokens; ++mm)
+            if (mm == m) v = tacc[mm];
+          const T val = from_f32<T>((m < m_tile && r < prm.rank) ? prm.lora_scale * v : 0.f);
+          const uint32_t addr = tb + m * 64 + (((r >> 3) ^ ((m >> 1) & 3)) << 4) + (r & 7) * 2;
+          asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr),
+                       "h"(*reinterpret_cast<const unsigned short*>(&val))
+                       : "memory");
+        }
+        fence_async_smem();
+      }
+      lora_bar_sync();
+      if (lt == 0) mbar_arrive(&full[s]);
     }
   }
   __syncwarp();
 
   // ---------------- epilogue ----------------
-  const bool acc_ok = mbar_wait(acc_full, 0);
-  tc_fence_after();
-  const bool ok = acc_ok && (*abort_flag == 0);
-  const int o_local = warp * 32 + lane;
-  const uint32_t lane_addr = tmem_base + ((uint32_t)(warp * 32) << 16);
-  T* __restrict__ y = reinterpret_cast<T*>(prm.y);
-  const int jn = (m_tile + 15) / 16;  // 16-token column groups holding real tokens
+  // Warps 0-3 own the 128 TMEM lanes (one output row each); the LoRA warps
+  // of the CUDA-core mode go straight to the teardown.
+  if (warp < 4) {
+    const bool acc_ok = mbar_wait(acc_full, 0);
+    tc_fence_after();
+    const bool ok = acc_ok && (*abort_flag == 0);
+    const int o_local = warp * 32 + lane;
+    const uint32_t lane_addr = tmem_base + ((uint32_t)(warp * 32) << 16);
+    T* __restrict__ y = reinterpret_cast<T*>(prm.y);
+    const int jn = (m_tile + 15) / 16;  // 16-token column groups holding real tokens
 
-  if (prm.split_k == 1) {
-    const int o = o0 + o_local;
-    float b[4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a) b[a] = to_f32(bias_raw[a]);
-#pragma unroll 1
-    for (int j = 0; j < jn; ++j) {
-      float v[4][16];
-#pragma unroll
-      for (int a = 0; a < 4; ++a) tmem_ld16(lane_addr + a * N_TOK + j * 16, v[a]);
-      tmem_ld_wait();
-      if (ok && o < prm.N_g) {
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const int m = t0 + j * 16 + t;
-          if (m < prm.M) {
-            *reinterpret_cast<uint2*>(y + (int64_t)m * prm.ld_y + 4 * o) =
-                pack4<T>(v[0][t] + b[0], v[1][t] + b[1], v[2][t] + b[2], v[3][t] + b[3]);
+    if (prm.split_k == 1) {
+      const int o = o0 + o_local;
+      float b[4];
+  #pragma unroll
+      for (int a = 0; a < 4; ++a) b[a] = to_f32(bias_raw[a]);
+  #pragma unroll 1
+      for (int j = 0; j < jn; ++j) {
+        float v[4][16];
+  #pragma unroll
+        for (int a = 0; a < 4; ++a) tmem_ld16(lane_addr + a * N_TOK + j * 16, v[a]);
+        tmem_ld_wait();
+        if (ok && o < prm.N_g) {
+  #pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const int m = t0 + j * 16 + t;
+            if (m < prm.M) {
+              *reinterpret_cast<uint2*>(y + (int64_t)m * prm.ld_y + 4 * o) =
+                  pack4<T>(v[0][t] + b[0], v[1][t] + b[1], v[2][t] + b[2], v[3][t] + b[3]);
+            }
           }
         }
       }
-    }
-  } else {
-    // K split: fp32 partials of the real tokens go to this CTA's slot of the
-    // workspace as [token][row] float4 (a = 0..3).  They are summed with the
-    // bias and rounded either by qlin_splitk_reduce_kernel or, for a few
-    // tokens, here: the last CTA of the tile to arrive (arrival counter in the
-    // workspace, reset to zero by that CTA) reads all slots in split order.
-    const size_t slot_stride = (size_t)gridDim.z * gridDim.y * (N_TOK * kTcBlockO);
-    const size_t tile_off = ((size_t)blockIdx.z * gridDim.y + blockIdx.y) * (N_TOK * kTcBlockO);
-    float4* part = prm.partials + (size_t)ks * slot_stride + tile_off;
-#pragma unroll 1
-    for (int j = 0; j < jn; ++j) {
-      float v[4][16];
-#pragma unroll
-      for (int a = 0; a < 4; ++a) tmem_ld16(lane_addr + a * N_TOK + j * 16, v[a]);
-      tmem_ld_wait();
-      if (ok) {
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const int tok = j * 16 + t;
-          if (tok < m_tile) part[tok * kTcBlockO + o_local] = make_float4(v[0][t], v[1][t], v[2][t], v[3][t]);
+    } else {
+      // K split: fp32 partials of the real tokens go to this CTA's slot of the
+      // workspace as [token][row] float4 (a = 0..3).  They are summed with the
+      // bias and rounded either by qlin_splitk_reduce_kernel or, for a few
+      // tokens, here: the last CTA of the tile to arrive (arrival counter in the
+      // workspace, reset to zero by that CTA) reads all slots in split order.
+      const size_t slot_stride = (size_t)gridDim.z * gridDim.y * (N_TOK * kTcBlockO);
+      const size_t tile_off = ((size_t)blockIdx.z * gridDim.y + blockIdx.y) * (N_TOK * kTcBlockO);
+      float4* part = prm.partials + (size_t)ks * slot_stride + tile_off;
+  #pragma unroll 1
+      for (int j = 0; j < jn; ++j) {
+        float v[4][16];
+  #pragma unroll
+        for (int a = 0; a < 4; ++a) tmem_ld16(lane_addr + a * N_TOK + j * 16, v[a]);
+        tmem_ld_wait();
+        if (ok) {
+  #pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const int tok = j * 16 + t;
+            if (tok < m_tile) part[tok * kTcBlockO + o_local] = make_float4(v[0][t], v[1][t], v[2][t], v[3][t]);
+          }
         }
       }
-    }
-    if (prm.fuse_reduce) {
-      __shared__ int s_last;
-      __threadfence();  // this thread's partials are visible device-wide
-      __syncthreads();
-      const unsigned tile_id = blockIdx.z * gridDim.y + blockIdx.y;
-      if (threadIdx.x == 0) s_last = (atomicAdd(&prm.counters[tile_id], 1u) == (unsigned)(prm.split_k - 1));
-      __syncthreads();
-      if (s_last) {
-        __threadfence();
-        const int o = o0 + o_local;
-        float b[4];
-#pragma unroll
-        for (int a = 0; a < 4; ++a) b[a] = to_f32(bias_raw_split<T>(prm, o, a));
-        for (int tok = 0; tok < m_tile; ++tok) {
-          float4 vs[kTcMaxSplit];
-#pragma unroll
-          for (int sp = 0; sp < kTcMaxSplit; ++sp)
-            vs[sp] = sp < prm.split_k ? __ldcg(prm.partials + (size_t)sp * slot_stride + tile_off +
-                                               tok * kTcBlockO + o_local)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int sp = 0; sp < kTcMaxSplit; ++sp) {
-            acc.x += vs[sp].x; acc.y += vs[sp].y; acc.z += vs[sp].z; acc.w += vs[sp].w;
-          }
-          if (ok && o < prm.N_g) {
-            *reinterpret_cast<uint2*>(y + (int64_t)(t0 + tok) * prm.ld_y + 4 * o) =
-                pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]);
-          }
+      if (prm.fuse_reduce) {
+        // Arrival: the CTA's partial stores are ordered before thread 0's
+        // release (bar.sync, then a gpu-scope acq_rel fence before the atomic);
+        // the last arriver's acquire fence orders the others' partials before
+        // its reads, which bar.sync extends to the whole CTA.
+        __shared__ int s_last;
+        epi_bar_sync();
+        const unsigned tile_id = blockIdx.z * gridDim.y + blockIdx.y;
+        if (threadIdx.x == 0) {
+          const unsigned prev = atomic_add_release_gpu(&prm.counters[tile_id], 1u);
+          const bool last = prev == (unsigned)(prm.split_k - 1);
+          if (last) fence_acq_rel_gpu();
+          s_last = last;
         }
-        if (threadIdx.x == 0) prm.counters[tile_id] = 0u;
+        epi_bar_sync();
+        if (s_last && m_tile <= 2) {
+          // One or two tokens: every thread loads its row's partials of all
+          // splits at once straight from L2, summed in split order (as the
+          // reduction kernel does).
+          const int o = o0 + o_local;
+          float b[4];
+  #pragma unroll
+          for (int a = 0; a < 4; ++a) b[a] = to_f32(bias_raw[a]);
+          for (int tok = 0; tok < m_tile; ++tok) {
+            float4 vs[kTcMaxSplit];
+  #pragma unroll
+            for (int sp = 0; sp < kTcMaxSplit; ++sp)
+              vs[sp] = sp < prm.split_k ? __ldcg(prm.partials + (size_t)sp * slot_stride + tile_off +
+                                                 tok * kTcBlockO + o_local)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  #pragma unroll
+            for (int sp = 0; sp < kTcMaxSplit; ++sp) {
+              acc.x += vs[sp].x; acc.y += vs[sp].y; acc.z += vs[sp].z; acc.w += vs[sp].w;
+            }
+            if (ok && o < prm.N_g) {
+              *reinterpret_cast<uint2*>(y + (int64_t)(t0 + tok) * prm.ld_y + 4 * o) =
+                  pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]);
+            }
+          }
+          if (threadIdx.x == 0) prm.counters[tile_id] = 0u;
+        } else if (s_last) {
+          // Three or four tokens: every split's partials of this tile
+          // ([token][row] float4, the real tokens only) are pulled into the
+          // now idle stage buffers by bulk copies completing on one barrier,
+          // one round trip for all of them, and summed in split order.
+          const uint32_t slot_bytes = (uint32_t)(m_tile * kTcBlockO * 16);
+          float4* red = reinterpret_cast<float4*>(smem);
+          bool have = ok;
+          if (threadIdx.x == 0 && ok) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");  // generic-proxy partials -> bulk copy
+            mbar_arrive_expect_tx(red_full, slot_bytes * prm.split_k);
+            for (int sp = 0; sp < prm.split_k; ++sp)
+              bulk_load(smem + sp * slot_bytes, prm.partials + (size_t)sp * slot_stride + tile_off, slot_bytes,
+                        red_full);
+          }
+          if (ok) have = mbar_wait(red_full, 0);
+          const int o = o0 + o_local;
+          float b[4];
+  #pragma unroll
+          for (int a = 0; a < 4; ++a) b[a] = to_f32(bias_raw[a]);
+          for (int tok = 0; tok < m_tile; ++tok) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int sp = 0; sp < prm.split_k; ++sp) {
+              const float4 v = red[(sp * m_tile + tok) * kTcBlockO + o_local];
+              acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+            }
+            if (have && o < prm.N_g) {
+              *reinterpret_cast<uint2*>(y + (int64_t)(t0 + tok) * prm.ld_y + 4 * o) =
+                  pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]);
+            }
+          }
+          if (threadIdx.x == 0) prm.counters[tile_id] = 0u;
+        }
       }
     }
   }
@@ -474,6 +745,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     // Let TMA loads that were issued but never consumed land before exiting.
     for (int it = *consumed_count; it < *issued_count; ++it)
       mbar_wait(&full[it % S], (it / S) & 1, 50000000ull);
+    if (LORA == kLoraSimt) mbar_wait(t_full, 0, 50000000ull);  // the lora_a slice
   }
   __syncthreads();
   if (warp == 1) {

@@ -74,7 +74,8 @@ def test_tc_path_ragged_shapes(qb, oracle, workloads, cuda, M, fin, fout, dt):
     assert rel_err(oracle, simt, want) <= REL_TOL[dt]
 
 
-@pytest.mark.parametrize("M,rank", [(1, 8), (5, 16), (16, 32), (40, 40), (130, 64), (7, 4)])
+@pytest.mark.parametrize("M,rank", [(1, 8), (5, 16), (16, 32), (20, 24), (32, 32), (1, 64), (33, 8),
+                                    (40, 40), (130, 64), (7, 4)])
 def test_tc_path_bias_and_lora(qb, oracle, workloads, cuda, M, rank):
     lay = workloads.make_layer("bf16", M, 256, 384, 100 + M, bias="normal", lora_rank=rank,
                                lora_std=0.05)
@@ -83,6 +84,26 @@ def test_tc_path_bias_and_lora(qb, oracle, workloads, cuda, M, rank):
     for algo in (ALGO_AUTO, ALGO_TC, ALGO_SIMT):
         got = run(qb, d, algo).float().cpu().numpy()
         assert rel_err(oracle, got, want) <= 1e-2, algo
+
+
+@pytest.mark.parametrize("M,rank,fin", [(1, 32, 4096), (3, 8, 2048), (4, 32, 1024), (2, 16, 160),
+                                        (4, 32, 128), (16, 24, 1024), (20, 32, 512), (32, 16, 4096),
+                                        (1, 64, 1024)])
+def test_lora_term_alone(qb, oracle, workloads, cuda, M, rank, fin):
+    # zero quaternion weights: the output is bias + LoRA only, so the down
+    # projection is checked on its own against the oracle: on the builder
+    # warps' CUDA cores (<= 4 tokens, <= 4 K chunks per split: 160 features
+    # also has a ragged last chunk), on the tensor cores (<= 32 tokens), both
+    # per K split with every split applying its own partial, or in the
+    # prologue kernel (rank 64)
+    lay = workloads.make_layer("bf16", M, fin, 512, 900 + M, bias="normal", lora_rank=rank,
+                               lora_std=0.05)
+    lay.wr, lay.wi, lay.wj, lay.wk = (np.zeros_like(w) for w in lay.weights)
+    d = to_device(lay, cuda)
+    want = oracle_rows(oracle, lay)
+    got = run(qb, d, ALGO_TC).float().cpu().numpy()
+    assert np.abs(want).max() > 0.05
+    assert rel_err(oracle, got, want) <= 1e-2
 
 
 @pytest.mark.parametrize("M", [1, 7, 33, 128])

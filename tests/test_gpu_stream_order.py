@@ -85,9 +85,11 @@ def test_weight_update_right_before_call_is_seen(qb, cuda, M):
 
 
 def test_plan_reports_the_decode_split(qb, cuda):
-    # LoRA prologue + main kernel (+ the split-K reduction kernel unless the
-    # workspace is zero-filled, as the module path's decode workspace is)
+    # main kernel (LoRA rank <= 32 computed inside it) + the split-K reduction
+    # kernel, unless the workspace is zero-filled, as the module path's decode
+    # workspace is; a rank-64 LoRA adds the prologue kernel
     plan = qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 32, flags=0)
     assert plan["algo"] == "tcgen05" and plan["tile_tokens"] == 16
-    assert plan["split_k"] > 1 and plan["launches"] == 3
-    assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 32)["launches"] == 2
+    assert plan["split_k"] > 1 and plan["launches"] == 2
+    assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 32)["launches"] == 1
+    assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 64, flags=0)["launches"] == 3
