@@ -47,8 +47,18 @@ WORKLOADS = {
     "decode_m1": dict(fn="decode_4096", M=1, bound="hbm"),
     "decode_m16": dict(fn="decode_4096", M=16, bound="hbm"),
     "prefill_m2048": dict(fn="prefill_11008", M=2048, bound="tensor"),
+    # the fp32 layer in=out=1024 at M=128 (CUDA-core fp32 path)
+    "fp32_m128": dict(fn="fp32_1024", M=128, bound="fp32"),
+    # the large layer in=5120 -> out=27648 on one GPU (the sharded sweep's N=1 points)
+    "large_m1": dict(fn="sharded_27648", M=1, bound="hbm"),
+    "large_m16": dict(fn="sharded_27648", M=16, bound="hbm"),
+    "large_m512": dict(fn="sharded_27648", M=512, bound="tensor"),
+    "large_m8192": dict(fn="sharded_27648", M=8192, bound="tensor"),
 }
 DEFAULT = "decode_m1"
+# FP32 CUDA-core peak (no measured figure exists): 148 SMs x 128 lanes x 2
+# FLOP x 1.965 GHz, nominal.
+FP32_NOMINAL_TFLOPS = 74.4
 
 
 def _pkg():
@@ -253,6 +263,65 @@ def time_device(qb, lay, torch, dev, K, W, dist=None, flags=0):
         ms = float(t.item())
     del graph
     return ms, ncopy, plan
+
+
+def time_stack(qb, wl, torch, dev, R, W):
+    """All 48 quaternion linears of one forward of the GPT-2-small-shaped
+    stack (12 blocks x qkv/proj/fc/fc2, M = 8 x 1024 tokens, bf16), captured
+    as one CUDA graph of 48 qlin_forward_ex calls and replayed R times.
+    Each layer reads its own weights and an N(0,1) activation of its input
+    width; the whole footprint (about 200 MB) exceeds L2."""
+    layers = wl.gpt2_stack()
+    lib = qb._lib.load()
+    code = qb._lib.dtype_code(torch.bfloat16)
+    M = layers[0].M
+    xs, ys = {}, {}
+    calls = []
+    flops = 0.0
+    for lay in layers:
+        fin, fout = 4 * lay.K_g, 4 * lay.N_g
+        if fin not in xs:
+            xs[fin] = torch.from_numpy(lay.x).to(dev, torch.bfloat16)
+        if fout not in ys:
+            ys[fout] = torch.empty(M, fout, dtype=torch.bfloat16, device=dev)
+        w = [torch.from_numpy(a).to(dev, torch.bfloat16) for a in lay.weights]
+        nws = qb._lib.workspace_size(torch.bfloat16, M, lay.K_g, lay.N_g, 0)
+        ws = torch.zeros(max(nws, 256), dtype=torch.uint8, device=dev)
+        calls.append((xs[fin], w, ys[fout], lay.K_g, lay.N_g, ws, nws))
+        flops += 2.0 * M * fin * fout
+    stream_of = qb._lib.stream_handle
+
+    def forward():
+        for x, w, y, K_g, N_g, ws, nws in calls:
+            st = lib.qlin_forward_ex(code, x.data_ptr(), 4 * K_g, *(a.data_ptr() for a in w), K_g,
+                                     None, None, None, 0, 0.0, y.data_ptr(), 4 * N_g, M, K_g, N_g,
+                                     ws.data_ptr(), nws, 0, qb._lib.FLAG_ZEROED_WORKSPACE, stream_of(dev))
+            if st != 0:
+                qb._lib.check(st, "qlin_forward")
+
+    for _ in range(W):
+        forward()
+    torch.cuda.synchronize(dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        forward()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        forward()
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(R):
+        graph.replay()
+    e.record()
+    torch.cuda.synchronize(dev)
+    us = s.elapsed_time(e) * 1e3 / R
+    plans = {f"{4 * k}x{4 * n}": qb._lib.plan(torch.bfloat16, M, k, n, 0)
+             for (_, _, _, k, n, _, _) in calls[:4]}
+    del graph
+    return us, flops, len(calls), plans
 
 
 def time_dense(lay, torch, dev, K, W):
@@ -486,7 +555,7 @@ def main():
                 if name == args.workload:
                     continue
                 xl = _layer(wl, name)
-                kk = K if WORKLOADS[name]["bound"] == "hbm" else max(3, min(K, 200))
+                kk = K if WORKLOADS[name]["bound"] == "hbm" else max(3, min(K, 100))
                 xms, xcopy, xplan = time_device(qb, xl, torch, dev, kk, W)
                 xus = xms * 1e3 / kk
                 xb, xf = algorithmic_work(xl)
@@ -497,11 +566,27 @@ def main():
                     a = xb / (xus * 1e-6) / 1e9
                     entry["roofline"] = {"bound": "hbm", "achieved": a, "peak": peaks["hbm_gbs"],
                                          "unit": "GB/s", "frac": a / peaks["hbm_gbs"]}
+                elif WORKLOADS[name]["bound"] == "fp32":
+                    a = xf / (xus * 1e-6) / 1e12
+                    entry["roofline"] = {"bound": "fp32 CUDA cores", "achieved": a,
+                                         "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s",
+                                         "frac": a / FP32_NOMINAL_TFLOPS, "peak_source": "nominal"}
                 else:
                     a = xf / (xus * 1e-6) / 1e12
                     entry["roofline"] = {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"],
                                          "unit": "TFLOP/s", "frac": a / peaks["bf16_tflops"]}
                 also[name] = entry
+            sus, sflops, ncalls, splans = time_stack(qb, wl, torch, dev, 20, W)
+            a = sflops / (sus * 1e-6) / 1e12
+            also["gpt2_stack"] = {
+                "us_per_forward": sus, "linears": ncalls, "replays": 20, "plans": splans,
+                "config": {"workload": "gpt2_small_stack_12x4_linears_bf16_m8192", "M": 8192,
+                           "blocks": 12, "linears": "qkv 768->2304, proj 768->768, fc 768->3072, "
+                                                    "fc2 3072->768",
+                           "inputs": "seeded synthetic N(0,1) activations, N(0,1/in) weights"},
+                "roofline": {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"],
+                             "unit": "TFLOP/s", "frac": a / peaks["bf16_tflops"]},
+            }
             result["also"] = also
     if dist is not None:
         dist.barrier()

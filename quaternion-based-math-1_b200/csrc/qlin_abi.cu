@@ -203,6 +203,17 @@ int lora_mode(int64_t M, int rank, int64_t K_g, int split) {
 // Threads of a tensor-core CTA: 128, plus two LoRA warps in the CUDA-core mode.
 constexpr int tc_block_threads(int lora) { return lora == kLoraSimt ? kTcMaxThreads : kTcThreads; }
 
+// K split the device path uses.  With the CUDA-core LoRA (at most 4
+// tokens) every split also loads LoRA B and applies its own LoRA term, a
+// fixed cost per CTA; there at most 8 splits (each streaming more weights)
+// measured faster than 16 on B200 for the 4096-wide decode layer.
+int split_for(int64_t M, int64_t K_g, int64_t N_g, int rank, int64_t sms) {
+  const int s = max_split_for(M, K_g, N_g, sms);
+  const int64_t chunks = (K_g + kTcChunk - 1) / kTcChunk;
+  if (rank > 0 && rank <= kTcLoraInRank && M <= kTcLoraSimtTokens && s > 8 && (chunks + 7) / 8 <= 4) return 8;
+  return s;
+}
+
 template <typename T, int N_TOK, int LORA>
 int ensure_tc_attrs(DeviceInfo* dev) {
   using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>, LORA>;
@@ -247,7 +258,7 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
   const int64_t o_blocks = (N_g + kTcBlockO - 1) / kTcBlockO;
   const int64_t t_blocks = (M + N_TOK - 1) / N_TOK;
   if (o_blocks > 65535 || t_blocks > 65535) return QLIN_ERR_SHAPE;
-  const int split = max_split_for(M, K_g, N_g, dev->num_sms);
+  const int split = split_for(M, K_g, N_g, base_prm.rank, dev->num_sms);
   prm.split_k = split;
   prm.partials = split > 1 ? partials : nullptr;
   if (split > 1 && !partials) return QLIN_ERR_WORKSPACE;
@@ -302,7 +313,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
   T* t = rank > 0 ? reinterpret_cast<T*>(ws + L.t_off) : nullptr;
   const int n_tok = n_tok_for(M);
   const bool stack = M <= kStackMaxTokens;
-  const int lmode = lora_mode(M, rank, K_g, max_split_for(M, K_g, N_g, dev->num_sms));
+  const int lmode = lora_mode(M, rank, K_g, split_for(M, K_g, N_g, rank, dev->num_sms));
   const bool lora_in = lmode != kLoraPrologue;
 
   // 1. prologue: component planes of x (plane mode) and the scaled LoRA down
@@ -466,7 +477,7 @@ int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void*
 
 template <typename T, int N_TOK>
 int plan_tc(DeviceInfo* dev, int64_t M, int64_t K_g, int64_t N_g, int rank, int* split, int* resident) {
-  *split = max_split_for(M, K_g, N_g, dev->num_sms);
+  *split = split_for(M, K_g, N_g, rank, dev->num_sms);
   const int li = lora_mode(M, rank, K_g, *split);
   int st = QLIN_OK;
   if constexpr (N_TOK == 16) {
