@@ -324,6 +324,138 @@ def time_stack(qb, wl, torch, dev, R, W):
     return us, flops, len(calls), plans
 
 
+def _time_ranks(torch, dev, dist, call, steps, W):
+    """Device time per call of call(i) on every rank, max over ranks: steps
+    calls captured in one CUDA graph (eager launches if capture is refused)."""
+    for i in range(W):
+        call(i)
+    torch.cuda.synchronize(dev)
+    mode = "graph"
+    graph = None
+    try:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            call(0)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(steps):
+                call(i)
+    except Exception:  # capture refused: time eager launches
+        graph = None
+        mode = "eager"
+        torch.cuda.synchronize(dev)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(steps):
+            call(i)
+    e.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([s.elapsed_time(e) * 1e3 / steps], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del graph
+    torch.cuda.synchronize(dev)
+    return float(t.item()), mode
+
+
+def time_sharded(qb, wl, torch, dev, dist, world, rank, W, Ms=(1, 16, 512, 8192)):
+    """The large layer (in=5120 -> out=27648) column-partitioned over the
+    torchrun world: rank r runs the kernel on its out/4 rows (N_g/world of
+    6912).  Two ways to assemble [M, 27648] on every rank are timed: NCCL
+    (all-gather of the [M, 4*N_g/world] outputs over NVLink, then for M > 1
+    the column-gather kernel) and fused (qlin_forward_allgather: the
+    epilogue stores into every rank's output over NVLink, then a flag
+    barrier).  Each is captured in a CUDA graph (eager launches if capture
+    is refused); device time, max over ranks.  Weight shards rotate across
+    more than L2.  The fused roofline target is the slower of the shard's
+    compute (or HBM) time and its NVLink egress at 770 GB/s."""
+    lib = qb._lib.load()
+    code = qb._lib.dtype_code(torch.bfloat16)
+    stream_of = qb._lib.stream_handle
+    peaks_ref, _ = _peaks()
+    out = {}
+    for M in Ms:
+        lay = wl.sharded_27648(M)
+        N_g, K_g = lay.N_g, lay.K_g
+        n = -(-N_g // world)
+        b0, b1 = min(rank * n, N_g), min(rank * n + n, N_g)
+        shard_bytes = 4 * n * K_g * 2
+        ncopy = max(2, min(32, math.ceil(2 * L2_BYTES / shard_bytes)))
+        shards = []
+        for _ in range(ncopy):
+            ws_ = []
+            for a in lay.weights:
+                t = torch.zeros(n, K_g, dtype=torch.bfloat16, device=dev)
+                t[:b1 - b0].copy_(torch.from_numpy(a[b0:b1]))
+                ws_.append(t)
+            shards.append(ws_)
+        x = torch.from_numpy(lay.x).to(dev, torch.bfloat16)
+        y_loc = torch.empty(M, 4 * n, dtype=torch.bfloat16, device=dev)
+        flat = torch.empty(world * M, 4 * n, dtype=torch.bfloat16, device=dev)
+        y_full = torch.empty(M, 4 * n * world, dtype=torch.bfloat16, device=dev)
+        nws = qb._lib.workspace_size(torch.bfloat16, M, K_g, n, 0)
+        wsb = torch.zeros(max(nws, 256), dtype=torch.uint8, device=dev)
+
+        def call(i):
+            w = shards[i % ncopy]
+            st = lib.qlin_forward_ex(code, x.data_ptr(), 4 * K_g, *(a.data_ptr() for a in w), K_g, None, None,
+                                     None, 0, 0.0, y_loc.data_ptr(), 4 * n, M, K_g, n, wsb.data_ptr(), nws, 0,
+                                     qb._lib.FLAG_ZEROED_WORKSPACE, stream_of(dev))
+            if st != 0:
+                qb._lib.check(st, "qlin_forward")
+            dist.all_gather_into_tensor(flat, y_loc)
+            if M > 1:
+                qb._lib.check(lib.qlin_gather_columns(code, flat.data_ptr(), y_full.data_ptr(), world, M, 4 * n,
+                                                      4 * n * world, stream_of(dev)), "qlin_gather_columns")
+
+        # the same shard computation with the all-gather fused into the
+        # epilogue: outputs stored into every rank's full output over NVLink
+        po = qb.PeerOutputs(M, 4 * n * world, torch.bfloat16, dev)
+
+        def call_fused(i):
+            w = shards[i % ncopy]
+            st = lib.qlin_forward_allgather(code, x.data_ptr(), 4 * K_g, *(a.data_ptr() for a in w), K_g, None,
+                                            None, None, 0, 0.0, M, K_g, n, wsb.data_ptr(), nws,
+                                            qb._lib.FLAG_ZEROED_WORKSPACE, world, rank, po._outs, 4 * n * world,
+                                            4 * n * rank, po._flags, po.epoch.data_ptr(), stream_of(dev))
+            if st != 0:
+                qb._lib.check(st, "qlin_forward_allgather")
+
+        steps = 200 if M <= 16 else 20
+        us, mode = _time_ranks(torch, dev, dist, call, steps, W)
+        us_f, mode_f = _time_ranks(torch, dev, dist, call_fused, steps, W)
+        same = bool(torch.equal(po.out, y_full if M > 1 else flat.view(M, -1)))
+        nbytes = 2 * (4 * n * K_g + M * 4 * K_g + M * 4 * n)
+        flops = 2.0 * M * 4 * K_g * 4 * n
+        best = min(us, us_f)
+        if M <= 16:
+            a = nbytes / (best * 1e-6) / 1e9
+            roof = {"bound": "hbm", "achieved_per_gpu": a, "unit": "GB/s", "basis": "shard bytes per GPU"}
+        else:
+            a = flops / (best * 1e-6) / 1e12
+            roof = {"bound": "tensor", "achieved_per_gpu": a, "unit": "TFLOP/s", "basis": "shard FLOP per GPU"}
+        egress = (world - 1) * M * 4 * n * 2  # bytes each rank stores to its peers
+        t_nvl = egress / 770e9 * 1e6          # at the measured 770 GB/s peer copy, per direction
+        t_cmp = (nbytes / (peaks_ref["hbm_gbs"] * 1e9) if M <= 16 else flops / (peaks_ref["bf16_tflops"] * 1e12)) * 1e6
+        out[f"m{M}"] = {"us_per_call_nccl": us, "us_per_call_fused": us_f, "steps": steps,
+                        "timing": [mode, mode_f], "shard_rows": n, "fused_equals_nccl": same,
+                        "allgather_bytes_per_rank": M * 4 * n * 2, "roofline": roof,
+                        "fused_roofline": {"target_us": max(t_nvl, t_cmp), "nvlink_us": t_nvl,
+                                           "compute_or_hbm_us": t_cmp,
+                                           "frac": max(t_nvl, t_cmp) / us_f},
+                        "plan": qb._lib.plan(torch.bfloat16, M, K_g, n, 0)}
+        del shards, x, y_loc, flat, y_full, wsb
+        torch.cuda.empty_cache()
+    return out
+
+
 def time_dense(lay, torch, dev, K, W):
     """cuBLAS x @ W^T of the same logical shape (context only)."""
     dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
@@ -589,6 +721,17 @@ def main():
             }
             result["also"] = also
     if dist is not None:
+        # the large layer column-partitioned over all ranks (out/4 rows per
+        # rank, NCCL all-gather of the outputs)
+        peak_hbm, peak_tc = peaks["hbm_gbs"], peaks["bf16_tflops"]
+        sh = time_sharded(qb, wl, torch, dev, dist, world, rank, W)
+        for v in sh.values():
+            r = v["roofline"]
+            r["frac_per_gpu"] = r["achieved_per_gpu"] / (peak_hbm if r["bound"] == "hbm" else peak_tc)
+        result["sharded_large"] = {
+            "config": {"workload": "qlinear_5120x27648_bf16_column_partitioned", "gpus": world,
+                       "parallelism": f"column{world} + NCCL all-gather"},
+            **sh}
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

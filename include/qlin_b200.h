@@ -151,6 +151,56 @@ int qlin_forward_ex(int dtype,
 int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flags, int* algo,
               int* tile_tokens, int* split_k, int* launches, int* resident_ctas);
 
+/*
+ * One rank's shard of a layer column-partitioned along out/4 over `world`
+ * GPUs of one box, fused with the all-gather of the outputs (replaces the
+ * shard-then-NCCL-all-gather path; the reference has no distributed path).
+ *
+ * This rank computes output quaternion rows [N_g] of its shard (wr..wk,
+ * bias and lora_b hold the shard's rows; x and lora_a are replicated) and
+ * its epilogue stores every output both into its own full output and, over
+ * NVLink, into every other rank's, at columns [col_offset, col_offset+4*N_g):
+ *   outs        host array [world] of device pointers, as mapped in this
+ *               process (CUDA IPC), to every rank's full output [M, ld_out]
+ *               (outs[world_rank] is this rank's own);
+ *   flag_arrays host array [world] of device pointers to every rank's
+ *               barrier flags, unsigned[world], zero before the first call;
+ *   epoch_word  this rank's call counter (device, zero before the first call).
+ * A one-warp barrier kernel follows: on return of the stream work every
+ * rank's full output holds all ranks' columns.  Every rank must make the
+ * same sequence of calls.  16-bit types, tensor-core path only; waits are
+ * bounded (QLIN_ERR_TIMEOUT via qlin_get_device_error).  The other
+ * arguments are those of qlin_forward_ex (algo is the tensor-core kernel).
+ */
+int qlin_forward_allgather(int dtype,
+                           const void* x, int64_t ld_x,
+                           const void* wr, const void* wi, const void* wj, const void* wk,
+                           int64_t ld_w,
+                           const void* bias,
+                           const void* lora_a, const void* lora_b, int rank, float lora_scale,
+                           int64_t M, int64_t K_g, int64_t N_g,
+                           void* workspace, size_t workspace_bytes, int flags,
+                           int world, int world_rank,
+                           void* const* outs, int64_t ld_out, int64_t col_offset,
+                           unsigned* const* flag_arrays, unsigned* epoch_word,
+                           void* stream);
+
+/*
+ * Buffers shared between the processes of a column-partitioned layer (no
+ * reference counterpart; plumbing of qlin_forward_allgather).
+ * qlin_ipc_alloc allocates `bytes` of zero-filled device memory on the
+ * current device with plain cudaMalloc (so that its CUDA IPC handle exists
+ * whatever allocator the host framework uses) and writes the 64-byte
+ * cudaIpcMemHandle to `handle`; qlin_ipc_free releases it.  qlin_ipc_open
+ * maps another process's buffer, given its handle and a byte offset into
+ * it, for the current device (peer access enabled lazily) and returns the
+ * address of base + offset; qlin_ipc_close takes the mapped base.
+ */
+int qlin_ipc_alloc(size_t bytes, void** out, void* handle);
+int qlin_ipc_free(void* p);
+int qlin_ipc_open(const void* handle, int64_t offset, void** out);
+int qlin_ipc_close(void* base);
+
 /* Which algorithm qlin_forward would pick for this problem (QLIN_ALGO_*). */
 int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank);
 

@@ -32,7 +32,7 @@ from .packing import (
     unpack_quaternion_to_real,
 )
 from .planar import planar_coefficient_tensor, quaternion_linear_naive, quaternion_linear_planar
-from .sharded import ColumnParallelQuaternionLinear, gather_columns, shard_bounds
+from .sharded import ColumnParallelQuaternionLinear, PeerOutputs, gather_columns, shard_bounds
 
 __all__ = [
     "QuaternionLinear",
@@ -53,6 +53,7 @@ __all__ = [
     "build_block_matrix",
     "check_divisible",
     "ColumnParallelQuaternionLinear",
+    "PeerOutputs",
     "gather_columns",
     "shard_bounds",
     "device_error",

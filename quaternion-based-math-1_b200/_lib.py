@@ -44,6 +44,11 @@ EXPORTED = (
     "qlin_get_device_error",
     "qlin_gather_columns",
     "qlin_forward_noalloc",
+    "qlin_forward_allgather",
+    "qlin_ipc_alloc",
+    "qlin_ipc_free",
+    "qlin_ipc_open",
+    "qlin_ipc_close",
 )
 
 
@@ -83,6 +88,19 @@ def load(path: str | None = None):
         lib.qlin_forward_noalloc.restype = I
         lib.qlin_gather_columns.argtypes = [I, P, P, I64, I64, I64, I64, P]
         lib.qlin_gather_columns.restype = I
+        PP = ctypes.POINTER(P)
+        lib.qlin_forward_allgather.argtypes = (
+            [I, P, I64, P, P, P, P, I64, P, P, P, I, ctypes.c_float, I64, I64, I64, P, ctypes.c_size_t, I,
+             I, I, PP, I64, I64, PP, P, P])
+        lib.qlin_forward_allgather.restype = I
+        lib.qlin_ipc_alloc.argtypes = [ctypes.c_size_t, PP, ctypes.c_char_p]
+        lib.qlin_ipc_alloc.restype = I
+        lib.qlin_ipc_free.argtypes = [P]
+        lib.qlin_ipc_free.restype = I
+        lib.qlin_ipc_open.argtypes = [ctypes.c_char_p, I64, PP]
+        lib.qlin_ipc_open.restype = I
+        lib.qlin_ipc_close.argtypes = [P]
+        lib.qlin_ipc_close.restype = I
         if path is None:
             _lib = lib
         return lib

@@ -294,7 +294,7 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
     rc.numAttrs = 1;
     e = cudaLaunchKernelEx(&rc, qlin_splitk_reduce_kernel<T>, (const float4*)partials, split,
                            (int)t_blocks, (int)o_blocks, N_TOK, static_cast<const T*>(prm.bias),
-                           static_cast<T*>(prm.y), prm.ld_y, prm.M, prm.N_g, prm.static_weights);
+                           static_cast<T*>(prm.y), prm.ld_y, prm.M, prm.N_g, prm.static_weights, prm.peers);
     if (e != cudaSuccess) return QLIN_ERR_LAUNCH;
   }
   return QLIN_OK;
@@ -304,7 +304,7 @@ template <typename T>
 int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
            const T* bias, const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y,
            int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, uint8_t* ws, int flags,
-           cudaStream_t stream) {
+           const PeerOut& peers, cudaStream_t stream) {
   if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -408,6 +408,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
   prm.lora_scale = lora_scale;
   prm.lora_a = lora_a;
   prm.ld_a = 4 * K_g;
+  prm.peers = peers;
   float4* partials = L.part_bytes ? reinterpret_cast<float4*>(ws + L.part_off) : nullptr;
   switch (n_tok) {
     case 16:
@@ -457,19 +458,22 @@ template <typename T>
 int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void* const w[4],
              int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b, int rank,
              float lora_scale, void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
-             uint8_t* ws, int flags, cudaStream_t stream) {
+             uint8_t* ws, int flags, const PeerOut& peers, cudaStream_t stream) {
   const T* xt = static_cast<const T*>(x);
   const T* bt = static_cast<const T*>(bias);
   const T* la = static_cast<const T*>(lora_a);
   const T* lb = static_cast<const T*>(lora_b);
   T* yt = static_cast<T*>(y);
+  // peer outputs (column-partitioned layer) are written by the tensor-core path only
   if constexpr (std::is_same<T, float>::value) {
+    if (peers.n > 0) return QLIN_ERR_ALIGN;
     return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
                        stream);
   } else {
     if (algo == QLIN_ALGO_TC)
       return run_tc<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
-                       flags, stream);
+                       flags, peers, stream);
+    if (peers.n > 0) return QLIN_ERR_ALIGN;
     return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
                        stream);
   }
@@ -494,6 +498,55 @@ int plan_tc(DeviceInfo* dev, int64_t M, int64_t K_g, int64_t N_g, int rank, int*
   const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
   *resident = dev->resident[di][ti][li];
   return QLIN_OK;
+}
+
+// qlin_forward_ex, with every output also stored to the peers' outputs.
+static int forward_common(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi,
+                          const void* wj, const void* wk, int64_t ld_w, const void* bias, const void* lora_a,
+                          const void* lora_b, int rank, float lora_scale, void* y, int64_t ld_y, int64_t M,
+                          int64_t K_g, int64_t N_g, void* workspace, size_t workspace_bytes, int algo, int flags,
+                          void* stream, const PeerOut& peers) {
+  int st = validate(dtype, x, ld_x, wr, wi, wj, wk, ld_w, lora_a, lora_b, rank, y, ld_y, M, K_g, N_g);
+  if (st != QLIN_OK) return st;
+  if (M == 0) return QLIN_OK;
+  if (algo < QLIN_ALGO_AUTO || algo > QLIN_ALGO_TC) return QLIN_ERR_ARG;
+  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE)) return QLIN_ERR_ARG;
+  if (rank == 0) lora_a = lora_b = nullptr;
+  DeviceInfo* dev = nullptr;
+  st = device_info(&dev);
+  if (st != QLIN_OK) return st;
+  const void* w[4] = {wr, wi, wj, wk};
+  if (algo == QLIN_ALGO_AUTO) {
+    algo = select_algo(dtype);
+    if (algo == QLIN_ALGO_TC &&
+        !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g))
+      algo = QLIN_ALGO_SIMT;
+  } else if (algo == QLIN_ALGO_TC &&
+             !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g)) {
+    return QLIN_ERR_ALIGN;
+  }
+  const WsLayout L = ws_layout(dtype, M, K_g, N_g, rank);
+  if (L.total > 0 && (!workspace || workspace_bytes < L.total || !aligned(workspace, 256)))
+    return QLIN_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaGetLastError();  // clear stale errors so the check below is this call's
+  switch (dtype) {
+    case QLIN_F32:
+      st = dispatch<float>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
+                           K_g, N_g, ws, flags, peers, s);
+      break;
+    case QLIN_BF16:
+      st = dispatch<__nv_bfloat16>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
+                                   ld_y, M, K_g, N_g, ws, flags, peers, s);
+      break;
+    default:
+      st = dispatch<__half>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
+                            K_g, N_g, ws, flags, peers, s);
+      break;
+  }
+  if (st != QLIN_OK) return st;
+  return cudaGetLastError() == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
 }
 
 }  // namespace
@@ -573,47 +626,71 @@ int qlin_forward_ex(int dtype, const void* x, int64_t ld_x, const void* wr, cons
                     const void* wk, int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b,
                     int rank, float lora_scale, void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
                     void* workspace, size_t workspace_bytes, int algo, int flags, void* stream) {
-  int st = validate(dtype, x, ld_x, wr, wi, wj, wk, ld_w, lora_a, lora_b, rank, y, ld_y, M, K_g, N_g);
-  if (st != QLIN_OK) return st;
-  if (M == 0) return QLIN_OK;
-  if (algo < QLIN_ALGO_AUTO || algo > QLIN_ALGO_TC) return QLIN_ERR_ARG;
-  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE)) return QLIN_ERR_ARG;
-  if (rank == 0) lora_a = lora_b = nullptr;
-  DeviceInfo* dev = nullptr;
-  st = device_info(&dev);
-  if (st != QLIN_OK) return st;
-  const void* w[4] = {wr, wi, wj, wk};
-  if (algo == QLIN_ALGO_AUTO) {
-    algo = select_algo(dtype);
-    if (algo == QLIN_ALGO_TC &&
-        !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g))
-      algo = QLIN_ALGO_SIMT;
-  } else if (algo == QLIN_ALGO_TC &&
-             !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g)) {
-    return QLIN_ERR_ALIGN;
-  }
-  const WsLayout L = ws_layout(dtype, M, K_g, N_g, rank);
-  if (L.total > 0 && (!workspace || workspace_bytes < L.total || !aligned(workspace, 256)))
-    return QLIN_ERR_WORKSPACE;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  cudaGetLastError();  // clear stale errors so the check below is this call's
-  switch (dtype) {
-    case QLIN_F32:
-      st = dispatch<float>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
-                           K_g, N_g, ws, flags, s);
-      break;
-    case QLIN_BF16:
-      st = dispatch<__nv_bfloat16>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
-                                   ld_y, M, K_g, N_g, ws, flags, s);
-      break;
-    default:
-      st = dispatch<__half>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
-                            K_g, N_g, ws, flags, s);
-      break;
-  }
-  if (st != QLIN_OK) return st;
+  PeerOut none;
+  none.n = 0;
+  return forward_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y,
+                        M, K_g, N_g, workspace, workspace_bytes, algo, flags, stream, none);
+}
+
+int qlin_forward_allgather(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi,
+                           const void* wj, const void* wk, int64_t ld_w, const void* bias, const void* lora_a,
+                           const void* lora_b, int rank, float lora_scale, int64_t M, int64_t K_g, int64_t N_g,
+                           void* workspace, size_t workspace_bytes, int flags, int world, int world_rank,
+                           void* const* outs, int64_t ld_out, int64_t col_offset, unsigned* const* flag_arrays,
+                           unsigned* epoch_word, void* stream) {
+  if (dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
+  if (world < 1 || world > kMaxPeers + 1 || world_rank < 0 || world_rank >= world) return QLIN_ERR_ARG;
+  if (!outs || (world > 1 && (!flag_arrays || !epoch_word))) return QLIN_ERR_ARG;
+  for (int q = 0; q < world; ++q)
+    if (!outs[q] || (world > 1 && !flag_arrays[q])) return QLIN_ERR_ARG;
+  if (col_offset < 0 || col_offset % 4 != 0 || ld_out < col_offset + 4 * N_g) return QLIN_ERR_SHAPE;
+  PeerOut peers;
+  peers.n = 0;
+  for (int q = 0; q < world; ++q)
+    if (q != world_rank) peers.y[peers.n++] = static_cast<uint8_t*>(outs[q]) + col_offset * 2;
+  void* y = static_cast<uint8_t*>(outs[world_rank]) + col_offset * 2;
+  int st = forward_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
+                          ld_out, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_TC, flags, stream, peers);
+  if (st != QLIN_OK || M == 0 || world == 1) return st;
+  PeerFlags pf;
+  for (int q = 0; q < world; ++q) pf.f[q] = flag_arrays[q];
+  qlin_peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(pf, epoch_word, world_rank, world);
   return cudaGetLastError() == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+}
+
+int qlin_ipc_alloc(size_t bytes, void** out, void* handle) {
+  if (!out || !handle || bytes == 0) return QLIN_ERR_ARG;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return QLIN_ERR_LAUNCH;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return QLIN_ERR_LAUNCH;
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *out = p;
+  return QLIN_OK;
+}
+
+int qlin_ipc_free(void* p) {
+  if (!p) return QLIN_ERR_ARG;
+  return cudaFree(p) == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+}
+
+int qlin_ipc_open(const void* handle, int64_t offset, void** out) {
+  if (!handle || !out || offset < 0) return QLIN_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess || !base)
+    return QLIN_ERR_LAUNCH;
+  *out = static_cast<uint8_t*>(base) + offset;
+  return QLIN_OK;
+}
+
+int qlin_ipc_close(void* base) {
+  if (!base) return QLIN_ERR_ARG;
+  return cudaIpcCloseMemHandle(base) == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
 }
 
 int qlin_forward(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi, const void* wj,

@@ -29,6 +29,27 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
 // Four fp32 values -> four 16-bit values packed in 8 bytes (round to nearest even).
+// Output rows of the column-partitioned layer's other ranks: the same
+// [M, ld] layout, already offset to this rank's columns (peer memory mapped
+// through CUDA IPC; plain stores over NVLink, no multicast).
+constexpr int kMaxPeers = 7;
+struct PeerOut {
+  void* y[kMaxPeers];
+  int n;
+};
+
+// Stores four 16-bit outputs (8 bytes) at element offset off of y and of
+// every peer's output.
+template <typename T>
+__device__ __forceinline__ void store_out(T* y, const PeerOut& peers, int64_t off, uint2 v) {
+  *reinterpret_cast<uint2*>(y + off) = v;
+  for (int p = 0; p < peers.n; ++p) *reinterpret_cast<uint2*>(reinterpret_cast<T*>(peers.y[p]) + off) = v;
+}
+
+// Orders this thread's earlier stores (peer memory included) before any
+// later signal at system scope.
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 // Dot product of two vectors of eight 16-bit elements (16 bytes each), fp32.
 template <typename T>
 __device__ __forceinline__ float dot8(uint4 a, uint4 b) {

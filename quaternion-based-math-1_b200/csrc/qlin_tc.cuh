@@ -143,6 +143,7 @@ struct TcParams {
   float lora_scale;    // in-kernel LoRA: t = lora_scale * x A^T
   const void* lora_a;  // CUDA-core in-kernel LoRA: A [rank, ld_a]
   int64_t ld_a;
+  PeerOut peers;       // column-partitioned layer: every output also stored to these
 };
 
 __device__ __forceinline__ void builder_bar_sync() {
@@ -631,8 +632,8 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
           for (int t = 0; t < 16; ++t) {
             const int m = t0 + j * 16 + t;
             if (m < prm.M) {
-              *reinterpret_cast<uint2*>(y + (int64_t)m * prm.ld_y + 4 * o) =
-                  pack4<T>(v[0][t] + b[0], v[1][t] + b[1], v[2][t] + b[2], v[3][t] + b[3]);
+              store_out<T>(y, prm.peers, (int64_t)m * prm.ld_y + 4 * o,
+                           pack4<T>(v[0][t] + b[0], v[1][t] + b[1], v[2][t] + b[2], v[3][t] + b[3]));
             }
           }
         }
@@ -696,8 +697,8 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
               acc.x += vs[sp].x; acc.y += vs[sp].y; acc.z += vs[sp].z; acc.w += vs[sp].w;
             }
             if (ok && o < prm.N_g) {
-              *reinterpret_cast<uint2*>(y + (int64_t)(t0 + tok) * prm.ld_y + 4 * o) =
-                  pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]);
+              store_out<T>(y, prm.peers, (int64_t)(t0 + tok) * prm.ld_y + 4 * o,
+                           pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
             }
           }
           if (threadIdx.x == 0) prm.counters[tile_id] = 0u;
@@ -728,8 +729,8 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
               acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
             }
             if (have && o < prm.N_g) {
-              *reinterpret_cast<uint2*>(y + (int64_t)(t0 + tok) * prm.ld_y + 4 * o) =
-                  pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]);
+              store_out<T>(y, prm.peers, (int64_t)(t0 + tok) * prm.ld_y + 4 * o,
+                           pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
             }
           }
           if (threadIdx.x == 0) prm.counters[tile_id] = 0u;
@@ -737,6 +738,10 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
       }
     }
   }
+
+  // Outputs stored to peers are performed at system scope before the CTA
+  // ends, so the barrier kernel that follows may signal them.
+  if (prm.peers.n > 0) fence_sys();
 
   // ---------------- teardown ----------------
   tc_fence_before();
@@ -762,7 +767,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 qlin_splitk_reduce_kernel(const float4* __restrict__ partials, int split, int t_blocks, int o_blocks,
                           int n_tok, const T* __restrict__ bias, T* __restrict__ y, int64_t ld_y, int M,
-                          int N_g, int static_weights) {
+                          int N_g, int static_weights, const PeerOut peers) {
   pdl_launch_dependents();
   const int64_t per_slot = (int64_t)t_blocks * o_blocks * n_tok * kTcBlockO;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -801,8 +806,8 @@ qlin_splitk_reduce_kernel(const float4* __restrict__ partials, int split, int t_
   float b[4];
 #pragma unroll
   for (int a = 0; a < 4; ++a) b[a] = to_f32(braw[a]);
-  *reinterpret_cast<uint2*>(y + (int64_t)m * ld_y + 4 * o) =
-      pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]);
+  store_out<T>(y, peers, (int64_t)m * ld_y + 4 * o, pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
+  if (peers.n > 0) fence_sys();
 }
 
 }  // namespace qlin

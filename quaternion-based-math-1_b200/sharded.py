@@ -14,9 +14,17 @@ large layers.
 Works with any backend whose all-gather accepts the tensors' device (NCCL for
 CUDA tensors).  The shard arithmetic itself is device-free and is tested on
 CPU with gloo ranks.
+
+With ``fused_allgather=True`` (bf16/f16, one process per GPU of one box) the
+all-gather is fused into the kernel instead: every rank's full output is
+mapped into every other rank (CUDA IPC, exchanged once per output shape),
+each rank's epilogue stores its columns into all of them over NVLink, and a
+bounded cross-rank flag barrier ends the call (``qlin_forward_allgather``).
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -26,7 +34,7 @@ from . import _lib
 from .linear import QuaternionLinear, fused_quaternion_linear
 from .packing import check_divisible
 
-__all__ = ["shard_bounds", "ColumnParallelQuaternionLinear", "gather_columns"]
+__all__ = ["shard_bounds", "ColumnParallelQuaternionLinear", "gather_columns", "PeerOutputs"]
 
 
 def shard_bounds(out_groups: int, world: int, rank: int) -> tuple[int, int, int]:
@@ -56,13 +64,101 @@ def gather_columns(shards: torch.Tensor, M: int, n_cols: int, out: torch.Tensor 
     return out
 
 
+class PeerOutputs:
+    """Every rank's full ``[M, cols]`` output, mapped into this process.
+
+    Built collectively (every rank of ``group`` constructs it with the same
+    shape): each rank allocates its output and its barrier flags ``[world]``
+    plus call counter with ``qlin_ipc_alloc`` (plain cudaMalloc, zero-filled),
+    the CUDA IPC handles are exchanged with ``all_gather_object``, and the
+    peers' buffers are mapped with this rank's GPU current (``qlin_ipc_open``:
+    plain peer mappings, no multicast objects).  The buffers must outlive
+    every use by the peers: instances live for the process's life unless
+    ``close`` is called on every rank after a final barrier.
+    """
+
+    def __init__(self, M: int, cols: int, dtype, device, group=None):
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        lib = _lib.load()
+        elem = torch.empty((), dtype=dtype).element_size()
+        self._owned = []   # this rank's allocations (qlin_ipc_alloc)
+        self._mapped = []  # peers' mapped bases (qlin_ipc_open)
+        with torch.cuda.device(self.device):
+            out_ptr, out_h = self._alloc(lib, M * cols * elem)
+            flag_ptr, flag_h = self._alloc(lib, 4 * (self.world + 1))  # flags[world] + call counter
+        self.out = _device_view(out_ptr, (M, cols), dtype, self.device, self)
+        self.flags = _device_view(flag_ptr, (self.world,), torch.int32, self.device, self)
+        self.epoch = _device_view(flag_ptr + 4 * self.world, (1,), torch.int32, self.device, self)
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, (out_h, flag_h), group=group)
+        outs, flags = [], []
+        with torch.cuda.device(self.device):
+            for q, (oh, fh) in enumerate(everyone):
+                if q == self.rank:
+                    outs.append(out_ptr)
+                    flags.append(flag_ptr)
+                    continue
+                outs.append(self._open(lib, oh))
+                flags.append(self._open(lib, fh))
+        P = ctypes.c_void_p
+        self._outs = (P * self.world)(*outs)
+        self._flags = (P * self.world)(*flags)
+
+    def _alloc(self, lib, nbytes):
+        p = ctypes.c_void_p()
+        h = ctypes.create_string_buffer(64)
+        _lib.check(lib.qlin_ipc_alloc(nbytes, ctypes.byref(p), h), "qlin_ipc_alloc")
+        self._owned.append(p.value)
+        return p.value, h.raw
+
+    def _open(self, lib, handle):
+        p = ctypes.c_void_p()
+        _lib.check(lib.qlin_ipc_open(handle, 0, ctypes.byref(p)), "qlin_ipc_open")
+        self._mapped.append(p.value)
+        return p.value
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (after every rank is done with them)."""
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            for b in self._mapped:
+                lib.qlin_ipc_close(b)
+            for p in self._owned:
+                lib.qlin_ipc_free(p)
+        self._mapped, self._owned = [], []
+
+
+class _CudaArray:
+    """__cuda_array_interface__ of a raw device buffer (zero-copy torch view)."""
+
+    def __init__(self, ptr, shape, typestr, owner):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+        self.owner = owner
+
+
+_TYPESTR = {torch.bfloat16: "<V2", torch.float16: "<f2", torch.int32: "<i4"}
+
+
+def _device_view(ptr, shape, dtype, device, owner):
+    if dtype == torch.bfloat16:  # no bf16 typestr: view int16 storage as bf16
+        t = torch.as_tensor(_CudaArray(ptr, shape, "<i2", owner), device=device)
+        return t.view(torch.bfloat16)
+    return torch.as_tensor(_CudaArray(ptr, shape, _TYPESTR[dtype], owner), device=device)
+
+
 class ColumnParallelQuaternionLinear(nn.Module):
     """One rank's shard of a ``QuaternionLinear`` partitioned along out/4."""
 
     def __init__(self, in_features: int, out_features: int, bias: bool = False,
                  process_group=None, device=None, dtype=None, world_size: int | None = None,
-                 rank: int | None = None):
+                 rank: int | None = None, fused_allgather: bool = False):
         super().__init__()
+        self.fused_allgather = fused_allgather
+        self._peer_outputs: dict[int, PeerOutputs] = {}
         self.in_features = in_features
         self.out_features = out_features
         self.in_groups = check_divisible(in_features, "in_features")
@@ -113,8 +209,42 @@ class ColumnParallelQuaternionLinear(nn.Module):
         return fused_quaternion_linear(x, self.wr, self.wi, self.wj, self.wk, self.bias,
                                        self.lora_A, self.lora_B, self.lora_scale)
 
+    def _fused_forward(self, x: torch.Tensor) -> torch.Tensor:
+        """Shard GEMM with the all-gather fused into its epilogue (see module doc)."""
+        x2 = x.reshape(-1, self.in_features).contiguous()
+        M = x2.shape[0]
+        G = self.world_size
+        cols = 4 * self.shard * G
+        po = self._peer_outputs.get(M)
+        if po is None:
+            po = self._peer_outputs[M] = PeerOutputs(M, cols, x2.dtype, x2.device, self.process_group)
+        la, lb = self.lora_A, self.lora_B
+        rank_l = 0 if la is None else la.shape[0]
+        if rank_l % 8:
+            # the tensor-core path takes ranks in multiples of 8: zero-pad
+            pad = 8 - rank_l % 8
+            la = torch.cat((la, la.new_zeros(pad, la.shape[1])), 0)
+            lb = torch.cat((lb, lb.new_zeros(lb.shape[0], pad)), 1).contiguous()
+            rank_l += pad
+        K_g, n = self.in_groups, self.shard
+        ws_bytes = _lib.workspace_size(x2.dtype, M, K_g, n, rank_l)
+        ws = _lib.zeroed_workspace(x2.device, ws_bytes) if ws_bytes else None
+        flags = _lib.FLAG_ZEROED_WORKSPACE if ws is not None else 0
+        ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        with torch.cuda.device(x2.device):
+            code = _lib.load().qlin_forward_allgather(
+                _lib.dtype_code(x2.dtype), x2.data_ptr(), self.in_features,
+                self.wr.data_ptr(), self.wi.data_ptr(), self.wj.data_ptr(), self.wk.data_ptr(), K_g,
+                ptr(self.bias), ptr(la), ptr(lb), rank_l, float(self.lora_scale),
+                M, K_g, n, ptr(ws), ws_bytes, flags, G, self.rank, po._outs, cols, 4 * n * self.rank,
+                po._flags, po.epoch.data_ptr(), _lib.stream_handle(x2.device))
+        _lib.check(code, "qlin_forward_allgather")
+        return po.out[:, :self.out_features].clone()
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         lead = x.shape[:-1]
+        if self.fused_allgather and self.world_size > 1:
+            return self._fused_forward(x).reshape(*lead, self.out_features)
         y_local = self.local_forward(x).reshape(-1, 4 * self.shard)
         M = y_local.shape[0]
         G = self.world_size
