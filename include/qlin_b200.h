@@ -221,10 +221,13 @@ int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank);
  *  - The first call on a device looks up the buffer's device address
  *    (cudaGetSymbolAddress) with that device current; make that first call
  *    before any stream capture.
- *  - All calls on a device share the one buffer and it keeps the last call's
- *    contents (nothing in it needs to start at zero).  Calls that overlap on
- *    the GPU -- on different streams, or from different threads -- race on
- *    it; serialise them (one stream, or events between streams).
+ *  - All calls on a device share the one buffer.  It starts zero-filled and
+ *    only this entry point uses it, so calls run as with
+ *    QLIN_FLAG_ZEROED_WORKSPACE (decode-sized K splits summed inside the
+ *    main kernel; its counter bytes are back at zero after every call).
+ *    Calls that overlap on the GPU -- on different streams, or from
+ *    different threads -- race on it; serialise them (one stream, or events
+ *    between streams).
  * Nothing is allocated: no cudaMalloc, no cudaFree, no allocating library call.
  */
 #define QLIN_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
