@@ -622,6 +622,9 @@ def main():
         import torch.distributed as tdist
 
         torch.cuda.set_device(local)
+        # keep stdout to the one JSON line: NCCL's version banner only when asked for
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                  device_id=torch.device("cuda", local))
         dist = tdist

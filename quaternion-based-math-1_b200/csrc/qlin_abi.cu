@@ -30,8 +30,8 @@ struct DeviceInfo {
   int cc_major = 0, cc_minor = 0, num_sms = 0;
   // per (element type, N_TOK, in-kernel LoRA) kernel instance: attributes
   // set, and how many CTAs of it the device keeps resident at once
-  bool tc_attr_set[2][4][3] = {};
-  int resident[2][4][3] = {};
+  bool tc_attr_set[2][4][3][2] = {};
+  int resident[2][4][3][2] = {};
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mutex;
@@ -214,15 +214,15 @@ int split_for(int64_t M, int64_t K_g, int64_t N_g, int rank, int64_t sms) {
   return s;
 }
 
-template <typename T, int N_TOK, int LORA>
+template <typename T, int N_TOK, int LORA, bool PEERS = false>
 int ensure_tc_attrs(DeviceInfo* dev) {
   using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>, LORA>;
-  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA>;
+  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA, PEERS>;
   const int ti = n_tok_index(N_TOK);
   const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
-  const int li = LORA;
+  const int li = LORA, pi = PEERS ? 1 : 0;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (dev->tc_attr_set[di][ti][li]) return QLIN_OK;
+  if (dev->tc_attr_set[di][ti][li][pi]) return QLIN_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
       cudaSuccess)
     return QLIN_ERR_LAUNCH;
@@ -242,8 +242,8 @@ int ensure_tc_attrs(DeviceInfo* dev) {
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, tc_block_threads(LORA), Cfg::kSmemBytes) !=
       cudaSuccess)
     return QLIN_ERR_LAUNCH;
-  dev->resident[di][ti][li] = per_sm * dev->num_sms;
-  dev->tc_attr_set[di][ti][li] = true;
+  dev->resident[di][ti][li][pi] = per_sm * dev->num_sms;
+  dev->tc_attr_set[di][ti][li][pi] = true;
   return QLIN_OK;
 }
 
@@ -251,8 +251,11 @@ template <typename T, int N_TOK, int LORA>
 int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& base_prm, int64_t M,
                    int64_t K_g, int64_t N_g, float4* partials, cudaStream_t stream) {
   using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>, LORA>;
-  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA>;
-  int st = ensure_tc_attrs<T, N_TOK, LORA>(dev);
+  // outputs also stored to peers only in the column-partitioned path's build
+  const bool peers = base_prm.peers.n > 0;
+  auto kernel = peers ? qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA, true>
+                      : qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA, false>;
+  int st = peers ? ensure_tc_attrs<T, N_TOK, LORA, true>(dev) : ensure_tc_attrs<T, N_TOK, LORA, false>(dev);
   if (st != QLIN_OK) return st;
   TcParams prm = base_prm;
   const int64_t o_blocks = (N_g + kTcBlockO - 1) / kTcBlockO;
@@ -496,7 +499,7 @@ int plan_tc(DeviceInfo* dev, int64_t M, int64_t K_g, int64_t N_g, int rank, int*
   if (st != QLIN_OK) return st;
   const int ti = n_tok_index(N_TOK);
   const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
-  *resident = dev->resident[di][ti][li];
+  *resident = dev->resident[di][ti][li][0];
   return QLIN_OK;
 }
 

@@ -38,12 +38,15 @@ struct PeerOut {
   int n;
 };
 
-// Stores four 16-bit outputs (8 bytes) at element offset off of y and of
-// every peer's output.
-template <typename T>
+// Stores four 16-bit outputs (8 bytes) at element offset off of y and, for
+// kernels built with peer outputs, of every peer's output (a compile-time
+// choice: the runtime loop alone cost 8% of a prefill call).
+template <typename T, bool PEERS>
 __device__ __forceinline__ void store_out(T* y, const PeerOut& peers, int64_t off, uint2 v) {
   *reinterpret_cast<uint2*>(y + off) = v;
-  for (int p = 0; p < peers.n; ++p) *reinterpret_cast<uint2*>(reinterpret_cast<T*>(peers.y[p]) + off) = v;
+  if constexpr (PEERS) {
+    for (int p = 0; p < peers.n; ++p) *reinterpret_cast<uint2*>(reinterpret_cast<T*>(peers.y[p]) + off) = v;
+  }
 }
 
 // Orders this thread's earlier stores (peer memory included) before any

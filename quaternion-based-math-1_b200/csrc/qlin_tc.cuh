@@ -173,7 +173,7 @@ __device__ __forceinline__ unsigned atomic_add_release_gpu(unsigned* p, unsigned
   return old;
 }
 
-template <typename T, int N_TOK, bool STACK, int LORA>
+template <typename T, int N_TOK, bool STACK, int LORA, bool PEERS>
 __global__ void __launch_bounds__(kTcMaxThreads, 1)
 qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant__ CUtensorMap map_wi,
                const __grid_constant__ CUtensorMap map_wj, const __grid_constant__ CUtensorMap map_wk,
@@ -632,7 +632,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
           for (int t = 0; t < 16; ++t) {
             const int m = t0 + j * 16 + t;
             if (m < prm.M) {
-              store_out<T>(y, prm.peers, (int64_t)m * prm.ld_y + 4 * o,
+              store_out<T, PEERS>(y, prm.peers, (int64_t)m * prm.ld_y + 4 * o,
                            pack4<T>(v[0][t] + b[0], v[1][t] + b[1], v[2][t] + b[2], v[3][t] + b[3]));
             }
           }
@@ -697,7 +697,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
               acc.x += vs[sp].x; acc.y += vs[sp].y; acc.z += vs[sp].z; acc.w += vs[sp].w;
             }
             if (ok && o < prm.N_g) {
-              store_out<T>(y, prm.peers, (int64_t)(t0 + tok) * prm.ld_y + 4 * o,
+              store_out<T, PEERS>(y, prm.peers, (int64_t)(t0 + tok) * prm.ld_y + 4 * o,
                            pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
             }
           }
@@ -729,7 +729,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
               acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
             }
             if (have && o < prm.N_g) {
-              store_out<T>(y, prm.peers, (int64_t)(t0 + tok) * prm.ld_y + 4 * o,
+              store_out<T, PEERS>(y, prm.peers, (int64_t)(t0 + tok) * prm.ld_y + 4 * o,
                            pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
             }
           }
@@ -741,7 +741,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
 
   // Outputs stored to peers are performed at system scope before the CTA
   // ends, so the barrier kernel that follows may signal them.
-  if (prm.peers.n > 0) fence_sys();
+  if (PEERS) fence_sys();
 
   // ---------------- teardown ----------------
   tc_fence_before();
@@ -806,7 +806,8 @@ qlin_splitk_reduce_kernel(const float4* __restrict__ partials, int split, int t_
   float b[4];
 #pragma unroll
   for (int a = 0; a < 4; ++a) b[a] = to_f32(braw[a]);
-  store_out<T>(y, peers, (int64_t)m * ld_y + 4 * o, pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
+  store_out<T, true>(y, peers, (int64_t)m * ld_y + 4 * o,
+                     pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
   if (peers.n > 0) fence_sys();
 }
 
