@@ -86,6 +86,21 @@ def _peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
+def _traffic(workload):
+    """DRAM bytes per launch of the workload's main kernel from the ncu
+    summary table in profiles/ (None when no capture is recorded)."""
+    path = os.path.join(REPO, "profiles", "dram_traffic_per_launch.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                cells = [c.strip() for c in line.strip().strip("|").split("|")]
+                if len(cells) >= 4 and cells[0] == workload and cells[2].isdigit():
+                    return int(cells[2]), f"profiles/{cells[3]}"
+    except OSError:
+        pass
+    return None, None
+
+
 def _layer(wl, name):
     spec = WORKLOADS[name]
     return getattr(wl, spec["fn"])(spec["M"])
@@ -641,15 +656,18 @@ def main():
     bound = WORKLOADS[args.workload]["bound"]
     if bound == "hbm":
         achieved = nbytes / (us_call * 1e-6) / 1e9
+        traffic, tsrc = _traffic(args.workload)
         roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic, "traffic_source": tsrc,
                 "basis": f"{nbytes} algorithmic bytes per call / device time per call "
                          f"({launches} launches per call)",
                 "peak_source": peak_src}
     else:
         achieved = flops / (us_call * 1e-6) / 1e12
+        traffic, tsrc = _traffic(args.workload)
         roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,
+                "traffic_source": tsrc,
                 "basis": f"{flops:.4g} dense-equivalent FLOP per call / device time per call",
                 "peak_source": peak_src}
 
