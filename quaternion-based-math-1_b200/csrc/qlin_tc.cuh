@@ -182,6 +182,11 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
                const TcParams prm) {
   using Cfg = TcCfg<N_TOK, STACK, LORA>;
   constexpr int S = Cfg::kStages;
+  // Activation operands built in shared memory by the builder warps
+  // (stacked tiles) or TMA-loaded from the prologue's planar copy of x
+  // (plane tiles; building those in the kernel measured 1.5x slower for
+  // 128-token tiles: two builder warps cannot feed the tensor cores).
+  constexpr bool kBuilt = STACK;
   constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   constexpr uint32_t kIdescPos = make_idesc_f16(128, N_TOK, kFmt, false);
   constexpr uint32_t kIdescNeg = make_idesc_f16(128, N_TOK, kFmt, true);
@@ -252,7 +257,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     for (int it = 0; it < pre; ++it) {
       if (it < my_main) {
         const int k = (c_begin + it) * kTcChunk;
-        mbar_arrive_expect_tx(&full[it], 4 * kTcWTileBytes + (STACK ? 0 : 4 * Cfg::kXTileBytes) +
+        mbar_arrive_expect_tx(&full[it], 4 * kTcWTileBytes + (kBuilt ? 0 : 4 * Cfg::kXTileBytes) +
                                              Cfg::kLoraABytes);
 #pragma unroll
         for (int p = 0; p < 4; ++p) tma_load_2d(w_tile(it, p), wmap[p], &full[it], k, o0);
@@ -284,7 +289,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   // previous kernel of the stream.
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], STACK ? 2 : 1);  // producer (+ builders)
+      mbar_init(&full[s], kBuilt ? 2 : 1);  // producer (+ builders)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -298,7 +303,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     tma_prefetch_desc(&map_wi);
     tma_prefetch_desc(&map_wj);
     tma_prefetch_desc(&map_wk);
-    if (!STACK) tma_prefetch_desc(&map_x);
+    if (!kBuilt) tma_prefetch_desc(&map_x);
     if (LORA != kLoraPrologue) tma_prefetch_desc(&map_la);
     // With static weights the caller guarantees that no earlier work on the
     // stream writes the weights, bias or LoRA B, so their first tiles are
@@ -324,10 +329,10 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   if (threadIdx.x == 0) {
     // ---------------- TMA producer ----------------
     if (!early) issue_pre_weights();
-    if (prm.after_prologue && (!STACK || my_lora > 0)) pdl_wait_prior();  // x planes / LoRA t
+    if (prm.after_prologue && (!kBuilt || my_lora > 0)) pdl_wait_prior();  // x planes / LoRA t
     for (int it = 0; it < pre; ++it) {
       if (it < my_main) {
-        if (!STACK) {
+        if (!kBuilt) {
           const int k = (c_begin + it) * kTcChunk;
 #pragma unroll
           for (int q = 0; q < 4; ++q) tma_load_3d(x_tile(it, q), &map_x, &full[it], k, t0, q);
@@ -346,11 +351,11 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
       if (*abort_flag) break;
       if (it < my_main) {
         const int k = (c_begin + it) * kTcChunk;
-        mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + (STACK ? 0 : 4 * Cfg::kXTileBytes) +
+        mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + (kBuilt ? 0 : 4 * Cfg::kXTileBytes) +
                                             Cfg::kLoraABytes);
 #pragma unroll
         for (int p = 0; p < 4; ++p) tma_load_2d(w_tile(s, p), wmap[p], &full[s], k, o0);
-        if (!STACK) {
+        if (!kBuilt) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) tma_load_3d(x_tile(s, q), &map_x, &full[s], k, t0, q);
         }
@@ -420,7 +425,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     }
     *consumed_count = it;
     umma_commit(acc_full);  // fires once every UMMA issued above has completed
-  } else if (STACK && (warp == 2 || warp == 3)) {
+  } else if (kBuilt && (warp == 2 || warp == 3)) {
     // ---------------- Xhat builders (warps 2-3) ----------------
     // Xhat_p row (a*N_TOK + token), 16-byte chunk c (input groups 8c..8c+7
     // of the chunk) = s(a,p) * X_{p^a}: one work item moves 8 quaternions of
@@ -438,46 +443,59 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
       if (it >= S && !*abort_flag && !mbar_wait(&empty[s], (n - 1) & 1)) *abort_flag = 1;
       if (it < my_main && !*abort_flag) {
         const int g0 = (c_begin + it) * kTcChunk;
-        for (int item = bt; item < N_TOK * 4; item += 64) {
-          const int tok = item >> 2, gb = item & 3;
-          const int m = t0 + tok, gbase = g0 + 8 * gb;
-          uint32_t w[16];
+        // N_TOK*4 items of 64 bytes per stage, 64 builders: kItems each, in
+        // batches of up to 4 whose loads are all issued before any is used
+        // (one L2 round trip per batch, not per item).
+        constexpr int kItems = N_TOK * 4 / 64;
+        constexpr int kBatch = kItems < 4 ? kItems : 4;
+#pragma unroll 1
+        for (int b0 = 0; b0 < kItems; b0 += kBatch) {
+          uint4 ld[kBatch][4];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) w[j] = 0u;
-          if (m < prm.M && gbase < prm.K_g) {
-            const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)m * prm.ld_x + 4 * gbase);
+          for (int k = 0; k < kBatch; ++k) {
+            const int item = bt + 64 * (b0 + k);
+            const int m = t0 + (item >> 2), gbase = g0 + 8 * (item & 3);
+            const bool live = m < prm.M && gbase < prm.K_g;
+            const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(live ? m : 0) * prm.ld_x + 4 * (live ? gbase : 0));
+#pragma unroll
+            for (int c = 0; c < 4; ++c) ld[k][c] = live ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
+          }
+#pragma unroll
+          for (int k = 0; k < kBatch; ++k) {
+            const int item = bt + 64 * (b0 + k);
+            const int tok = item >> 2, gb = item & 3;
+            uint32_t w[16];
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-              const uint4 v = __ldg(src + c);
-              w[4 * c + 0] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+              w[4 * c + 0] = ld[k][c].x; w[4 * c + 1] = ld[k][c].y; w[4 * c + 2] = ld[k][c].z; w[4 * c + 3] = ld[k][c].w;
             }
-          }
-          // plane q of the 8 quaternions: word j = (X_q[2j], X_q[2j+1])
-          uint32_t pl[4][4];
+            // plane q of the 8 quaternions: word j = (X_q[2j], X_q[2j+1])
+            uint32_t pl[4][4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
+            for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              pl[q][j] = __byte_perm(w[4 * j + (q >> 1)], w[4 * j + 2 + (q >> 1)], (q & 1) ? 0x7632 : 0x5410);
+              for (int j = 0; j < 4; ++j)
+                pl[q][j] = __byte_perm(w[4 * j + (q >> 1)], w[4 * j + 2 + (q >> 1)], (q & 1) ? 0x7632 : 0x5410);
 #pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            const uint32_t base = smem_u32(x_tile(s, p));
+            for (int p = 0; p < 4; ++p) {
+              const uint32_t base = smem_u32(x_tile(s, p));
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int a = p ^ q;
-              const uint32_t sg = quat_neg(a, p) ? 0x80008000u : 0u;
-              const int row = a * N_TOK + tok;
-              const uint32_t addr = base + row * 64 + ((gb ^ ((row >> 1) & 3)) << 4);
-              st_shared_v4(addr, pl[q][0] ^ sg, pl[q][1] ^ sg, pl[q][2] ^ sg, pl[q][3] ^ sg);
+              for (int q = 0; q < 4; ++q) {
+                const int a = p ^ q;
+                const uint32_t sg = quat_neg(a, p) ? 0x80008000u : 0u;
+                const int row = a * N_TOK + tok;
+                const uint32_t addr = base + row * 64 + ((gb ^ ((row >> 1) & 3)) << 4);
+                st_shared_v4(addr, pl[q][0] ^ sg, pl[q][1] ^ sg, pl[q][2] ^ sg, pl[q][3] ^ sg);
+              }
             }
-          }
-          if (LORA == kLoraTc) {
-            // the same 64 bytes unchanged: row tok of raw sub-tile gb
-            const uint32_t rbase = smem_u32(raw_tile(s, gb)) + tok * 64;
+            if (LORA == kLoraTc) {
+              // the same 64 bytes unchanged: row tok of raw sub-tile gb
+              const uint32_t rbase = smem_u32(raw_tile(s, gb)) + tok * 64;
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-              st_shared_v4(rbase + ((c ^ ((tok >> 1) & 3)) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2],
-                           w[4 * c + 3]);
+              for (int c = 0; c < 4; ++c)
+                st_shared_v4(rbase + ((c ^ ((tok >> 1) & 3)) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2],
+                             w[4 * c + 3]);
+            }
           }
         }
         fence_async_smem();
