@@ -30,8 +30,11 @@ struct DeviceInfo {
   int cc_major = 0, cc_minor = 0, num_sms = 0;
   // per (element type, N_TOK, in-kernel LoRA) kernel instance: attributes
   // set, and how many CTAs of it the device keeps resident at once
-  bool tc_attr_set[2][4][3][2] = {};
-  int resident[2][4][3][2] = {};
+  bool tc_attr_set[2][4][3][2][2] = {};  // [dtype][N_TOK][LoRA mode][peers][cluster]
+  int resident[2][4][3][2][2] = {};
+  // cluster K split: how many clusters of `split` CTAs fit at once, by
+  // [dtype][LoRA mode][split] (-1: not queried yet)
+  int cluster_cap[2][3][kTcClusterMax + 1];
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mutex;
@@ -49,6 +52,9 @@ int device_info(DeviceInfo** out) {
     d.cc_major = prop.major;
     d.cc_minor = prop.minor;
     d.num_sms = prop.multiProcessorCount;
+    for (auto& a : d.cluster_cap)
+      for (auto& b : a)
+        for (int& c : b) c = -1;
     d.init = true;
   }
   *out = &d;
@@ -214,15 +220,15 @@ int split_for(int64_t M, int64_t K_g, int64_t N_g, int rank, int64_t sms) {
   return s;
 }
 
-template <typename T, int N_TOK, int LORA, bool PEERS = false>
+template <typename T, int N_TOK, int LORA, bool PEERS = false, bool CLUSTER = false>
 int ensure_tc_attrs(DeviceInfo* dev) {
-  using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>, LORA>;
-  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA, PEERS>;
+  using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>, LORA, CLUSTER>;
+  auto kernel = qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA, PEERS, CLUSTER>;
   const int ti = n_tok_index(N_TOK);
   const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
-  const int li = LORA, pi = PEERS ? 1 : 0;
+  const int li = LORA, pi = PEERS ? 1 : 0, ci = CLUSTER ? 1 : 0;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (dev->tc_attr_set[di][ti][li][pi]) return QLIN_OK;
+  if (dev->tc_attr_set[di][ti][li][pi][ci]) return QLIN_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
       cudaSuccess)
     return QLIN_ERR_LAUNCH;
@@ -242,9 +248,49 @@ int ensure_tc_attrs(DeviceInfo* dev) {
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, tc_block_threads(LORA), Cfg::kSmemBytes) !=
       cudaSuccess)
     return QLIN_ERR_LAUNCH;
-  dev->resident[di][ti][li][pi] = per_sm * dev->num_sms;
-  dev->tc_attr_set[di][ti][li][pi] = true;
+  dev->resident[di][ti][li][pi][ci] = per_sm * dev->num_sms;
+  dev->tc_attr_set[di][ti][li][pi][ci] = true;
   return QLIN_OK;
+}
+
+// Cluster K split for decode tiles: every split of a tile in one cluster
+// (at most kTcClusterMax CTAs), the partials summed through distributed
+// shared memory.  Used when at most kTcClusterTokens tokens, 2..8 splits and
+// all clusters of the grid fit on the device at once.
+template <typename T, int LORA>
+bool cluster_fits(DeviceInfo* dev, int split, int64_t tiles) {
+  if constexpr (LORA == kLoraTc) {
+    return false;
+  } else {
+    const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
+    int cap;
+    {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      cap = dev->cluster_cap[di][LORA][split];
+    }
+    if (cap < 0) {
+      if (ensure_tc_attrs<T, 16, LORA, false, true>(dev) != QLIN_OK) return false;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)split, (unsigned)tiles, 1);
+      cfg.blockDim = dim3(tc_block_threads(LORA), 1, 1);
+      cfg.dynamicSmemBytes = TcCfg<16, true, LORA, true>::kSmemBytes;
+      cudaLaunchAttribute a;
+      a.id = cudaLaunchAttributeClusterDimension;
+      a.val.clusterDim.x = (unsigned)split;
+      a.val.clusterDim.y = 1;
+      a.val.clusterDim.z = 1;
+      cfg.attrs = &a;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, qlin_tc_kernel<T, 16, true, LORA, false, true>, &cfg) != cudaSuccess)
+        n = 0;
+      cudaGetLastError();
+      cap = n;
+      std::lock_guard<std::mutex> lock(g_mutex);
+      dev->cluster_cap[di][LORA][split] = cap;
+    }
+    return cap >= tiles;
+  }
 }
 
 template <typename T, int N_TOK, int LORA>
@@ -253,6 +299,37 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
   using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>, LORA>;
   // outputs also stored to peers only in the column-partitioned path's build
   const bool peers = base_prm.peers.n > 0;
+  {
+    const int64_t o_blocks = (N_g + kTcBlockO - 1) / kTcBlockO, t_blocks = (M + N_TOK - 1) / N_TOK;
+    const int split = split_for(M, K_g, N_g, base_prm.rank, dev->num_sms);
+    if constexpr (N_TOK == 16 && LORA != kLoraTc) {
+      if (M <= kTcClusterTokens && split > 1 && split <= kTcClusterMax && !peers &&
+          cluster_fits<T, LORA>(dev, split, o_blocks * t_blocks)) {
+        TcParams prm = base_prm;
+        prm.split_k = split;
+        prm.partials = nullptr;
+        prm.fuse_reduce = 0;
+        cudaLaunchAttribute attrs[2];
+        attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[0].val.programmaticStreamSerializationAllowed = 1;
+        attrs[1].id = cudaLaunchAttributeClusterDimension;
+        attrs[1].val.clusterDim.x = (unsigned)split;
+        attrs[1].val.clusterDim.y = 1;
+        attrs[1].val.clusterDim.z = 1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)split, (unsigned)o_blocks, (unsigned)t_blocks);
+        cfg.blockDim = dim3(tc_block_threads(LORA), 1, 1);
+        cfg.dynamicSmemBytes = TcCfg<16, true, LORA, true>::kSmemBytes;
+        cfg.stream = stream;
+        cfg.attrs = attrs;
+        cfg.numAttrs = 2;
+        return cudaLaunchKernelEx(&cfg, qlin_tc_kernel<T, 16, true, LORA, false, true>, maps[0], maps[1],
+                                  maps[2], maps[3], maps[4], maps[5], maps[6], maps[7], prm) == cudaSuccess
+                   ? QLIN_OK
+                   : QLIN_ERR_LAUNCH;
+      }
+    }
+  }
   auto kernel = peers ? qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA, true>
                       : qlin_tc_kernel<T, N_TOK, kStackFor<N_TOK>, LORA, false>;
   int st = peers ? ensure_tc_attrs<T, N_TOK, LORA, true>(dev) : ensure_tc_attrs<T, N_TOK, LORA, false>(dev);
@@ -499,7 +576,7 @@ int plan_tc(DeviceInfo* dev, int64_t M, int64_t K_g, int64_t N_g, int rank, int*
   if (st != QLIN_OK) return st;
   const int ti = n_tok_index(N_TOK);
   const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
-  *resident = dev->resident[di][ti][li][0];
+  *resident = dev->resident[di][ti][li][0][0];
   return QLIN_OK;
 }
 
@@ -611,7 +688,17 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flag
                        : plan_tc<__half, 128>(dev, M, K_g, N_g, rank, &sp, &res); break;
     }
     if (st != QLIN_OK) return st;
-    const bool fused = (flags & QLIN_FLAG_ZEROED_WORKSPACE) && M <= kFusedReduceMaxTokens;
+    bool clustered = false;
+    if (nt == 16 && M <= kTcClusterTokens && sp > 1 && sp <= kTcClusterMax) {
+      const int lm = lora_mode(M, rank, K_g, sp);
+      const int64_t tiles = (N_g + kTcBlockO - 1) / kTcBlockO;
+      if (lm == kLoraSimt)
+        clustered = bf ? cluster_fits<__nv_bfloat16, kLoraSimt>(dev, sp, tiles) : cluster_fits<__half, kLoraSimt>(dev, sp, tiles);
+      else if (lm == kLoraPrologue)
+        clustered = bf ? cluster_fits<__nv_bfloat16, kLoraPrologue>(dev, sp, tiles)
+                       : cluster_fits<__half, kLoraPrologue>(dev, sp, tiles);
+    }
+    const bool fused = clustered || ((flags & QLIN_FLAG_ZEROED_WORKSPACE) && M <= kFusedReduceMaxTokens);
     const bool prologue = M > kStackMaxTokens || (rank > 0 && lora_mode(M, rank, K_g, sp) == kLoraPrologue);
     nl = 1 + (prologue ? 1 : 0) + ((sp > 1 && !fused) ? 1 : 0);
   } else {

@@ -84,7 +84,13 @@ __host__ __device__ constexpr int tmem_cols_for(int n) {
   return n <= 32 ? 32 : (n <= 64 ? 64 : (n <= 128 ? 128 : (n <= 256 ? 256 : 512)));
 }
 
-template <int N_TOK, bool STACK, int LORA = kLoraPrologue>
+// Cluster K split (decode, at most kTcClusterTokens tokens): every split of
+// a tile is one CTA of an 8-at-most CTA cluster and pushes its fp32 partial
+// into the leader CTA's receive buffer [split-1][token][128] x float4.
+constexpr int kTcClusterTokens = 2;
+constexpr int kTcClusterMax = 8;
+
+template <int N_TOK, bool STACK, int LORA = kLoraPrologue, bool CLUSTER = false>
 struct TcCfg {
   // Activation operand per weight component and stage: stacked [4*N_TOK rows]
   // or one plane [N_TOK rows], 64 bytes per row either way.
@@ -98,17 +104,20 @@ struct TcCfg {
   // CUDA-core LoRA: the split's lora_a slice [32 rows][<= 512 elements],
   // loaded once, ahead of the weights, as row pieces of kTcLoraSliceBox
   static constexpr int kSliceBytes = LORA == kLoraSimt ? kTcLoraInRank * kTcLoraSliceMax * 2 : 0;
-  static constexpr int kFit = (200 * 1024 - kSliceBytes) / kStageBytes;
+  static constexpr int kRecvBytes = CLUSTER ? (kTcClusterMax - 1) * kTcClusterTokens * kTcBlockO * 16 : 0;
+  static constexpr int kFit = ((CLUSTER ? 212 : 200) * 1024 - kSliceBytes - kRecvBytes) / kStageBytes;
   static constexpr int kStages = kFit > 6 ? 6 : (kFit < 2 ? 2 : kFit);
   static constexpr int kSliceOffset = kStages * kStageBytes;
+  static constexpr int kRecvOffset = kSliceOffset + kSliceBytes;
   // accumulators: 4*N_TOK columns of Y (+ kTcLoraInRank columns of t)
   static constexpr int kTmemCols = tmem_cols_for(4 * N_TOK + (LORA == kLoraTc ? kTcLoraInRank : 0));
-  static constexpr int kBarOffset = kSliceOffset + kSliceBytes;
+  static constexpr int kBarOffset = kRecvOffset + kRecvBytes;
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
   static_assert(N_TOK == 16 || N_TOK == 32 || N_TOK == 64 || N_TOK == 128, "UMMA N");
   static_assert(!STACK || N_TOK <= 64, "stacked operand has 4*N_TOK <= 256 rows");
   static_assert(LORA != kLoraTc || (STACK && N_TOK <= 32), "tensor-core LoRA: stacked, tokens in lanes 64..95");
   static_assert(LORA != kLoraSimt || (STACK && N_TOK == 16), "CUDA-core LoRA: stacked, at most 4 tokens");
+  static_assert(!CLUSTER || (STACK && N_TOK == 16), "cluster K split: decode tiles");
   // The LoRA down projection's A operand (128 rows from kTcTLane rows before
   // a raw x sub-tile) stays inside the stage: 4 KB of x operands before the
   // raw rows, at least 4 KB (raw rows + lora_a) after the last sub-tile.
@@ -173,14 +182,14 @@ __device__ __forceinline__ unsigned atomic_add_release_gpu(unsigned* p, unsigned
   return old;
 }
 
-template <typename T, int N_TOK, bool STACK, int LORA, bool PEERS>
+template <typename T, int N_TOK, bool STACK, int LORA, bool PEERS, bool CLUSTER = false>
 __global__ void __launch_bounds__(kTcMaxThreads, 1)
 qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant__ CUtensorMap map_wi,
                const __grid_constant__ CUtensorMap map_wj, const __grid_constant__ CUtensorMap map_wk,
                const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_lb,
                const __grid_constant__ CUtensorMap map_t, const __grid_constant__ CUtensorMap map_la,
                const TcParams prm) {
-  using Cfg = TcCfg<N_TOK, STACK, LORA>;
+  using Cfg = TcCfg<N_TOK, STACK, LORA, CLUSTER>;
   constexpr int S = Cfg::kStages;
   // Activation operands built in shared memory by the builder warps
   // (stacked tiles) or TMA-loaded from the prologue's planar copy of x
@@ -201,7 +210,8 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   uint64_t* acc_full = empty + S;
   uint64_t* t_full = acc_full + 1;  // LoRA: down projection complete (tensor cores) / lora_a slice loaded (CUDA cores)
   uint64_t* red_full = t_full + 1;  // fused K-split reduction: all partials are in shared memory
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_full + 1);
+  uint64_t* gather = red_full + 1;  // cluster K split (leader): every peer's partial has arrived
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gather + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued_count = const_cast<int*>(abort_flag) + 1;
   int* consumed_count = issued_count + 1;
@@ -280,7 +290,8 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   auto load_bias = [&](T (&raw)[4]) {
     const int ob = o0 + (int)threadIdx.x;
     const T* __restrict__ bp = reinterpret_cast<const T*>(prm.bias);
-    const bool has = bp && (prm.split_k == 1 || prm.fuse_reduce) && ob < prm.N_g && threadIdx.x < kTcBlockO;
+    const bool has = bp && (prm.split_k == 1 || prm.fuse_reduce || (CLUSTER && ks == 0)) && ob < prm.N_g &&
+                     threadIdx.x < kTcBlockO;
 #pragma unroll
     for (int a = 0; a < 4; ++a) raw[a] = has ? bp[4 * ob + a] : from_f32<T>(0.f);
   };
@@ -295,6 +306,11 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     mbar_init(acc_full, 1);
     mbar_init(t_full, 1);
     mbar_init(red_full, 1);
+    mbar_init(gather, 1);
+    // the leader arms its receive barrier before any peer can send (the
+    // cluster barrier below orders this before every peer's epilogue)
+    if (CLUSTER && ks == 0)
+      mbar_arrive_expect_tx(gather, (uint32_t)((prm.split_k - 1) * m_tile * kTcBlockO * 16));
     *abort_flag = 0;
     *issued_count = 0;
     *consumed_count = 0;
@@ -319,6 +335,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (CLUSTER) cluster_sync_all();  // every CTA's barriers are initialised
   const uint32_t tmem_base = *tmem_slot;
   // Everything below may read what earlier kernels of the stream wrote (x,
   // the prologue's outputs, the workspace) or write what they read (y).
@@ -656,6 +673,46 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
           }
         }
       }
+    } else if (CLUSTER) {
+      // Cluster K split (at most kTcClusterTokens tokens): the peers push
+      // their fp32 partial of the real tokens into the leader's receive
+      // buffer (st.async, counted on the leader's gather barrier) -- sent even
+      // after an abort so the leader's count completes -- and the leader adds
+      // them, in split order after its own, to the bias.
+      float v[4][16];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) tmem_ld16(lane_addr + a * N_TOK, v[a]);
+      tmem_ld_wait();
+      if (ks > 0) {
+        const uint32_t rbase = map_peer_smem(smem_u32(smem + Cfg::kRecvOffset), 0);
+        const uint32_t rbar = map_peer_smem(smem_u32(gather), 0);
+#pragma unroll
+        for (int t = 0; t < kTcClusterTokens; ++t)
+          if (t < m_tile)
+            st_async_v4(rbase + (uint32_t)((((ks - 1) * kTcClusterTokens + t) * kTcBlockO + o_local) * 16),
+                        make_float4(v[0][t], v[1][t], v[2][t], v[3][t]), rbar);
+      } else {
+        const bool got = mbar_wait(gather, 0);
+        const float4* recv = reinterpret_cast<const float4*>(smem + Cfg::kRecvOffset);
+        const int o = o0 + o_local;
+        float b[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) b[a] = to_f32(bias_raw[a]);
+#pragma unroll
+        for (int t = 0; t < kTcClusterTokens; ++t) {
+          if (t < m_tile) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            acc.x += v[0][t]; acc.y += v[1][t]; acc.z += v[2][t]; acc.w += v[3][t];
+            for (int sp = 1; sp < prm.split_k; ++sp) {
+              const float4 r = recv[((sp - 1) * kTcClusterTokens + t) * kTcBlockO + o_local];
+              acc.x += r.x; acc.y += r.y; acc.z += r.z; acc.w += r.w;
+            }
+            if (ok && got && o < prm.N_g)
+              store_out<T, PEERS>(y, prm.peers, (int64_t)(t0 + t) * prm.ld_y + 4 * o,
+                                  pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
+          }
+        }
+      }
     } else {
       // K split: fp32 partials of the real tokens go to this CTA's slot of the
       // workspace as [token][row] float4 (a = 0..3).  They are summed with the
@@ -764,6 +821,12 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   // ---------------- teardown ----------------
   tc_fence_before();
   __syncthreads();
+  // No CTA of a cluster leaves while another may still store into it: the
+  // leader arrives once every partial has landed, the peers after sending.
+  if (CLUSTER) {
+    cluster_arrive_release();
+    cluster_wait_acquire();
+  }
   if (threadIdx.x == 0 && *abort_flag) {
     // Let TMA loads that were issued but never consumed land before exiting.
     for (int it = *consumed_count; it < *issued_count; ++it)
