@@ -209,13 +209,17 @@ int lora_mode(int64_t M, int rank, int64_t K_g, int split) {
 // Threads of a tensor-core CTA: 128, plus two LoRA warps in the CUDA-core mode.
 constexpr int tc_block_threads(int lora) { return lora == kLoraSimt ? kTcMaxThreads : kTcThreads; }
 
-// K split the device path uses.  With the CUDA-core LoRA (at most 4
-// tokens) every split also loads LoRA B and applies its own LoRA term, a
-// fixed cost per CTA; there at most 8 splits (each streaming more weights)
-// measured faster than 16 on B200 for the 4096-wide decode layer.
-int split_for(int64_t M, int64_t K_g, int64_t N_g, int rank, int64_t sms) {
+// K split the device path uses (same-box measurements on B200, 4096-wide
+// decode layer).  At most 2 tokens: 8 splits, one cluster per tile, summed
+// through distributed shared memory (6.6 vs 8.1 us/call with LoRA r=32, 6.2
+// vs 6.8 without) -- except with static weights and no LoRA, where 16
+// splits prefetching their weights stay faster (5.9 vs 6.3).  With the
+// CUDA-core LoRA (at most 4 tokens) every split also loads LoRA B and
+// applies its own LoRA term, a fixed cost per CTA: at most 8 splits there.
+int split_for(int64_t M, int64_t K_g, int64_t N_g, int rank, int64_t sms, bool static_weights = false) {
   const int s = max_split_for(M, K_g, N_g, sms);
   const int64_t chunks = (K_g + kTcChunk - 1) / kTcChunk;
+  if (M <= kTcClusterTokens && s > kTcClusterMax && !(static_weights && rank == 0)) return kTcClusterMax;
   if (rank > 0 && rank <= kTcLoraInRank && M <= kTcLoraSimtTokens && s > 8 && (chunks + 7) / 8 <= 4) return 8;
   return s;
 }
@@ -301,7 +305,7 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
   const bool peers = base_prm.peers.n > 0;
   {
     const int64_t o_blocks = (N_g + kTcBlockO - 1) / kTcBlockO, t_blocks = (M + N_TOK - 1) / N_TOK;
-    const int split = split_for(M, K_g, N_g, base_prm.rank, dev->num_sms);
+    const int split = split_for(M, K_g, N_g, base_prm.rank, dev->num_sms, base_prm.static_weights != 0);
     if constexpr (N_TOK == 16 && LORA != kLoraTc) {
       if (M <= kTcClusterTokens && split > 1 && split <= kTcClusterMax && !peers &&
           cluster_fits<T, LORA>(dev, split, o_blocks * t_blocks)) {
@@ -338,7 +342,7 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
   const int64_t o_blocks = (N_g + kTcBlockO - 1) / kTcBlockO;
   const int64_t t_blocks = (M + N_TOK - 1) / N_TOK;
   if (o_blocks > 65535 || t_blocks > 65535) return QLIN_ERR_SHAPE;
-  const int split = split_for(M, K_g, N_g, base_prm.rank, dev->num_sms);
+  const int split = split_for(M, K_g, N_g, base_prm.rank, dev->num_sms, base_prm.static_weights != 0);
   prm.split_k = split;
   prm.partials = split > 1 ? partials : nullptr;
   if (split > 1 && !partials) return QLIN_ERR_WORKSPACE;
@@ -393,7 +397,8 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
   T* t = rank > 0 ? reinterpret_cast<T*>(ws + L.t_off) : nullptr;
   const int n_tok = n_tok_for(M);
   const bool stack = M <= kStackMaxTokens;
-  const int lmode = lora_mode(M, rank, K_g, split_for(M, K_g, N_g, rank, dev->num_sms));
+  const int lmode =
+      lora_mode(M, rank, K_g, split_for(M, K_g, N_g, rank, dev->num_sms, (flags & QLIN_FLAG_STATIC_WEIGHTS) != 0));
   const bool lora_in = lmode != kLoraPrologue;
 
   // 1. prologue: component planes of x (plane mode) and the scaled LoRA down
@@ -560,8 +565,9 @@ int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void*
 }
 
 template <typename T, int N_TOK>
-int plan_tc(DeviceInfo* dev, int64_t M, int64_t K_g, int64_t N_g, int rank, int* split, int* resident) {
-  *split = split_for(M, K_g, N_g, rank, dev->num_sms);
+int plan_tc(DeviceInfo* dev, int64_t M, int64_t K_g, int64_t N_g, int rank, int flags, int* split,
+            int* resident) {
+  *split = split_for(M, K_g, N_g, rank, dev->num_sms, (flags & QLIN_FLAG_STATIC_WEIGHTS) != 0);
   const int li = lora_mode(M, rank, K_g, *split);
   int st = QLIN_OK;
   if constexpr (N_TOK == 16) {
@@ -678,14 +684,14 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flag
     nt = n_tok_for(M);
     const bool bf = dtype == QLIN_BF16;
     switch (nt) {
-      case 16: st = bf ? plan_tc<__nv_bfloat16, 16>(dev, M, K_g, N_g, rank, &sp, &res)
-                       : plan_tc<__half, 16>(dev, M, K_g, N_g, rank, &sp, &res); break;
-      case 32: st = bf ? plan_tc<__nv_bfloat16, 32>(dev, M, K_g, N_g, rank, &sp, &res)
-                       : plan_tc<__half, 32>(dev, M, K_g, N_g, rank, &sp, &res); break;
-      case 64: st = bf ? plan_tc<__nv_bfloat16, 64>(dev, M, K_g, N_g, rank, &sp, &res)
-                       : plan_tc<__half, 64>(dev, M, K_g, N_g, rank, &sp, &res); break;
-      default: st = bf ? plan_tc<__nv_bfloat16, 128>(dev, M, K_g, N_g, rank, &sp, &res)
-                       : plan_tc<__half, 128>(dev, M, K_g, N_g, rank, &sp, &res); break;
+      case 16: st = bf ? plan_tc<__nv_bfloat16, 16>(dev, M, K_g, N_g, rank, flags, &sp, &res)
+                       : plan_tc<__half, 16>(dev, M, K_g, N_g, rank, flags, &sp, &res); break;
+      case 32: st = bf ? plan_tc<__nv_bfloat16, 32>(dev, M, K_g, N_g, rank, flags, &sp, &res)
+                       : plan_tc<__half, 32>(dev, M, K_g, N_g, rank, flags, &sp, &res); break;
+      case 64: st = bf ? plan_tc<__nv_bfloat16, 64>(dev, M, K_g, N_g, rank, flags, &sp, &res)
+                       : plan_tc<__half, 64>(dev, M, K_g, N_g, rank, flags, &sp, &res); break;
+      default: st = bf ? plan_tc<__nv_bfloat16, 128>(dev, M, K_g, N_g, rank, flags, &sp, &res)
+                       : plan_tc<__half, 128>(dev, M, K_g, N_g, rank, flags, &sp, &res); break;
     }
     if (st != QLIN_OK) return st;
     bool clustered = false;

@@ -95,16 +95,29 @@ def test_fused_reduction_in_a_graph_and_back_to_back(qb, workloads, cuda):
     assert qb.device_error(cuda) == 0
 
 def test_plan_counts_the_fused_reduction(qb, cuda):
-    p0 = qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 0, flags=0)
-    p1 = qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 0, flags=FLAG_ZEROED)
+    # three or four tokens: the K split is summed by the last CTA of each tile
+    # on a zero-filled workspace, else by the reduction kernel
+    p0 = qb._lib.plan(torch.bfloat16, 3, 1024, 1024, 0, flags=0)
+    p1 = qb._lib.plan(torch.bfloat16, 3, 1024, 1024, 0, flags=FLAG_ZEROED)
     assert p0["split_k"] > 1
     assert p1["launches"] == p0["launches"] - 1 == 1
     # above four tokens the separate reduction kernel stays
     p5 = qb._lib.plan(torch.bfloat16, 5, 1024, 1024, 0, flags=FLAG_ZEROED)
     assert p5["launches"] == 2
+    # one or two tokens: an 8-way split summed inside a thread-block cluster,
+    # one launch whatever the workspace (static weights without LoRA keep the
+    # wider split and the workspace paths)
+    for M in (1, 2):
+        for rank in (0, 32):
+            p = qb._lib.plan(torch.bfloat16, M, 1024, 1024, rank, flags=0)
+            assert p["split_k"] == 8 and p["launches"] == 1, (M, rank, p)
+    ps = qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 0, flags=1)
+    assert ps["split_k"] == 16 and ps["launches"] == 2
+    assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 0, flags=1 | FLAG_ZEROED)["launches"] == 1
     # the module path uses the zeroed workspace for decode-sized calls, and a
     # rank <= 32 LoRA down projection runs inside the main kernel: one launch
     assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 32)["launches"] == 1
+
 
 def test_module_path_keeps_its_workspace_counters_zero(qb, cuda):
     g = torch.Generator().manual_seed(11)
