@@ -31,6 +31,7 @@ ERR_TIMEOUT = 7
 _DTYPE_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 
 _lib = None
+_fast = None  # CPython binding of qlin_forward_ex (lib/_qlin_call*.so), when built
 _lock = threading.Lock()
 
 EXPORTED = (
@@ -103,7 +104,28 @@ def load(path: str | None = None):
         lib.qlin_ipc_close.restype = I
         if path is None:
             _lib = lib
+            _load_fast(os.path.dirname(p))
         return lib
+
+
+def _load_fast(lib_dir: str) -> None:
+    """Import the CPython binding built next to the library (it links to the
+    same libqlin_b200.so, already loaded above); keep ctypes without it."""
+    global _fast
+    import glob
+    import importlib.util
+
+    for f in glob.glob(os.path.join(lib_dir, "_qlin_call*.so")):
+        spec = importlib.util.spec_from_file_location("_qlin_call", f)
+        if spec is None or spec.loader is None:
+            continue
+        try:
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+        except ImportError:
+            continue
+        _fast = mod
+        return
 
 
 def status_string(code: int) -> str:
@@ -130,14 +152,23 @@ def dtype_code(dtype: torch.dtype) -> int:
 
 
 def stream_handle(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """Raw handle of the current CUDA stream of ``device`` (cudaStream_t as int)."""
+    return torch._C._cuda_getCurrentRawStream(device.index if device.index is not None
+                                              else torch.cuda.current_device())
+
+
+_ws_sizes: dict[tuple, int] = {}
 
 
 def workspace_size(dtype: torch.dtype, M: int, K_g: int, N_g: int, rank: int) -> int:
-    n = ctypes.c_size_t(0)
-    check(load().qlin_workspace_size(dtype_code(dtype), M, K_g, N_g, rank, ctypes.byref(n)),
-          "qlin_workspace_size")
-    return int(n.value)
+    key = (dtype, M, K_g, N_g, rank)
+    n = _ws_sizes.get(key)
+    if n is None:
+        c = ctypes.c_size_t(0)
+        check(load().qlin_workspace_size(dtype_code(dtype), M, K_g, N_g, rank, ctypes.byref(c)),
+              "qlin_workspace_size")
+        n = _ws_sizes[key] = int(c.value)
+    return n
 
 
 def device_error(device: torch.device | None = None, clear: bool = True) -> int:
@@ -184,8 +215,7 @@ def zeroed_workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
     """The zero-filled workspace of the current stream of ``device``, grown to
     ``nbytes`` if needed; None while a CUDA graph is being captured and the
     cached buffer is too small (the caller then uses a plain workspace)."""
-    stream = torch.cuda.current_stream(device)
-    key = (device.index, stream.cuda_stream)
+    key = (device.index, stream_handle(device))
     buf = _zeroed_ws.get(key)
     if buf is not None and buf.numel() >= nbytes:
         return buf
@@ -199,7 +229,7 @@ def zeroed_workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
 def forward_raw(x2, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y2, ld_y,
                 M, K_g, N_g, algo=ALGO_AUTO, flags=0):
     """Call ``qlin_forward_ex`` on prepared 2-D device tensors (see linear.py)."""
-    lib = load()
+    lib = _lib if _lib is not None else load()
     dev = x2.device
     ws_bytes = workspace_size(x2.dtype, M, K_g, N_g, rank)
     ws = None
@@ -209,10 +239,12 @@ def forward_raw(x2, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y2, l
             flags |= FLAG_ZEROED_WORKSPACE
     if ws is None and ws_bytes:
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    code = lib.qlin_forward_ex(
-        dtype_code(x2.dtype), _ptr(x2), ld_x, _ptr(w[0]), _ptr(w[1]), _ptr(w[2]), _ptr(w[3]), ld_w,
-        _ptr(bias), _ptr(lora_a), _ptr(lora_b), int(rank), float(lora_scale),
-        _ptr(y2), ld_y, M, K_g, N_g, _ptr(ws), ws_bytes, int(algo), int(flags), stream_handle(dev),
+    fn = _fast.forward_ex if _fast is not None else lib.qlin_forward_ex
+    code = fn(
+        _DTYPE_CODE[x2.dtype], x2.data_ptr(), ld_x, w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(),
+        w[3].data_ptr(), ld_w, _ptr(bias), _ptr(lora_a), _ptr(lora_b), rank, lora_scale,
+        y2.data_ptr(), ld_y, M, K_g, N_g, _ptr(ws), ws_bytes, algo, flags,
+        torch._C._cuda_getCurrentRawStream(dev.index),
     )
     check(code, "qlin_forward")
     return y2

@@ -13,6 +13,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(PKG)
@@ -27,7 +28,7 @@ DEPENDS = SOURCES + [os.path.join(CSRC, f) for f in ("qlin_common.cuh", "qlin_si
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo", "-O3", "-std=c++17",
-    "-Xcompiler", "-fPIC", "-shared", "-cudart", "static",
+    "-Xcompiler", "-fPIC", "-shared", "-cudart", "static", "-Xlinker", "-soname=libqlin_b200.so",
     "-Xptxas", "-v",
     "-I", os.path.join(REPO, "include"),
 ]
@@ -40,11 +41,27 @@ def find_nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
+# CPython binding of qlin_forward_ex (the per-call path; ctypes otherwise)
+PYCALL_SRC = os.path.join(CSRC, "qlin_pycall.c")
+PYCALL_PATH = os.path.join(LIB_DIR, "_qlin_call" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+
+
 def needs_build() -> bool:
-    if not os.path.exists(LIB_PATH):
+    if not os.path.exists(LIB_PATH) or not os.path.exists(PYCALL_PATH):
         return True
-    t = os.path.getmtime(LIB_PATH)
-    return any(os.path.getmtime(p) > t for p in DEPENDS)
+    t = min(os.path.getmtime(LIB_PATH), os.path.getmtime(PYCALL_PATH))
+    return any(os.path.getmtime(p) > t for p in DEPENDS + [PYCALL_SRC])
+
+
+def build_pycall() -> None:
+    cc = os.environ.get("QLIN_CC") or shutil.which("gcc") or "cc"
+    cmd = [cc, "-O2", "-shared", "-fPIC", "-I", sysconfig.get_paths()["include"], "-I",
+           os.path.join(REPO, "include"), "-o", PYCALL_PATH + ".tmp", PYCALL_SRC, "-L", LIB_DIR,
+           "-lqlin_b200", "-Wl,-rpath,$ORIGIN"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"building the CPython binding failed:\n{res.stderr[-2000:]}")
+    os.replace(PYCALL_PATH + ".tmp", PYCALL_PATH)
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -60,6 +77,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed ({res.returncode}); see {log}\n{res.stderr[-4000:]}")
     os.replace(tmp, LIB_PATH)
+    build_pycall()
     if verbose:
         print(res.stderr)
     return LIB_PATH

@@ -120,10 +120,15 @@ def _forward_impl(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=None, lora_s
         rank += pad
     y = torch.empty((M, 4 * out_groups), dtype=x.dtype, device=dev)
     if M:
-        with torch.cuda.device(dev):
-            _lib.forward_raw(x2, ld_x, ws, ld_w, b, la, lb, rank, lora_scale, y, 4 * out_groups,
-                             M, in_groups, out_groups, algo,
-                             _lib.FLAG_STATIC_WEIGHTS if static_weights else 0)
+        flags = _lib.FLAG_STATIC_WEIGHTS if static_weights else 0
+        # the library launches on the current device: switch only when needed
+        if torch.cuda.current_device() == dev.index:
+            _lib.forward_raw(x2, ld_x, ws, ld_w, b, la, lb, rank, float(lora_scale), y, 4 * out_groups,
+                             M, in_groups, out_groups, int(algo), flags)
+        else:
+            with torch.cuda.device(dev):
+                _lib.forward_raw(x2, ld_x, ws, ld_w, b, la, lb, rank, float(lora_scale), y,
+                                 4 * out_groups, M, in_groups, out_groups, int(algo), flags)
     return y.reshape(*lead, 4 * out_groups)
 
 

@@ -83,3 +83,22 @@ def test_shape_status_maps_to_valueerror(qb):
         qb._lib.check(1, "x")
     with pytest.raises(RuntimeError):
         qb._lib.check(5, "x")
+
+
+def test_cpython_binding_matches_ctypes_on_refusals(qb):
+    # the per-call path's CPython binding of qlin_forward_ex (built next to
+    # the library) gives the same status codes as the ctypes binding
+    lib = qb._lib.load()
+    fast = qb._lib._fast
+    assert fast is not None, "lib/_qlin_call*.so not built"
+    P = None
+    cases = [
+        (1, 1, 10, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 0, P),  # ld_x < 4*K_g
+        (1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 4, P),  # unknown flag
+        (7, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 0, P),  # dtype
+        (1, P, 16, P, P, P, P, 4, P, P, P, 0, 0.0, P, 16, 0, 4, 4, P, 0, 0, 0, P),  # M == 0
+    ]
+    for c in cases:
+        assert fast.forward_ex(*c) == lib.qlin_forward_ex(*c)
+    with pytest.raises(TypeError):
+        fast.forward_ex(1, 2, 3)
