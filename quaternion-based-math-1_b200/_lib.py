@@ -32,6 +32,7 @@ _DTYPE_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 
 _lib = None
 _fast = None  # CPython binding of qlin_forward_ex (lib/_qlin_call*.so), when built
+_torch_ext = None  # C++ inference forward of the modules (lib/_qlin_torch*.so), when built
 _lock = threading.Lock()
 
 EXPORTED = (
@@ -109,23 +110,29 @@ def load(path: str | None = None):
 
 
 def _load_fast(lib_dir: str) -> None:
-    """Import the CPython binding built next to the library (it links to the
-    same libqlin_b200.so, already loaded above); keep ctypes without it."""
-    global _fast
+    """Import the bindings built next to the library (both link to the same
+    libqlin_b200.so, already loaded above): the CPython binding of
+    qlin_forward_ex and the C++ inference forward; keep ctypes and the Python
+    forward without them."""
+    global _fast, _torch_ext
     import glob
     import importlib.util
 
-    for f in glob.glob(os.path.join(lib_dir, "_qlin_call*.so")):
-        spec = importlib.util.spec_from_file_location("_qlin_call", f)
-        if spec is None or spec.loader is None:
-            continue
-        try:
-            mod = importlib.util.module_from_spec(spec)
-            spec.loader.exec_module(mod)
-        except ImportError:
-            continue
-        _fast = mod
-        return
+    def imp(pattern, name):
+        for f in glob.glob(os.path.join(lib_dir, pattern)):
+            spec = importlib.util.spec_from_file_location(name, f)
+            if spec is None or spec.loader is None:
+                continue
+            try:
+                mod = importlib.util.module_from_spec(spec)
+                spec.loader.exec_module(mod)
+            except ImportError:
+                continue
+            return mod
+        return None
+
+    _fast = imp("_qlin_call*.so", "_qlin_call")
+    _torch_ext = imp("_qlin_torch*.so", "_qlin_torch")
 
 
 def status_string(code: int) -> str:

@@ -46,11 +46,40 @@ PYCALL_SRC = os.path.join(CSRC, "qlin_pycall.c")
 PYCALL_PATH = os.path.join(LIB_DIR, "_qlin_call" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
 
+# torch extension: the modules' inference forward in C++
+TORCH_EXT_SRC = os.path.join(CSRC, "qlin_torch_ext.cpp")
+TORCH_EXT_PATH = os.path.join(LIB_DIR, "_qlin_torch" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+
+
 def needs_build() -> bool:
-    if not os.path.exists(LIB_PATH) or not os.path.exists(PYCALL_PATH):
+    outs = (LIB_PATH, PYCALL_PATH, TORCH_EXT_PATH)
+    if not all(os.path.exists(p) for p in outs):
         return True
-    t = min(os.path.getmtime(LIB_PATH), os.path.getmtime(PYCALL_PATH))
-    return any(os.path.getmtime(p) > t for p in DEPENDS + [PYCALL_SRC])
+    t = min(os.path.getmtime(p) for p in outs)
+    return any(os.path.getmtime(p) > t for p in DEPENDS + [PYCALL_SRC, TORCH_EXT_SRC])
+
+
+def build_torch_ext() -> None:
+    import torch
+    import torch.utils.cpp_extension as ce
+
+    torch_lib = os.path.join(os.path.dirname(torch.__file__), "lib")
+    cuda_home = ce.CUDA_HOME or "/usr/local/cuda"
+    cxx = os.environ.get("QLIN_CXX") or shutil.which("g++") or "c++"
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           "-DTORCH_EXTENSION_NAME=_qlin_torch", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           "-I", os.path.join(os.path.dirname(torch.__file__), "include"),
+           "-I", os.path.join(os.path.dirname(torch.__file__), "include", "torch", "csrc", "api", "include"),
+           "-I", os.path.join(cuda_home, "include"), "-I", sysconfig.get_paths()["include"],
+           "-I", os.path.join(REPO, "include"),
+           "-o", TORCH_EXT_PATH + ".tmp", TORCH_EXT_SRC,
+           "-L", torch_lib, "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+           "-L", LIB_DIR, "-lqlin_b200", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"building the torch extension failed:\n{res.stderr[-3000:]}")
+    os.replace(TORCH_EXT_PATH + ".tmp", TORCH_EXT_PATH)
 
 
 def build_pycall() -> None:
@@ -78,6 +107,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         raise RuntimeError(f"nvcc failed ({res.returncode}); see {log}\n{res.stderr[-4000:]}")
     os.replace(tmp, LIB_PATH)
     build_pycall()
+    build_torch_ext()
     if verbose:
         print(res.stderr)
     return LIB_PATH

@@ -50,6 +50,19 @@ def _validate(x: torch.Tensor, wr, wi, wj, wk) -> tuple[int, int]:
 
 
 def _check_device(tensors) -> torch.device:
+    x = tensors[0]
+    if x.is_cuda:
+        # common case: every tensor on x's device with x's dtype
+        dev, dtype = x.device, x.dtype
+        ok = True
+        for t in tensors:
+            if t is not None and (t.device != dev or t.dtype != dtype):
+                ok = False
+                break
+        if ok:
+            if dtype not in _lib._DTYPE_CODE:
+                _lib.dtype_code(dtype)
+            return dev
     dev = None
     dtype = None
     for t in tensors:
@@ -71,6 +84,8 @@ def _check_device(tensors) -> torch.device:
 
 
 def _rows(x: torch.Tensor, K: int) -> tuple[torch.Tensor, int]:
+    if x.is_contiguous():
+        return x.view(-1, K), K
     x2 = x.reshape(-1, K)
     if x2.stride(-1) != 1 or (x2.shape[0] > 1 and x2.stride(0) < K):
         x2 = x2.contiguous()
@@ -79,6 +94,9 @@ def _rows(x: torch.Tensor, K: int) -> tuple[torch.Tensor, int]:
 
 
 def _weights(ws):
+    w0, w1, w2, w3 = ws
+    if w0.is_contiguous() and w1.is_contiguous() and w2.is_contiguous() and w3.is_contiguous():
+        return ws, w0.shape[1]
     ld = ws[0].stride(0)
     if any(w.stride(1) != 1 or w.stride(0) != ld for w in ws) or ld < ws[0].shape[1]:
         ws = tuple(w.contiguous() for w in ws)
@@ -88,6 +106,12 @@ def _weights(ws):
 
 def _forward_impl(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=None, lora_scale=0.0,
                   algo=_lib.ALGO_AUTO, static_weights=False):
+    if algo == _lib.ALGO_AUTO:
+        ext = _lib._torch_ext if _lib._lib is not None else (_lib.load() and _lib._torch_ext)
+        if ext is not None:
+            # the same checks, allocation and call in C++ (csrc/qlin_torch_ext.cpp)
+            return ext.forward(x, wr, wi, wj, wk, bias, lora_a, lora_b, float(lora_scale),
+                               bool(static_weights))
     in_groups, out_groups = _validate(x, wr, wi, wj, wk)
     if bias is not None and (bias.dim() != 1 or bias.shape[0] != 4 * out_groups):
         raise ValueError(f"bias must be [{4 * out_groups}], got {tuple(bias.shape)}")
@@ -107,9 +131,9 @@ def _forward_impl(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=None, lora_s
     x2, ld_x = _rows(x, K)
     M = x2.shape[0]
     ws, ld_w = _weights((wr, wi, wj, wk))
-    b = bias.contiguous() if bias is not None else None
-    la = lora_a.contiguous() if rank else None
-    lb = lora_b.contiguous() if rank else None
+    b = bias if bias is None or bias.is_contiguous() else bias.contiguous()
+    la = (lora_a if lora_a.is_contiguous() else lora_a.contiguous()) if rank else None
+    lb = (lora_b if lora_b.is_contiguous() else lora_b.contiguous()) if rank else None
     if rank % 8 and x.dtype != torch.float32:
         # The tensor-core path reads B through TMA with rows of rank elements;
         # zero-padding the rank to a multiple of 8 keeps it on that path and
@@ -122,7 +146,7 @@ def _forward_impl(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=None, lora_s
     if M:
         flags = _lib.FLAG_STATIC_WEIGHTS if static_weights else 0
         # the library launches on the current device: switch only when needed
-        if torch.cuda.current_device() == dev.index:
+        if torch._C._cuda_getDevice() == dev.index:
             _lib.forward_raw(x2, ld_x, ws, ld_w, b, la, lb, rank, float(lora_scale), y, 4 * out_groups,
                              M, in_groups, out_groups, int(algo), flags)
         else:
@@ -201,10 +225,10 @@ def fused_quaternion_linear(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=No
     stream writes the weights, bias or LoRA B (inference with fixed weights):
     the kernel may then stream them while the previous kernel finishes.
     """
-    if torch.is_grad_enabled() and any(
-        t is not None and t.requires_grad for t in (x, wr, wi, wj, wk, bias, lora_a, lora_b)
-    ):
-        return _QLinFn.apply(x, wr, wi, wj, wk, bias, lora_a, lora_b, float(lora_scale))
+    if torch.is_grad_enabled():
+        for t in (x, wr, wi, wj, wk, bias, lora_a, lora_b):
+            if t is not None and t.requires_grad:
+                return _QLinFn.apply(x, wr, wi, wj, wk, bias, lora_a, lora_b, float(lora_scale))
     return _forward_impl(x, wr, wi, wj, wk, bias, lora_a, lora_b, lora_scale,
                          static_weights=static_weights)
 

@@ -128,6 +128,10 @@ def test_module_path_keeps_its_workspace_counters_zero(qb, cuda):
         ref = qb.linear._forward_impl(x, *w, None, None, None, 0.0, algo=qb._lib.ALGO_SIMT)
         torch.cuda.synchronize()
         assert (y.float() - ref.float()).abs().max().item() <= 2e-2 * ref.float().abs().max().item()
-    for buf in qb._lib._zeroed_ws.values():
+    bufs = list(qb._lib._zeroed_ws.values())
+    if qb._lib._torch_ext is not None:  # the C++ inference forward keeps its own
+        bufs += qb._lib._torch_ext.workspaces()
+    assert bufs
+    for buf in bufs:
         assert int(buf[:COUNTER_BYTES].count_nonzero()) == 0
     assert qb.device_error(cuda) == 0
