@@ -650,11 +650,22 @@ def main():
         import torch.distributed as tdist
 
         torch.cuda.set_device(local)
-        # keep stdout to the one JSON line: NCCL's version banner only when asked for
+        # keep stdout to the one JSON line: whatever the communicator set-up
+        # prints (NCCL's version banner) goes to stderr
         if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
             os.environ["NCCL_DEBUG"] = "WARN"
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                 device_id=torch.device("cuda", local))
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                     device_id=torch.device("cuda", local))
+            tdist.barrier()
+            torch.cuda.synchronize(local)
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
         dist = tdist
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)

@@ -61,6 +61,7 @@ def _rank_main(rank, port, out_q):
             x = torch.randn(M, fin, generator=g).to(dev, torch.bfloat16)
             want = qb.fused_quaternion_linear(x, full.wr, full.wi, full.wj, full.wk, full.bias, la, lb, scale)
             plain = qb.ColumnParallelQuaternionLinear.from_full(full, lora_A=la, lora_B=lb, lora_scale=scale)
+            plain.fused_allgather = False
             fused = qb.ColumnParallelQuaternionLinear.from_full(full, lora_A=la, lora_B=lb, lora_scale=scale)
             fused.fused_allgather = True
             for _ in range(3):
