@@ -201,7 +201,7 @@ class ClockSampler:
 # device timing
 # ---------------------------------------------------------------------------
 
-def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES, flags=0):
+def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES, flags=0, algo=0):
     """Device copies rotated to exceed L2, preallocated outputs and workspace."""
     dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
     nbytes, _ = algorithmic_work(lay)
@@ -237,12 +237,14 @@ def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES, flags=0):
                                  c["la"].data_ptr() if c["la"] is not None else None,
                                  c["lb"].data_ptr() if c["lb"] is not None else None,
                                  rank, float(lay.lora_scale), y.data_ptr(), 4 * N_g, M, K_g, N_g,
-                                 ws.data_ptr(), ws_bytes, 0, flags, stream_of(dev))
+                                 ws.data_ptr(), ws_bytes, algo, flags, stream_of(dev))
         if st != 0:
             qb._lib.check(st, "qlin_forward")
 
     with torch.cuda.device(dev):
         plan = qb._lib.plan(dt, M, K_g, N_g, rank, flags=flags)
+    if algo == qb._lib.ALGO_TC and plan["algo"] != "tcgen05":
+        plan = {"algo": "tcgen05 (forced)"}
     return call, ncopy, copies, ys, plan
 
 
@@ -256,8 +258,8 @@ def _settle(torch, dev, fn, seconds=0.5):
         torch.cuda.synchronize(dev)
 
 
-def time_device(qb, lay, torch, dev, K, W, dist=None, flags=0):
-    call, ncopy, copies, ys, plan = _device_case(qb, lay, torch, dev, flags=flags)
+def time_device(qb, lay, torch, dev, K, W, dist=None, flags=0, algo=0):
+    call, ncopy, copies, ys, plan = _device_case(qb, lay, torch, dev, flags=flags, algo=algo)
     for i in range(W):
         call(i)
     torch.cuda.synchronize(dev)
@@ -712,6 +714,10 @@ def main():
     # streams its weights while the previous call's kernels finish.
     sms, _, _ = time_device(qb, lay, torch, dev, K, W, dist, flags=qb._lib.FLAG_STATIC_WEIGHTS)
     result["static_weights_us_per_call"] = sms * 1e3 / K / world
+    if plan["algo"] == "gemv":
+        # context: the same calls forced onto the tensor-core kernel
+        tms, _, _ = time_device(qb, lay, torch, dev, K, W, dist, algo=qb._lib.ALGO_TC)
+        result["tensor_core_kernel_us_per_call"] = tms * 1e3 / K / world
 
     e2e_us, h2d, d2h = time_e2e(qb, lay, torch, dev, K, W)
     if dist is not None:

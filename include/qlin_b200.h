@@ -47,14 +47,18 @@ enum {
 enum {
   QLIN_ALGO_AUTO = 0,
   QLIN_ALGO_SIMT = 1,   /* CUDA-core tiled kernel: every dtype, every shape     */
-  QLIN_ALGO_TC = 2      /* TMA + tcgen05/TMEM kernel: bf16/f16, aligned shapes  */
+  QLIN_ALGO_TC = 2,     /* TMA + tcgen05/TMEM kernel: bf16/f16, aligned shapes  */
+  QLIN_ALGO_GEMV = 3    /* CUDA-core decode GEMV: bf16/f16, at most 4 tokens,
+                           K_g a multiple of 8, LoRA rank <= 32 and a multiple
+                           of 4; one launch, no workspace (QLIN_ALGO_AUTO picks
+                           it for at most 2 tokens)                            */
 };
 
 /*
  * Flags of qlin_forward_ex.
  *
  * QLIN_FLAG_STATIC_WEIGHTS: the caller guarantees that no work queued earlier
- * on the stream writes wr..wk, bias or lora_b (inference with fixed
+ * on the stream writes wr..wk, bias, lora_a or lora_b (inference with fixed
  * weights).  The kernels then start streaming the weights while the previous
  * kernel of the stream is still finishing (programmatic dependent launch);
  * x, the workspace and y are still only touched after it completed.

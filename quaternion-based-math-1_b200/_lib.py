@@ -20,7 +20,7 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG_DIR, "lib", "libqlin_b200.so")
 
 F32, BF16, F16 = 0, 1, 2
-ALGO_AUTO, ALGO_SIMT, ALGO_TC = 0, 1, 2
+ALGO_AUTO, ALGO_SIMT, ALGO_TC, ALGO_GEMV = 0, 1, 2, 3
 FLAG_STATIC_WEIGHTS = 1
 FLAG_ZEROED_WORKSPACE = 2
 
@@ -198,7 +198,7 @@ def plan(dtype: torch.dtype, M: int, K_g: int, N_g: int, rank: int, flags: int |
                            *(ctypes.byref(o) for o in outs)),
           "qlin_plan")
     algo, tok, split, launches, resident = (o.value for o in outs)
-    return {"algo": {ALGO_SIMT: "simt", ALGO_TC: "tcgen05"}.get(algo, str(algo)),
+    return {"algo": {ALGO_SIMT: "simt", ALGO_TC: "tcgen05", ALGO_GEMV: "gemv"}.get(algo, str(algo)),
             "tile_tokens": tok, "split_k": split, "launches": launches, "resident_ctas": resident}
 
 

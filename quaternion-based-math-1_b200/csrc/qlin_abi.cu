@@ -16,6 +16,7 @@
 #include <type_traits>
 
 #include "../../include/qlin_b200.h"
+#include "qlin_gemv.cuh"
 #include "qlin_simt.cuh"
 #include "qlin_tc.cuh"
 
@@ -35,6 +36,8 @@ struct DeviceInfo {
   // cluster K split: how many clusters of `split` CTAs fit at once, by
   // [dtype][LoRA mode][split] (-1: not queried yet)
   int cluster_cap[2][3][kTcClusterMax + 1];
+  // CUDA-core decode kernel: shared-memory limit raised, by [dtype][MT][LoRA][peers]
+  bool gemv_attr_set[2][3][2][2] = {};
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mutex;
@@ -178,6 +181,45 @@ bool tc_eligible(int dtype, const void* x, int64_t ld_x, const void* const w[4],
 }
 
 int select_algo(int dtype) { return dtype == QLIN_F32 ? QLIN_ALGO_SIMT : QLIN_ALGO_TC; }
+
+// Tokens up to which QLIN_ALGO_AUTO runs the CUDA-core decode kernel (when
+// eligible) instead of the tensor-core kernel.
+constexpr int64_t kGemvAutoTokens = 2;
+// Largest LoRA rank for which QLIN_ALGO_AUTO runs the decode kernel.
+constexpr int kGemvAutoRank = 32;
+
+// Largest shared memory the decode kernel may ask for (staged x + LoRA slots).
+constexpr size_t kGemvMaxSmem = 200 * 1024;
+
+int gemv_tokens(int64_t M) { return M <= 1 ? 1 : (M <= 2 ? 2 : 4); }
+
+// QLIN_ALGO_AUTO's choice of the decode kernel: at most kGemvAutoTokens
+// tokens and output quaternions for at most one CTA of 8 warps per SM (one
+// wave: every CTA's latency-bound start and end then overlap the others'
+// weight streams; larger layers keep the pipelined tensor-core kernel).
+bool gemv_auto(int64_t M, int64_t N_g, int rank, const DeviceInfo* dev) {
+  return M <= kGemvAutoTokens && rank <= kGemvAutoRank && (N_g + kGemvWarps - 1) / kGemvWarps <= dev->num_sms;
+}
+
+// The CUDA-core decode kernel: 16-bit types, at most kGemvMaxTokens tokens,
+// 16-byte weight pieces (K_g and ld_w multiples of 8, 16-byte aligned
+// weights), 8-byte x quaternions, bias and output stores, LoRA rank at most
+// 32 and a multiple of 4, staged x within kGemvMaxSmem.
+bool gemv_eligible(int dtype, const void* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
+                   const void* bias, const void* lora_a, const void* lora_b, int rank, const void* y,
+                   int64_t ld_y, int64_t M, int64_t K_g) {
+  if (dtype == QLIN_F32 || M > kGemvMaxTokens) return false;
+  if (K_g % 8 != 0 || ld_w % 8 != 0 || ld_x % 4 != 0 || ld_y % 4 != 0) return false;
+  if (!aligned(x, 8) || !aligned(y, 8) || (bias && !aligned(bias, 8))) return false;
+  for (int p = 0; p < 4; ++p)
+    if (!aligned(w[p], 16)) return false;
+  // LoRA: the prologue kernel reads x and lora_a in 16-byte vectors
+  if (rank > 0 && (rank > kGemvMaxRank || rank % 4 != 0 || !aligned(lora_a, 16) || !aligned(lora_b, 8) ||
+                   !aligned(x, 16) || ld_x % 8 != 0))
+    return false;
+  const int nch = (int)((K_g + kGemvChunk - 1) / kGemvChunk);
+  return gemv_smem_bytes(gemv_tokens(M), nch, rank > 0) <= kGemvMaxSmem;
+}
 
 CUresult encode(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* base, const cuuint64_t* dims,
                 const cuuint64_t* strides, const cuuint32_t* box,
@@ -471,7 +513,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
     }
   }
   // 3. main kernel (+ split-K reduction)
-  TcParams prm;
+  TcParams prm{};
   prm.x = x;
   prm.ld_x = ld_x;
   prm.bias = bias;
@@ -539,6 +581,99 @@ int run_simt(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], 
   return QLIN_OK;
 }
 
+template <typename T, int MT, bool LORA, bool PEERS>
+int launch_gemv(DeviceInfo* dev, GemvParams prm, cudaStream_t stream) {
+  auto kernel = qlin_gemv_kernel<T, MT, LORA, PEERS>;
+  const size_t smem = gemv_smem_bytes(MT, prm.nch, LORA);
+  const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
+  const int ti = MT == 1 ? 0 : (MT == 2 ? 1 : 2);
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!dev->gemv_attr_set[di][ti][LORA][PEERS]) {
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvMaxSmem) !=
+          cudaSuccess)
+        return QLIN_ERR_LAUNCH;
+      dev->gemv_attr_set[di][ti][LORA][PEERS] = true;
+    }
+  }
+  // one output quaternion per row warp, 8 row warps (+ the LoRA warp) per CTA;
+  // with LoRA a programmatic dependent of this call's prologue
+  const int64_t blocks = (prm.N_g + kGemvWarps - 1) / kGemvWarps;
+  if (blocks > INT32_MAX) return QLIN_ERR_SHAPE;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks, 1, 1);
+  cfg.blockDim = dim3(LORA ? kGemvLoraThreads : kGemvThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, prm) == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+}
+
+template <typename T, int MT>
+int launch_gemv_mt(DeviceInfo* dev, const GemvParams& prm, bool peers, cudaStream_t stream) {
+  if (prm.rank > 0)
+    return peers ? launch_gemv<T, MT, true, true>(dev, prm, stream) : launch_gemv<T, MT, true, false>(dev, prm, stream);
+  return peers ? launch_gemv<T, MT, false, true>(dev, prm, stream) : launch_gemv<T, MT, false, false>(dev, prm, stream);
+}
+
+// CUDA-core decode kernel (one launch, no workspace).
+template <typename T>
+int run_gemv(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
+             const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y, int64_t ld_y, int64_t M,
+             int64_t K_g, int64_t N_g, uint8_t* ws, int flags, const PeerOut& peers, cudaStream_t stream) {
+  GemvParams prm{};
+  prm.x = x;
+  prm.ld_x = ld_x;
+  for (int p = 0; p < 4; ++p) prm.w[p] = w[p];
+  prm.ld_w = ld_w;
+  prm.bias = bias;
+  prm.lora_a = rank > 0 ? lora_a : nullptr;
+  prm.lora_b = rank > 0 ? lora_b : nullptr;
+  prm.rank = rank;
+  prm.lora_scale = lora_scale;
+  prm.y = y;
+  prm.ld_y = ld_y;
+  prm.M = (int)M;
+  prm.K_g = (int)K_g;
+  prm.N_g = (int)N_g;
+  prm.nch = (int)((K_g + kGemvChunk - 1) / kGemvChunk);
+  prm.static_weights = (flags & QLIN_FLAG_STATIC_WEIGHTS) ? 1 : 0;
+  prm.peers = peers;
+  prm.t = nullptr;
+  prm.ld_t = 0;
+  if (rank > 0) {
+    // the scaled LoRA down projection t from the prologue kernel, in the
+    // workspace (the same piece the tensor-core path uses)
+    if (!ws) return QLIN_ERR_WORKSPACE;
+    const WsLayout L = ws_layout(QLIN_BF16, M, K_g, N_g, rank);
+    T* t = reinterpret_cast<T*>(ws + L.t_off);
+    cudaLaunchAttribute pattr;
+    pattr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pattr.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t pc = {};
+    pc.gridDim = dim3((unsigned)(((M + 7) / 8) * rank), 1, 1);
+    pc.blockDim = dim3(256, 1, 1);
+    pc.stream = stream;
+    pc.attrs = &pattr;
+    pc.numAttrs = 1;
+    if (cudaLaunchKernelEx(&pc, qlin_prologue_kernel<T, 1>, x, ld_x, static_cast<T*>(nullptr), M, K_g,
+                           (int64_t)0, lora_a, rank, lora_scale, t, L.ld_t) != cudaSuccess)
+      return QLIN_ERR_LAUNCH;
+    prm.t = t;
+    prm.ld_t = L.ld_t;
+  }
+  const bool pe = peers.n > 0;
+  switch (gemv_tokens(M)) {
+    case 1: return launch_gemv_mt<T, 1>(dev, prm, pe, stream);
+    case 2: return launch_gemv_mt<T, 2>(dev, prm, pe, stream);
+    default: return launch_gemv_mt<T, 4>(dev, prm, pe, stream);
+  }
+}
+
 template <typename T>
 int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void* const w[4],
              int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b, int rank,
@@ -555,6 +690,9 @@ int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void*
     return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
                        stream);
   } else {
+    if (algo == QLIN_ALGO_GEMV)
+      return run_gemv<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws, flags,
+                         peers, stream);
     if (algo == QLIN_ALGO_TC)
       return run_tc<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
                        flags, peers, stream);
@@ -595,7 +733,7 @@ static int forward_common(int dtype, const void* x, int64_t ld_x, const void* wr
   int st = validate(dtype, x, ld_x, wr, wi, wj, wk, ld_w, lora_a, lora_b, rank, y, ld_y, M, K_g, N_g);
   if (st != QLIN_OK) return st;
   if (M == 0) return QLIN_OK;
-  if (algo < QLIN_ALGO_AUTO || algo > QLIN_ALGO_TC) return QLIN_ERR_ARG;
+  if (algo < QLIN_ALGO_AUTO || algo > QLIN_ALGO_GEMV) return QLIN_ERR_ARG;
   if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE)) return QLIN_ERR_ARG;
   if (rank == 0) lora_a = lora_b = nullptr;
   DeviceInfo* dev = nullptr;
@@ -604,11 +742,17 @@ static int forward_common(int dtype, const void* x, int64_t ld_x, const void* wr
   const void* w[4] = {wr, wi, wj, wk};
   if (algo == QLIN_ALGO_AUTO) {
     algo = select_algo(dtype);
-    if (algo == QLIN_ALGO_TC &&
-        !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g))
+    if (algo == QLIN_ALGO_TC && gemv_auto(M, N_g, rank, dev) &&
+        gemv_eligible(dtype, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, y, ld_y, M, K_g))
+      algo = QLIN_ALGO_GEMV;
+    else if (algo == QLIN_ALGO_TC &&
+             !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g))
       algo = QLIN_ALGO_SIMT;
   } else if (algo == QLIN_ALGO_TC &&
              !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g)) {
+    return QLIN_ERR_ALIGN;
+  } else if (algo == QLIN_ALGO_GEMV &&
+             !gemv_eligible(dtype, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, y, ld_y, M, K_g)) {
     return QLIN_ERR_ALIGN;
   }
   const WsLayout L = ws_layout(dtype, M, K_g, N_g, rank);
@@ -677,10 +821,23 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flag
   DeviceInfo* dev = nullptr;
   int st = device_info(&dev);
   if (st != QLIN_OK) return st;
-  const int a = (dtype == QLIN_F32 || K_g % 8 != 0 || (rank > 0 && rank % 8 != 0)) ? QLIN_ALGO_SIMT
-                                                                                     : QLIN_ALGO_TC;
+  int a = (dtype == QLIN_F32 || K_g % 8 != 0 || (rank > 0 && rank % 8 != 0)) ? QLIN_ALGO_SIMT
+                                                                               : QLIN_ALGO_TC;
+  if (a == QLIN_ALGO_TC && gemv_auto(M, N_g, rank, dev) && rank <= kGemvMaxRank && rank % 4 == 0 &&
+      gemv_smem_bytes(gemv_tokens(M), (int)((K_g + kGemvChunk - 1) / kGemvChunk), rank > 0) <= kGemvMaxSmem)
+    a = QLIN_ALGO_GEMV;
   int nt = 0, sp = 1, res = 0, nl = 0;
-  if (a == QLIN_ALGO_TC) {
+  if (a == QLIN_ALGO_GEMV) {
+    nt = gemv_tokens(M);
+    nl = rank > 0 ? 2 : 1;  // LoRA: the down-projection prologue, then the decode kernel
+    int per_sm = 0;
+    const size_t smem = gemv_smem_bytes(nt, (int)((K_g + kGemvChunk - 1) / kGemvChunk), rank > 0);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qlin_gemv_kernel<__nv_bfloat16, 1, false, false>,
+                                                      kGemvThreads, smem) != cudaSuccess)
+      per_sm = 0;
+    cudaGetLastError();
+    res = per_sm * dev->num_sms;
+  } else if (a == QLIN_ALGO_TC) {
     nt = n_tok_for(M);
     const bool bf = dtype == QLIN_BF16;
     switch (nt) {
@@ -746,7 +903,7 @@ int qlin_forward_allgather(int dtype, const void* x, int64_t ld_x, const void* w
     if (q != world_rank) peers.y[peers.n++] = static_cast<uint8_t*>(outs[q]) + col_offset * 2;
   void* y = static_cast<uint8_t*>(outs[world_rank]) + col_offset * 2;
   int st = forward_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
-                          ld_out, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_TC, flags, stream, peers);
+                          ld_out, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_AUTO, flags, stream, peers);
   if (st != QLIN_OK || M == 0 || world == 1) return st;
   PeerFlags pf;
   for (int q = 0; q < world; ++q) pf.f[q] = flag_arrays[q];

@@ -1,0 +1,305 @@
+// Decode-sized quaternion linear forward on CUDA cores (sm_100a): a
+// memory-bound GEMV for at most MT tokens.
+//
+// Every row warp owns one output quaternion o and walks the whole input
+// width: lane l reads the 16-byte pieces W_p[o, 256c + 8l .. +8) of the four
+// weight components (128-bit coalesced loads, a warp reads 512 contiguous
+// bytes of one row per component and chunk c), so each weight byte crosses
+// HBM exactly once and no K split (partials, counters, reduction) is needed.
+// All chunks' loads of a row are in flight at once (kGemvDepth chunks of 256
+// input quaternions, refilled as each is consumed), issued before the
+// dependency wait when the caller declared the weights static.
+//
+// The Hamilton product of weight quaternion w = (w0, w1, w2, w3) with input
+// quaternion x gives all four output components from one set of loads
+// (reference quaternion/reference.py:31-45, the 4x4 sign table of
+// quaternion/packing.py:18-21):
+//   y0 += w0 x0 - w1 x1 - w2 x2 - w3 x3      y1 += w0 x1 + w1 x0 + w2 x3 - w3 x2
+//   y2 += w0 x2 - w1 x3 + w2 x0 + w3 x1      y3 += w0 x3 + w1 x2 - w2 x1 + w3 x0
+// in fp32; the 32 lanes' sums are combined by warp shuffles and rounded once
+// with bias and LoRA.  x is staged once per CTA in shared memory as fp32
+// quaternions, laid out so that a warp's reads of one chunk are
+// conflict-free: float4 index ((m * nch + c) * 8 + j) * 32 + (l ^ j) holds
+// input quaternion 256c + 8l + j of token m.
+//
+// LoRA (rank <= 32): y += lora_scale * B (A x).  The scaled down projection
+// t = lora_scale * A x needs every input, so this call's prologue kernel
+// computes it (qlin_prologue_kernel) and this kernel is its programmatic
+// dependent: the prologue lets it launch only after waiting for all earlier
+// work of the stream, so the row warps read weights and x at once, and one
+// more warp per CTA, the LoRA warp, waits for the prologue, reads t and
+// publishes it in shared memory at a named barrier that the row warps meet
+// only after their weight stream.
+#pragma once
+
+#include "qlin_common.cuh"
+
+namespace qlin {
+
+constexpr int kGemvWarps = 8;                // row warps (output quaternions) per CTA
+constexpr int kGemvThreads = 32 * kGemvWarps;
+constexpr int kGemvLoraThreads = kGemvThreads + 32;  // + the LoRA warp
+constexpr int kGemvChunk = 256;              // input quaternions per chunk (8 per lane)
+constexpr int kGemvDepth = 4;                // chunks of one row in flight per lane
+constexpr int kGemvMaxRank = 32;
+constexpr int kGemvMaxTokens = 4;
+constexpr int kGemvLoraBar = 1;              // named barrier: row warps + LoRA warp
+
+struct GemvParams {
+  const void* x;
+  int64_t ld_x;
+  const void* w[4];
+  int64_t ld_w;
+  const void* bias;    // [4*N_g] or null
+  const void* lora_a;  // [rank, 4*K_g] or null
+  const void* lora_b;  // [4*N_g, rank] or null
+  int rank;
+  float lora_scale;
+  void* y;
+  int64_t ld_y;
+  int M, K_g, N_g;
+  int nch;             // ceil(K_g / kGemvChunk)
+  const void* t;       // LoRA: scaled down projection [M, ld_t] from this call's prologue
+  int64_t ld_t;
+  int static_weights;  // weights, bias, LoRA A/B not written by earlier work on the stream
+  PeerOut peers;       // column-partitioned layer: every output also stored to these
+};
+
+// Dynamic shared memory of one CTA: staged x, then (LoRA) t [MT][kGemvMaxRank] fp32.
+__host__ __device__ constexpr size_t gemv_smem_bytes(int mt, int nch, bool lora) {
+  return (size_t)mt * nch * kGemvChunk * 16 + (lora ? (size_t)mt * kGemvMaxRank * 4 : 0);
+}
+
+// Eight 16-bit values (16 bytes) -> fp32.
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const T* h = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = to_f32(h[i]);
+}
+
+// Loads of the weights, x, bias, LoRA B and t: L2 only (ld.global.cg) --
+// each CTA reads them once, nothing is gained by allocating them in L1 --
+// and, through the memory clobber, kept in program order with the
+// dependency wait (griddepcontrol.wait, also a memory-clobbering asm).
+__device__ __forceinline__ uint4 ld_w_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+__device__ __forceinline__ uint2 ld_cg_v2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.cg.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
+  return r;
+}
+__device__ __forceinline__ unsigned short ld_cg_u16(const void* p) {
+  unsigned short r;
+  asm volatile("ld.global.cg.u16 %0, [%1];" : "=h"(r) : "l"(p) : "memory");
+  return r;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+template <typename T, int MT, bool LORA, bool PEERS>
+__global__ void __launch_bounds__(kGemvLoraThreads, 1)
+qlin_gemv_kernel(const GemvParams prm) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  float4* xs = reinterpret_cast<float4*>(smem_raw);
+  float* tsum = reinterpret_cast<float*>(smem_raw + (size_t)MT * prm.nch * kGemvChunk * 16);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nthr = blockDim.x;
+  const bool lora_warp = LORA && warp == kGemvWarps;
+  const int o = blockIdx.x * kGemvWarps + warp;  // this row warp's output quaternion
+  const bool row_ok = !lora_warp && o < prm.N_g;
+  const int nch = prm.nch;
+
+  pdl_launch_dependents();
+
+  // ---- row warps: weights, bias, LoRA B ----
+  uint4 wv[kGemvDepth][4];
+  auto load_chunk = [&](int d, int c) {
+    const int i = c * kGemvChunk + 8 * lane;
+    const bool ok = row_ok && c < nch && i < prm.K_g;
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+      wv[d][p] = ok ? ld_w_v4(reinterpret_cast<const T*>(prm.w[p]) + (int64_t)o * prm.ld_w + i)
+                    : make_uint4(0u, 0u, 0u, 0u);
+  };
+  uint2 braw = make_uint2(0u, 0u);   // lane 0: bias of the 4 components
+  uint2 lb = make_uint2(0u, 0u);     // LoRA B[4o + (lane>>3)][4*(lane&7) .. +4)
+  const int lb_r = 4 * (lane & 7);
+  auto load_small = [&]() {
+    if (row_ok && lane == 0 && prm.bias)
+      braw = ld_cg_v2(reinterpret_cast<const T*>(prm.bias) + 4 * (int64_t)o);
+    if (LORA && row_ok && lb_r < prm.rank)
+      lb = ld_cg_v2(reinterpret_cast<const T*>(prm.lora_b) + (4 * (int64_t)o + (lane >> 3)) * prm.rank + lb_r);
+  };
+  // Without LoRA this kernel follows the previous kernel of the stream and
+  // waits for it before reading what it may have written (weights first when
+  // they are static).  With LoRA it follows this call's prologue, whose
+  // launch of it implies that all earlier work is complete: no wait before
+  // the weights and x, only the LoRA warp waits, for t.
+  if (!LORA && prm.static_weights) {
+#pragma unroll
+    for (int d = 0; d < kGemvDepth; ++d) load_chunk(d, d);
+    load_small();
+  }
+  if (!LORA) pdl_wait_prior();
+  if (LORA || !prm.static_weights) {
+    if (!lora_warp) {
+#pragma unroll
+      for (int d = 0; d < kGemvDepth; ++d) load_chunk(d, d);
+      load_small();
+    }
+  }
+
+  // ---- stage x as fp32 quaternions (zeros past K_g and past M) ----
+  // Item q = (token m, input quaternion i) with i running over all chunks;
+  // thread tid converts items tid, tid + blockDim, ...  All of a batch's
+  // loads are issued before any is stored.
+  {
+    const T* __restrict__ x = reinterpret_cast<const T*>(prm.x);
+    const int nq = nch * kGemvChunk, items = MT * nq;
+    for (int b0 = 0; b0 < items; b0 += 8 * nthr) {
+      uint2 raw[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int q = b0 + u * nthr + tid, m = q / nq, i = q - m * nq;
+        raw[u] = (q < items && m < prm.M && i < prm.K_g)
+                     ? ld_cg_v2(x + (int64_t)m * prm.ld_x + 4 * (int64_t)i)
+                     : make_uint2(0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int q = b0 + u * nthr + tid;
+        if (q < items) {
+          const T* h = reinterpret_cast<const T*>(&raw[u]);
+          const int m = q / nq, i = q - m * nq;
+          const int c = i / kGemvChunk, l = (i / 8) & 31, j = i & 7;
+          xs[((m * nch + c) * 8 + j) * 32 + (l ^ j)] =
+              make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  if constexpr (LORA) {
+    if (lora_warp) {
+      // ---------------- LoRA warp ----------------
+      pdl_wait_prior();  // the prologue's t is complete
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        float v = 0.f;
+        if (m < prm.M && lane < prm.rank) {
+          const unsigned short h = ld_cg_u16(reinterpret_cast<const T*>(prm.t) + m * prm.ld_t + lane);
+          v = to_f32(*reinterpret_cast<const T*>(&h));
+        }
+        tsum[m * kGemvMaxRank + lane] = v;
+      }
+      __syncwarp();
+      named_bar_arrive(kGemvLoraBar, kGemvLoraThreads);  // t is in shared memory
+      return;
+    }
+  }
+
+  // ---- row warps: the Hamilton product over all input quaternions ----
+  float acc[MT][4];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int a = 0; a < 4; ++a) acc[m][a] = 0.f;
+  for (int cb = 0; cb < nch; cb += kGemvDepth) {
+#pragma unroll
+    for (int d = 0; d < kGemvDepth; ++d) {
+      const int c = cb + d;
+      if (c < nch) {
+        float w0[8], w1[8], w2[8], w3[8];
+        unpack8<T>(wv[d][0], w0);
+        unpack8<T>(wv[d][1], w1);
+        unpack8<T>(wv[d][2], w2);
+        unpack8<T>(wv[d][3], w3);
+        // refill: the chunk kGemvDepth further on reuses these registers
+        if (c + kGemvDepth < nch) load_chunk(d, c + kGemvDepth);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          const float4* xp = xs + ((m * nch + c) * 8) * 32;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 v = xp[j * 32 + (lane ^ j)];
+            float y0 = acc[m][0], y1 = acc[m][1], y2 = acc[m][2], y3 = acc[m][3];
+            y0 = fmaf(w0[j], v.x, y0); y0 = fmaf(-w1[j], v.y, y0); y0 = fmaf(-w2[j], v.z, y0); y0 = fmaf(-w3[j], v.w, y0);
+            y1 = fmaf(w0[j], v.y, y1); y1 = fmaf(w1[j], v.x, y1); y1 = fmaf(w2[j], v.w, y1); y1 = fmaf(-w3[j], v.z, y1);
+            y2 = fmaf(w0[j], v.z, y2); y2 = fmaf(-w1[j], v.w, y2); y2 = fmaf(w2[j], v.x, y2); y2 = fmaf(w3[j], v.y, y2);
+            y3 = fmaf(w0[j], v.w, y3); y3 = fmaf(w1[j], v.z, y3); y3 = fmaf(-w2[j], v.y, y3); y3 = fmaf(w3[j], v.x, y3);
+            acc[m][0] = y0; acc[m][1] = y1; acc[m][2] = y2; acc[m][3] = y3;
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int s = 16; s >= 1; s >>= 1) acc[m][a] += __shfl_xor_sync(0xffffffffu, acc[m][a], s);
+
+  // ---- LoRA up projection: lane l takes component l>>3, ranks 4(l&7)..+3 ----
+  float lora[MT][4];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int a = 0; a < 4; ++a) lora[m][a] = 0.f;
+  if constexpr (LORA) {
+    named_bar_sync(kGemvLoraBar, kGemvLoraThreads);  // the LoRA warp has written t
+    const T* bh = reinterpret_cast<const T*>(&lb);
+    float part[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float4 t = *reinterpret_cast<const float4*>(tsum + m * kGemvMaxRank + lb_r);
+      float s = to_f32(bh[0]) * t.x;
+      s = fmaf(to_f32(bh[1]), t.y, s);
+      s = fmaf(to_f32(bh[2]), t.z, s);
+      s = fmaf(to_f32(bh[3]), t.w, s);
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      part[m] = s;  // lanes 8a..8a+7 hold component a (t carries lora_scale)
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int a = 0; a < 4; ++a) lora[m][a] = __shfl_sync(0xffffffffu, part[m], 8 * a);
+  }
+
+  // ---- epilogue: lane 0 adds bias and LoRA, rounds once, stores 8 bytes per token ----
+  if (row_ok && lane == 0) {
+    const T* bh = reinterpret_cast<const T*>(&braw);
+    float b[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) b[a] = to_f32(bh[a]);
+    T* __restrict__ y = reinterpret_cast<T*>(prm.y);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m < prm.M)
+        store_out<T, PEERS>(y, prm.peers, (int64_t)m * prm.ld_y + 4 * (int64_t)o,
+                            pack4<T>(acc[m][0] + lora[m][0] + b[0], acc[m][1] + lora[m][1] + b[1],
+                                     acc[m][2] + lora[m][2] + b[2], acc[m][3] + lora[m][3] + b[3]));
+    }
+  }
+  // Outputs stored to peers are performed at system scope before the CTA
+  // ends, so the barrier kernel that follows may signal them.
+  if (PEERS) fence_sys();
+}
+
+}  // namespace qlin

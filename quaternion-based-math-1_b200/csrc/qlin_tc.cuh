@@ -322,7 +322,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     if (!kBuilt) tma_prefetch_desc(&map_x);
     if (LORA != kLoraPrologue) tma_prefetch_desc(&map_la);
     // With static weights the caller guarantees that no earlier work on the
-    // stream writes the weights, bias or LoRA B, so their first tiles are
+    // stream writes the weights, bias or LoRA A/B, so their first tiles are
     // requested before waiting for that work.
     if (early) issue_pre_weights();
   }

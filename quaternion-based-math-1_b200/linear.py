@@ -222,7 +222,7 @@ def fused_quaternion_linear(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=No
     """``quaternion_linear(x) + bias + lora_scale * (x A^T) B^T`` in one device call.
 
     ``static_weights=True`` declares that nothing queued earlier on the current
-    stream writes the weights, bias or LoRA B (inference with fixed weights):
+    stream writes the weights, bias or LoRA A/B (inference with fixed weights):
     the kernel may then stream them while the previous kernel finishes.
     """
     if torch.is_grad_enabled():

@@ -17,18 +17,19 @@ pytestmark = pytest.mark.gpu
 
 FLAG_ZEROED = 2
 COUNTER_BYTES = 4096
+ALGO_AUTO, ALGO_TC = 0, 2  # the fused reduction is a property of the tensor-core kernel
 
 def _ptr(t):
     return None if t is None else t.data_ptr()
 
-def _call(qb, d, y, M, K_g, N_g, rank, ws, flags):
+def _call(qb, d, y, M, K_g, N_g, rank, ws, flags, algo=ALGO_TC):
     lib = qb._lib.load()
     n = qb._lib.workspace_size(d["x"].dtype, M, K_g, N_g, rank)
     assert ws is None or ws.numel() >= n
     return lib.qlin_forward_ex(qb._lib.dtype_code(d["x"].dtype), _ptr(d["x"]), 4 * K_g,
                                *(_ptr(w) for w in d["w"]), K_g, _ptr(d["bias"]), _ptr(d["lora_a"]),
                                _ptr(d["lora_b"]), rank, float(d["scale"]), _ptr(y), 4 * N_g, M, K_g,
-                               N_g, _ptr(ws), n, 0, flags, qb._lib.stream_handle(d["x"].device))
+                               N_g, _ptr(ws), n, algo, flags, qb._lib.stream_handle(d["x"].device))
 
 def _both(qb, workloads, cuda, dtype, M, K, N, seed, rank, bias, zeroed_ws):
     lay = workloads.make_layer(dtype, M, K, N, seed, bias=bias, lora_rank=rank, lora_std=0.02)
@@ -63,10 +64,18 @@ def test_one_zeroed_workspace_serves_a_sequence_of_problems(qb, workloads, cuda)
     # ones keep finding zero counters
     ws = torch.zeros(8 << 20, dtype=torch.uint8, device=cuda)
     seq = [(1, 1024, 1024, 0), (100, 512, 512, 16), (2, 4096, 512, 0), (4, 1024, 4096, 32),
-           (1, 1024, 1024, 0), (70, 1024, 256, 0), (3, 2048, 2048, 8), (1, 1024, 1024, 0)]
+           (1, 1024, 1024, 32), (70, 1024, 256, 0), (3, 2048, 2048, 8), (2, 4096, 4096, 16),
+           (1, 1024, 1024, 0)]
     for i, (M, K, N, rank) in enumerate(seq):
-        _, y_f, y_r = _both(qb, workloads, cuda, "bf16", M, K, N, 200 + i, rank, "normal", ws)
+        lay, y_f, y_r = _both(qb, workloads, cuda, "bf16", M, K, N, 200 + i, rank, "normal", ws)
         assert torch.equal(y_f, y_r), (M, K, N, rank)
+        assert int(ws[:COUNTER_BYTES].count_nonzero()) == 0
+        # the automatic choice on the same workspace (the decode kernel, whose
+        # LoRA partials meet through the workspace, for 1-2 tokens)
+        y_a = torch.empty_like(y_f)
+        assert _call(qb, to_device(lay, cuda), y_a, M, K // 4, N // 4, rank, ws, FLAG_ZEROED, ALGO_AUTO) == 0
+        torch.cuda.synchronize()
+        assert ((y_a.float() - y_r.float()).norm() / y_r.float().norm()).item() <= 4e-3
         assert int(ws[:COUNTER_BYTES].count_nonzero()) == 0
     assert qb.device_error(cuda) == 0
 
@@ -104,19 +113,14 @@ def test_plan_counts_the_fused_reduction(qb, cuda):
     # above four tokens the separate reduction kernel stays
     p5 = qb._lib.plan(torch.bfloat16, 5, 1024, 1024, 0, flags=FLAG_ZEROED)
     assert p5["launches"] == 2
-    # one or two tokens: an 8-way split summed inside a thread-block cluster,
-    # one launch whatever the workspace (static weights without LoRA keep the
-    # wider split and the workspace paths)
+    # one or two tokens: the CUDA-core decode kernel, no K split, whatever
+    # the flags; one launch, two with LoRA (the down-projection prologue)
     for M in (1, 2):
-        for rank in (0, 32):
-            p = qb._lib.plan(torch.bfloat16, M, 1024, 1024, rank, flags=0)
-            assert p["split_k"] == 8 and p["launches"] == 1, (M, rank, p)
-    ps = qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 0, flags=1)
-    assert ps["split_k"] == 16 and ps["launches"] == 2
-    assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 0, flags=1 | FLAG_ZEROED)["launches"] == 1
-    # the module path uses the zeroed workspace for decode-sized calls, and a
-    # rank <= 32 LoRA down projection runs inside the main kernel: one launch
-    assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 32)["launches"] == 1
+        for flags in (0, 1, FLAG_ZEROED, 1 | FLAG_ZEROED):
+            for rank in (0, 32):
+                p = qb._lib.plan(torch.bfloat16, M, 1024, 1024, rank, flags=flags)
+                assert p["algo"] == "gemv" and p["split_k"] == 1, (M, flags, rank, p)
+                assert p["launches"] == (2 if rank else 1), (M, flags, rank, p)
 
 
 def test_module_path_keeps_its_workspace_counters_zero(qb, cuda):

@@ -43,7 +43,7 @@ def _reference(qb, layers, x):
     return x
 
 
-@pytest.mark.parametrize("M,lora", [(1, False), (16, True), (100, False), (200, True)])
+@pytest.mark.parametrize("M,lora", [(1, False), (1, True), (2, True), (16, True), (100, False), (200, True)])
 @pytest.mark.parametrize("static", [False, True])
 def test_dependent_chain_eager_and_graph(qb, cuda, M, lora, static):
     layers, x = _layers(qb, cuda, 12, 512, M, lora)
@@ -84,12 +84,93 @@ def test_weight_update_right_before_call_is_seen(qb, cuda, M):
     assert not torch.equal(y1, y2)
 
 
+@pytest.mark.parametrize("M2,lora", [(1, False), (1, True), (2, False), (16, False), (130, False)])
+def test_weights_written_by_the_previous_call_are_seen(qb, cuda, M2, lora):
+    # call 1 (a decode call of this library) writes its output into the buffer
+    # that call 2 reads as its weight wr; call 2 is launched right behind it
+    # and must not read wr before call 1 has finished (no static weights)
+    g = torch.Generator().manual_seed(9)
+    w1 = [(torch.randn(1024, 256, generator=g) / 32).to(cuda, torch.bfloat16) for _ in range(4)]
+    x1 = torch.randn(1, 1024, generator=g).to(cuda, torch.bfloat16)
+    wr2 = torch.empty(1, 4096, dtype=torch.bfloat16, device=cuda)  # call 1's output = call 2's wr [64, 64]
+    w2 = [(torch.randn(64, 64, generator=g) / 16).to(cuda, torch.bfloat16) for _ in range(3)]
+    x2 = torch.randn(M2, 256, generator=g).to(cuda, torch.bfloat16)
+    la = lb = None
+    if lora:
+        la = (torch.randn(16, 256, generator=g) * 0.05).to(cuda, torch.bfloat16)
+        lb = (torch.randn(256, 16, generator=g) * 0.05).to(cuda, torch.bfloat16)
+    scale = 2.0 if lora else 0.0
+
+    def two_calls():
+        wr2.zero_()
+        y1 = qb.fused_quaternion_linear(x1, *w1)
+        wr2.copy_(y1)  # (a copy kernel in between, as a framework would issue)
+        return qb.fused_quaternion_linear(x2, wr2.view(64, 64), *w2, None, la, lb, scale)
+
+    def two_calls_direct():
+        wr2.zero_()
+        # call 1 stores straight into wr2: call 2 directly follows the kernel
+        # that writes its weights (a programmatic dependent launch)
+        ws, ld = qb.linear._weights(tuple(w1))
+        qb._lib.forward_raw(x1, 1024, ws, ld, None, None, None, 0, 0.0, wr2, 4096, 1, 256, 1024)
+        return qb.fused_quaternion_linear(x2, wr2.view(64, 64), *w2, None, la, lb, scale)
+
+    y1 = qb.fused_quaternion_linear(x1, *w1)
+    torch.cuda.synchronize()
+    want = qb.fused_quaternion_linear(x2, y1.view(64, 64).clone(), *w2, None, la, lb, scale)
+    torch.cuda.synchronize()
+    for fn in (two_calls, two_calls_direct):
+        for _ in range(3):
+            got = fn()
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), fn.__name__
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = fn()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, want), fn.__name__
+        del graph
+    assert qb.device_error(cuda) == 0
+
+
+@pytest.mark.parametrize("M,lora", [(1, False), (1, True), (2, False), (16, True), (130, False)])
+def test_inputs_rewritten_every_replay_are_seen(qb, cuda, M, lora):
+    # a graph whose first node rewrites x0 in place every replay, then two
+    # calls where call 2 reads call 1's output as its input: every replay's
+    # outputs must follow the new x0 (no stale cached lines of an earlier
+    # replay's values)
+    layers, x0 = _layers(qb, cuda, 2, 512, M, lora)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        _chain(qb, layers, x0, False)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        x0.mul_(-1.5)
+        out = _chain(qb, layers, x0, False)
+    for _ in range(4):
+        graph.replay()
+        torch.cuda.synchronize()
+        want = _reference(qb, layers, x0.clone())
+        assert torch.equal(out, want)
+    del graph
+    assert qb.device_error(cuda) == 0
+
+
 def test_plan_reports_the_decode_split(qb, cuda):
-    # one kernel: the LoRA rank <= 32 down projection runs inside it and its
-    # 8-way K split is summed inside a thread-block cluster, whatever the
-    # workspace; without LoRA the same.  A rank-64 LoRA adds the prologue.
+    # decode calls: the CUDA-core decode kernel, after the LoRA down-projection
+    # prologue when there is a rank <= 32 LoRA; a rank-64 LoRA goes to the
+    # tensor-core kernel and its prologue
     plan = qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 32, flags=0)
-    assert plan["algo"] == "tcgen05" and plan["tile_tokens"] == 16
-    assert plan["split_k"] == 8 and plan["launches"] == 1
+    assert plan["algo"] == "gemv" and plan["tile_tokens"] == 1
+    assert plan["split_k"] == 1 and plan["launches"] == 2
     assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 64, flags=0)["launches"] == 2
     assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 0, flags=0)["launches"] == 1
