@@ -614,10 +614,9 @@ int launch_gemv(DeviceInfo* dev, GemvParams prm, cudaStream_t stream) {
 }
 
 template <typename T, int MT>
-int launch_gemv_mt(DeviceInfo* dev, const GemvParams& prm, bool peers, cudaStream_t stream) {
-  if (prm.rank > 0)
-    return peers ? launch_gemv<T, MT, true, true>(dev, prm, stream) : launch_gemv<T, MT, true, false>(dev, prm, stream);
-  return peers ? launch_gemv<T, MT, false, true>(dev, prm, stream) : launch_gemv<T, MT, false, false>(dev, prm, stream);
+int launch_gemv_mt(DeviceInfo* dev, const GemvParams& prm, cudaStream_t stream) {
+  return prm.rank > 0 ? launch_gemv<T, MT, true, false>(dev, prm, stream)
+                      : launch_gemv<T, MT, false, false>(dev, prm, stream);
 }
 
 // CUDA-core decode kernel (one launch, no workspace).
@@ -666,11 +665,10 @@ int run_gemv(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], 
     prm.t = t;
     prm.ld_t = L.ld_t;
   }
-  const bool pe = peers.n > 0;
   switch (gemv_tokens(M)) {
-    case 1: return launch_gemv_mt<T, 1>(dev, prm, pe, stream);
-    case 2: return launch_gemv_mt<T, 2>(dev, prm, pe, stream);
-    default: return launch_gemv_mt<T, 4>(dev, prm, pe, stream);
+    case 1: return launch_gemv_mt<T, 1>(dev, prm, stream);
+    case 2: return launch_gemv_mt<T, 2>(dev, prm, stream);
+    default: return launch_gemv_mt<T, 4>(dev, prm, stream);
   }
 }
 
@@ -690,6 +688,8 @@ int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void*
     return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
                        stream);
   } else {
+    // peer outputs (the fused all-gather) are written by the tensor-core kernel only
+    if (algo == QLIN_ALGO_GEMV && peers.n > 0) return QLIN_ERR_ALIGN;
     if (algo == QLIN_ALGO_GEMV)
       return run_gemv<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws, flags,
                          peers, stream);
@@ -903,7 +903,7 @@ int qlin_forward_allgather(int dtype, const void* x, int64_t ld_x, const void* w
     if (q != world_rank) peers.y[peers.n++] = static_cast<uint8_t*>(outs[q]) + col_offset * 2;
   void* y = static_cast<uint8_t*>(outs[world_rank]) + col_offset * 2;
   int st = forward_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
-                          ld_out, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_AUTO, flags, stream, peers);
+                          ld_out, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_TC, flags, stream, peers);
   if (st != QLIN_OK || M == 0 || world == 1) return st;
   PeerFlags pf;
   for (int q = 0; q < world; ++q) pf.f[q] = flag_arrays[q];

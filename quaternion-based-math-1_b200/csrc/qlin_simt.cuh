@@ -246,28 +246,44 @@ qlin_prologue_kernel(const T* __restrict__ x, int64_t ld_x, T* __restrict__ xp, 
   for (int t = 0; t < TT; ++t)
 #pragma unroll
     for (int r = 0; r < RR; ++r) acc[t][r] = 0.f;
-  for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
-    float a[RR][8];
+  // U 8-element vectors per thread and step (2 for RR = 1), all of a step's
+  // loads issued before any is used: a 4096-wide decode row is then one step
+  // of 256 threads, one memory round trip.
+  constexpr int U = RR == 1 ? 2 : 1;
+  for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += U * (int64_t)blockDim.x) {
+    uint4 ua[U][RR];
 #pragma unroll
-    for (int r = 0; r < RR; ++r) {
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (r0 + r < rank) u = __ldg(reinterpret_cast<const uint4*>(lora_a + (int64_t)(r0 + r) * K) + v);
-      const T* e = reinterpret_cast<const T*>(&u);
+    for (int h = 0; h < U; ++h) {
+      const int64_t v = v0 + h * (int64_t)blockDim.x;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) a[r][j] = to_f32(e[j]);
+      for (int r = 0; r < RR; ++r)
+        ua[h][r] = (v < nvec && r0 + r < rank)
+                       ? __ldcg(reinterpret_cast<const uint4*>(lora_a + (int64_t)(r0 + r) * K) + v)
+                       : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
       if (m0 + t >= M) break;
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(x + (m0 + t) * ld_x) + v);
-      const T* e = reinterpret_cast<const T*>(&u);
-      float xv[8];
+      uint4 ux[U];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) xv[j] = to_f32(e[j]);
+      for (int h = 0; h < U; ++h) {
+        const int64_t v = v0 + h * (int64_t)blockDim.x;
+        ux[h] = v < nvec ? __ldcg(reinterpret_cast<const uint4*>(x + (m0 + t) * ld_x) + v)
+                         : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-      for (int r = 0; r < RR; ++r)
+      for (int h = 0; h < U; ++h) {
+        const T* e = reinterpret_cast<const T*>(&ux[h]);
+        float xv[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[t][r] += a[r][j] * xv[j];
+        for (int j = 0; j < 8; ++j) xv[j] = to_f32(e[j]);
+#pragma unroll
+        for (int r = 0; r < RR; ++r) {
+          const T* ea = reinterpret_cast<const T*>(&ua[h][r]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[t][r] += to_f32(ea[j]) * xv[j];
+        }
+      }
     }
   }
   __shared__ float red[8][TT * RR];

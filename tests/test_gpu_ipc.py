@@ -33,7 +33,8 @@ def test_allgather_world_one_matches_forward(qb, workloads, cuda):
         want = torch.empty(M, 512, dtype=torch.bfloat16, device=cuda)
         args = (code, _ptr(d["x"]), 1024, *(_ptr(w) for w in d["w"]), K_g, _ptr(d["bias"]), _ptr(d["lora_a"]),
                 _ptr(d["lora_b"]), rank, float(d["scale"]))
-        assert lib.qlin_forward(*args, _ptr(want), 512, M, K_g, N_g, _ptr(ws), n, stream) == 0
+        # the fused all-gather runs the tensor-core kernel: compare with the same kernel
+        assert lib.qlin_forward_ex(*args, _ptr(want), 512, M, K_g, N_g, _ptr(ws), n, 2, 0, stream) == 0
         wide = torch.zeros(M, 512 * 3, dtype=torch.bfloat16, device=cuda)
         outs = (ctypes.c_void_p * 1)(wide.data_ptr())
         flags = (ctypes.c_void_p * 1)(None)

@@ -4,8 +4,9 @@ Each rank holds half of the output quaternion rows.  The NCCL path (shard
 kernel, all-gather, column gather) and the fused path (the shard kernel's
 epilogue stores into every rank's output over NVLink, then a bounded flag
 barrier; qlin_forward_allgather) must give the same [M, out] output on every
-rank, equal to each other and within the bf16 tolerance of the unpartitioned
-layer.  Output widths that do not divide by the world size exercise the
+rank, agreeing with each other (to fp32 summation order: the two paths may
+run different device kernels) and within the bf16 tolerance of the
+unpartitioned layer.  Output widths that do not divide by the world size exercise the
 padded last shard; repeated calls exercise the barrier's call counter.
 Ranks are child processes (spawn) with a short process-group timeout; the
 parent bounds their lifetime."""
@@ -69,7 +70,11 @@ def _rank_main(rank, port, out_q):
                 y_fused = fused(x)
             torch.cuda.synchronize()
             err = ((y_fused.float() - want.float()).norm() / want.float().norm()).item()
-            results.append((M, fout, bool(torch.equal(y_plain, y_fused)), err))
+            # the NCCL path's per-shard calls may run the decode GEMV (1-2
+            # tokens), the fused path the tensor-core kernel: fp32 summation
+            # order differs, so agreement, not bit equality
+            diff = ((y_plain.float() - y_fused.float()).norm() / y_fused.float().norm()).item()
+            results.append((M, fout, diff <= 4e-3, err))
         results.append(("device_error", qb.device_error(dev)))
         out_q.put((rank, results))
         ok = True
