@@ -186,6 +186,50 @@ def lora_forward(base_y, x, lora_a, lora_b, scale) -> np.ndarray:
     return np.asarray(base_y, np.float64) + scale * (t @ np.asarray(lora_b, np.float64).T)
 
 
+FACTORIZED_MODES = ("independent", "shared_input", "shared_output")
+
+
+def factorized_parameter_count(in_features: int, out_features: int, rank: int, mode: str) -> int:
+    """quaternion/factorized.py:35-49: scalar parameters of a factorized weight."""
+    if mode not in FACTORIZED_MODES:
+        raise ValueError(f"mode must be one of {FACTORIZED_MODES}, got {mode!r}")
+    og, ig = out_features // 4, in_features // 4
+    if mode == "independent":
+        return 4 * (og * rank + rank * ig)
+    if mode == "shared_input":
+        return 4 * og * rank + rank * ig
+    return og * rank + 4 * rank * ig
+
+
+def factorized_weights(mode: str, a, b):
+    """quaternion/factorized.py:113-124: the dense components from the factors.
+
+    ``a`` and ``b`` are the four left / right factors ([og, rank] / [rank, ig])
+    where the mode keeps them per component, or a single shared array."""
+    if mode not in FACTORIZED_MODES:
+        raise ValueError(f"mode must be one of {FACTORIZED_MODES}, got {mode!r}")
+    f64 = lambda t: np.asarray(t, dtype=np.float64)
+    if mode == "independent":
+        return tuple(f64(ac) @ f64(bc) for ac, bc in zip(a, b))
+    if mode == "shared_input":
+        return tuple(f64(ac) @ f64(b) for ac in a)
+    return tuple(f64(a) @ f64(bc) for bc in b)
+
+
+def normalize_quaternion(wr, wi, wj, wk, eps: float = 1e-8):
+    """quaternion/unit.py:26-34: element-wise projection onto the unit sphere."""
+    c = [np.asarray(t, dtype=np.float64) for t in (wr, wi, wj, wk)]
+    norm = np.maximum(np.sqrt(c[0] * c[0] + c[1] * c[1] + c[2] * c[2] + c[3] * c[3]), eps)
+    return tuple(t / norm for t in c)
+
+
+def unit_weights(vr, vi, vj, vk, log_magnitude):
+    """quaternion/unit.py:77-81: exp(log_magnitude) * the unit quaternion of v
+    (log_magnitude [og, 1] per output group or [og, ig] per element)."""
+    scale = np.exp(np.asarray(log_magnitude, dtype=np.float64))
+    return tuple(t * scale for t in normalize_quaternion(vr, vi, vj, vk))
+
+
 def relative_frobenius_error(a, b) -> float:
     """quaternion/metrics.py:38-43: ||a - b|| / ||b|| in float64."""
     a = np.asarray(a, dtype=np.float64)

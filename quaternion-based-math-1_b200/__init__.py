@@ -32,6 +32,7 @@ from .packing import (
     unpack_quaternion_to_real,
 )
 from .planar import planar_coefficient_tensor, quaternion_linear_naive, quaternion_linear_planar
+from .reparam import FactorizedQuaternionLinear, UnitQuaternionLinear, normalize_quaternion, parameter_count
 from .sharded import ColumnParallelQuaternionLinear, PeerOutputs, gather_columns, shard_bounds
 
 __all__ = [
@@ -52,6 +53,10 @@ __all__ = [
     "pack_components",
     "build_block_matrix",
     "check_divisible",
+    "FactorizedQuaternionLinear",
+    "parameter_count",
+    "UnitQuaternionLinear",
+    "normalize_quaternion",
     "ColumnParallelQuaternionLinear",
     "PeerOutputs",
     "gather_columns",
