@@ -50,8 +50,11 @@ enum {
   QLIN_ALGO_TC = 2,     /* TMA + tcgen05/TMEM kernel: bf16/f16, aligned shapes  */
   QLIN_ALGO_GEMV = 3    /* CUDA-core decode GEMV: bf16/f16, at most 4 tokens,
                            K_g a multiple of 8, LoRA rank <= 32 and a multiple
-                           of 4; one launch, no workspace (QLIN_ALGO_AUTO picks
-                           it for at most 2 tokens)                            */
+                           of 4 (then x and lora_a 16-byte aligned, ld_x a
+                           multiple of 8); one launch without LoRA, two with
+                           (the down-projection prologue, whose output lives in
+                           the workspace); QLIN_ALGO_AUTO picks it for at most
+                           2 tokens and at most one 8-quaternion CTA per SM    */
 };
 
 /*

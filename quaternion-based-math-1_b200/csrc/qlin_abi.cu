@@ -619,7 +619,8 @@ int launch_gemv_mt(DeviceInfo* dev, const GemvParams& prm, cudaStream_t stream) 
                       : launch_gemv<T, MT, false, false>(dev, prm, stream);
 }
 
-// CUDA-core decode kernel (one launch, no workspace).
+// CUDA-core decode kernel: one launch; with LoRA after the down-projection
+// prologue, whose t is in the workspace.
 template <typename T>
 int run_gemv(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
              const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y, int64_t ld_y, int64_t M,
