@@ -2,7 +2,7 @@
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py`` (its
 ``cpu_baseline`` leg and ``--impl reference`` arm) may import this module, and
-only as the checker or as the timed CPU baseline.  The product package never
+only to check device results or as the timed CPU baseline.  The product package never
 imports it and has no CPU path of its own.
 
 Each function restates the reference's algorithm in numpy (or calls the C

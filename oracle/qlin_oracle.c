@@ -1,7 +1,7 @@
 /*
  * CPU oracle for the quaternion linear forward.  TEST INFRASTRUCTURE ONLY:
  * tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference arm
- * call it as the checker or the timed CPU baseline; the product never links it.
+ * call it to check device results or as the timed CPU baseline; the product never links it.
  *
  * Restates, in double precision, the explicit Hamilton-product definition of
  * the reference:

@@ -2,7 +2,7 @@
 
 * registers the ``gpu`` marker (tests that need a B200; run with ``-m gpu``);
 * imports the package (its directory name is not an identifier) as ``qb``;
-* imports the CPU oracle (``oracle/oracle.py``) as the checker.
+* imports the CPU oracle (``oracle/oracle.py``) that device results are checked against.
 """
 
 from __future__ import annotations
