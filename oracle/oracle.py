@@ -230,6 +230,20 @@ def unit_weights(vr, vi, vj, vk, log_magnitude):
     return tuple(t * scale for t in normalize_quaternion(vr, vi, vj, vk))
 
 
+def project_onto_quaternion(weight):
+    """conversion/fit_linear.py:35-61: the least-squares quaternion components
+    of a real [4*og, 4*ig] matrix -- for each component, the signed mean of
+    the four block entries the block structure (build_block_matrix) gives it."""
+    w = np.asarray(weight, dtype=np.float64)
+    if w.ndim != 2 or w.shape[0] % 4 or w.shape[1] % 4:
+        raise ValueError("weight must be 2D with both dimensions divisible by 4")
+    og, ig = w.shape[0] // 4, w.shape[1] // 4
+    blocks = w.reshape(og, 4, ig, 4).transpose(0, 2, 1, 3)  # [og, ig, row, col]
+    # sign of component c at block entry (row, col): read off the block structure
+    basis = [build_block_matrix(*(np.eye(4)[c][k] * np.ones((1, 1)) for k in range(4))) for c in range(4)]
+    return tuple((blocks * basis[c][None, None]).sum(axis=(2, 3)) / 4.0 for c in range(4))
+
+
 def relative_frobenius_error(a, b) -> float:
     """quaternion/metrics.py:38-43: ||a - b|| / ||b|| in float64."""
     a = np.asarray(a, dtype=np.float64)

@@ -14,6 +14,7 @@ The directory name is not a Python identifier, so import it with
 """
 
 from . import ops
+from .convert import ConversionRecord, convert_model, eligible_modules, project_onto_quaternion
 from ._lib import device_error
 from .linear import QuaternionLinear, fused_quaternion_linear, quaternion_linear
 from .lora import (
@@ -57,6 +58,10 @@ __all__ = [
     "parameter_count",
     "UnitQuaternionLinear",
     "normalize_quaternion",
+    "convert_model",
+    "eligible_modules",
+    "project_onto_quaternion",
+    "ConversionRecord",
     "ColumnParallelQuaternionLinear",
     "PeerOutputs",
     "gather_columns",
