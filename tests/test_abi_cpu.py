@@ -66,6 +66,11 @@ def test_shape_errors_are_reported_before_device_use(qb):
     # unknown flag bits are refused (after the shape checks, before any device use)
     code = lib.qlin_forward_ex(1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 4, P)
     assert code == 8
+    # kernel choices: AUTO, SIMT, TC, GEMV (0-3); anything else is refused before device use
+    for algo in (-1, 4):
+        code = lib.qlin_forward_ex(1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, algo, 0, P)
+        assert code == 8, algo
+    assert qb._lib.ALGO_GEMV == 3
     # M == 0 is a no-op that succeeds without a device
     code = lib.qlin_forward(1, P, 16, P, P, P, P, 4, P, P, P, 0, 0.0, P, 16, 0, 4, 4, P, 0, P)
     assert code == 0
