@@ -7,8 +7,12 @@ the layer on one batch of seeded synthetic input.
 
 Default workload (N=1): the decode layer in=out=4096 bf16, M=1 token, fused
 bias [4096] and LoRA rank 32 (the decode configuration of the reference's
-benchmark set).  The same run also reports decode at M=16 and the prefill
-layer in=4096 -> out=11008 at M=2048 under "also".
+benchmark set).  The same run reports, as top-level keys ending the line, the
+metric's other halves -- "decode_m16" and "prefill_m2048" (in=4096 ->
+out=11008, M=2048) -- and under "also" the fp32 1024 layer, the 5120 -> 27648
+layer at M in {1, 16, 512, 8192} and the 48 linears of the GPT-2-small-shaped
+stack.  Every kernel number has cuBLAS dense of the same logical shape beside
+it, timed the same way.
 
 Timing: W untimed warm-up steps, then exactly K steps captured in one CUDA
 graph and replayed once between CUDA events (device time), bracketed by a
@@ -18,10 +22,17 @@ reported.  Consecutive steps rotate through enough copies of the weights
 HBM.  "e2e" times K steps through the public module API with the input copied
 from pinned host memory and the output read back every step.
 
-With torchrun (N>1) every rank runs an independent replica of the workload
-(weak scaling); value = max-over-ranks time / (K * N), the job-wide time per
-call.  `--impl reference` times the CPU restatement of the reference's K1
-(naive) operator on the host cores (rank 0 only).
+With torchrun (N>1) the headline is the 5120 -> 27648 layer column-partitioned
+over the N ranks (out/4 quaternion rows each) at --shard-m tokens (8192 by
+default), the full output assembled on every rank inside the timed region
+(strong scaling); the same layer unpartitioned on one GPU, the other token
+counts and independent decode replicas are extra keys.
+
+CPU baselines (rank 0, N=1): the unmodified reference module
+(QuaternionLinear + LoRAQuaternionLinear on CPU torch, installed under
+baseline/_ref) -- `--impl reference` prints it as its own line -- and the
+oracle's numpy restatement of the reference K1 operator, both under one sample
+policy (cpu_sample).
 """
 
 from __future__ import annotations
@@ -201,11 +212,17 @@ class ClockSampler:
 # device timing
 # ---------------------------------------------------------------------------
 
+def _ncopy(lay, min_bytes=2 * L2_BYTES):
+    """Copies of a workload's weights and inputs that the timed steps rotate
+    through so that together they exceed L2 (at least two)."""
+    nbytes, _ = algorithmic_work(lay)
+    return max(2, min(64, math.ceil(min_bytes / max(nbytes, 1))))
+
+
 def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES, flags=0, algo=0):
     """Device copies rotated to exceed L2, preallocated outputs and workspace."""
     dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
-    nbytes, _ = algorithmic_work(lay)
-    ncopy = max(2, min(64, math.ceil(min_bytes / max(nbytes, 1))))
+    ncopy = _ncopy(lay, min_bytes)
 
     def t(a):
         return None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev).to(dt)
@@ -394,23 +411,24 @@ def _time_ranks(torch, dev, dist, call, steps, W):
     return float(t.item()), mode
 
 
-def time_sharded(qb, wl, torch, dev, dist, world, rank, W, Ms=(1, 16, 512, 8192)):
+def time_sharded(qb, wl, torch, dev, dist, world, rank, W, cases):
     """The large layer (in=5120 -> out=27648) column-partitioned over the
     torchrun world: rank r runs the kernel on its out/4 rows (N_g/world of
     6912).  Two ways to assemble [M, 27648] on every rank are timed: NCCL
     (all-gather of the [M, 4*N_g/world] outputs over NVLink, then for M > 1
-    the column-gather kernel) and fused (qlin_forward_allgather: the
-    epilogue stores into every rank's output over NVLink, then a flag
-    barrier).  Each is captured in a CUDA graph (eager launches if capture
-    is refused); device time, max over ranks.  Weight shards rotate across
-    more than L2.  The fused roofline target is the slower of the shard's
-    compute (or HBM) time and its NVLink egress at 770 GB/s."""
+    the column-gather kernel) and fused (qlin_forward_allgather: entry flag
+    barrier, the epilogue stores into every rank's output over NVLink, exit
+    flag barrier).  Each is captured in a CUDA graph (eager launches if
+    capture is refused); device time, max over ranks.  Weight shards rotate
+    across more than L2.  `cases` is a list of (M, steps).  The fused
+    roofline target is the slower of the shard's compute (or HBM) time and
+    its NVLink egress at 770 GB/s."""
     lib = qb._lib.load()
     code = qb._lib.dtype_code(torch.bfloat16)
     stream_of = qb._lib.stream_handle
     peaks_ref, _ = _peaks()
     out = {}
-    for M in Ms:
+    for M, steps in cases:
         lay = wl.sharded_27648(M)
         N_g, K_g = lay.N_g, lay.K_g
         n = -(-N_g // world)
@@ -457,7 +475,6 @@ def time_sharded(qb, wl, torch, dev, dist, world, rank, W, Ms=(1, 16, 512, 8192)
             if st != 0:
                 qb._lib.check(st, "qlin_forward_allgather")
 
-        steps = 200 if M <= 16 else 20
         us, mode = _time_ranks(torch, dev, dist, call, steps, W)
         us_f, mode_f = _time_ranks(torch, dev, dist, call_fused, steps, W)
         same = bool(torch.equal(po.out, y_full if M > 1 else flat.view(M, -1)))
@@ -466,45 +483,99 @@ def time_sharded(qb, wl, torch, dev, dist, world, rank, W, Ms=(1, 16, 512, 8192)
         best = min(us, us_f)
         if M <= 16:
             a = nbytes / (best * 1e-6) / 1e9
-            roof = {"bound": "hbm", "achieved_per_gpu": a, "unit": "GB/s", "basis": "shard bytes per GPU"}
+            roof = {"bound": "hbm", "achieved_per_gpu": a, "unit": "GB/s", "peak": peaks_ref["hbm_gbs"],
+                    "frac_per_gpu": a / peaks_ref["hbm_gbs"], "basis": "shard bytes per GPU"}
         else:
             a = flops / (best * 1e-6) / 1e12
-            roof = {"bound": "tensor", "achieved_per_gpu": a, "unit": "TFLOP/s", "basis": "shard FLOP per GPU"}
+            roof = {"bound": "tensor", "achieved_per_gpu": a, "unit": "TFLOP/s", "peak": peaks_ref["bf16_tflops"],
+                    "frac_per_gpu": a / peaks_ref["bf16_tflops"], "basis": "shard FLOP per GPU"}
         egress = (world - 1) * M * 4 * n * 2  # bytes each rank stores to its peers
         t_nvl = egress / 770e9 * 1e6          # at the measured 770 GB/s peer copy, per direction
         t_cmp = (nbytes / (peaks_ref["hbm_gbs"] * 1e9) if M <= 16 else flops / (peaks_ref["bf16_tflops"] * 1e12)) * 1e6
-        out[f"m{M}"] = {"us_per_call_nccl": us, "us_per_call_fused": us_f, "steps": steps,
-                        "timing": [mode, mode_f], "shard_rows": n, "fused_equals_nccl": same,
-                        "allgather_bytes_per_rank": M * 4 * n * 2, "roofline": roof,
-                        "fused_roofline": {"target_us": max(t_nvl, t_cmp), "nvlink_us": t_nvl,
-                                           "compute_or_hbm_us": t_cmp,
-                                           "frac": max(t_nvl, t_cmp) / us_f},
-                        "plan": qb._lib.plan(torch.bfloat16, M, K_g, n, 0)}
+        launches = qb._lib.plan(torch.bfloat16, M, K_g, n, 0, flags=qb._lib.FLAG_ZEROED_WORKSPACE)["launches"]
+        out[M] = {"us_nccl": us, "us_fused": us_f, "steps": steps, "timing": [mode, mode_f], "shard_rows": n,
+                  "fused_equals_nccl": same, "roofline": roof,
+                  "fused_target_us": max(t_nvl, t_cmp), "fused_frac_of_target": max(t_nvl, t_cmp) / us_f,
+                  "nvlink_us": t_nvl, "launches_fused": launches + 2}
         del shards, x, y_loc, flat, y_full, wsb
         torch.cuda.empty_cache()
     return out
 
 
+def time_sharded_e2e(qb, wl, torch, dev, dist, world, M, K, W):
+    """K calls of the column-partitioned 5120->27648 layer through the public
+    module (ColumnParallelQuaternionLinear: its fused NVLink all-gather for
+    M >= 64), each with the input copied from pinned host memory and the
+    full output read back to pinned host memory; max over ranks."""
+    lay = wl.sharded_27648(M)
+    full = qb.QuaternionLinear(5120, 27648, device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for name, a in zip(("wr", "wi", "wj", "wk"), lay.weights):
+            getattr(full, name).copy_(torch.from_numpy(a))
+    mod = qb.ColumnParallelQuaternionLinear.from_full(full)
+    del full
+    torch.cuda.empty_cache()
+    x_host = torch.from_numpy(lay.x).to(torch.bfloat16).pin_memory()
+    y_host = torch.empty(M, 27648, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty(M, 5120, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y = mod(x_dev)
+        y_host.copy_(y, non_blocking=True)
+
+    with torch.inference_mode():
+        for _ in range(W):
+            step()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(K):
+            step()
+        e.record()
+        torch.cuda.synchronize(dev)
+    t = torch.tensor([s.elapsed_time(e) * 1e3 / K], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), M * 5120 * 2, M * 27648 * 2
+
+
 def time_dense(lay, torch, dev, K, W):
-    """cuBLAS x @ W^T of the same logical shape (context only)."""
+    """cuBLAS x @ W^T of the same logical shape (context only), captured in
+    one CUDA graph and replayed between CUDA events exactly like our calls."""
     dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
     M, Kf, N = lay.M, 4 * lay.K_g, 4 * lay.N_g
-    wbytes = N * Kf * 2
-    ncopy = max(2, min(32, math.ceil(2 * L2_BYTES / (wbytes + 2 * M * (Kf + N)))))
+    wbytes = N * Kf * dt.itemsize
+    ncopy = max(2, min(32, math.ceil(2 * L2_BYTES / (wbytes + dt.itemsize * M * (Kf + N)))))
     g = torch.Generator(device="cpu").manual_seed(0)
     ws = [(torch.randn(N, Kf, generator=g) / math.sqrt(Kf)).to(dev, dt) for _ in range(ncopy)]
     xs = [torch.randn(M, Kf, generator=g).to(dev, dt) for _ in range(ncopy)]
     ys = [torch.empty(M, N, device=dev, dtype=dt) for _ in range(ncopy)]
-    for i in range(W):
+
+    def call(i):
         torch.matmul(xs[i % ncopy], ws[i % ncopy].t(), out=ys[i % ncopy])
-    _settle(torch, dev, lambda: torch.matmul(xs[0], ws[0].t(), out=ys[0]), 0.3)
+
+    for i in range(W):
+        call(i)
+    torch.cuda.synchronize(dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        call(0)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(K):
+            call(i)
+    _settle(torch, dev, graph.replay, 0.3)
     torch.cuda.synchronize(dev)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for i in range(K):
-        torch.matmul(xs[i % ncopy], ws[i % ncopy].t(), out=ys[i % ncopy])
+    graph.replay()
     e.record()
     torch.cuda.synchronize(dev)
+    del graph
     return s.elapsed_time(e) * 1e3 / K
 
 
@@ -554,8 +625,59 @@ def time_e2e(qb, lay, torch, dev, K, W):
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the oracle's numpy restatement of the reference K1 operator
+# CPU baselines, one sample policy for both: the unmodified reference module
+# (installed under baseline/_ref) and the oracle's numpy restatement of K1
 # ---------------------------------------------------------------------------
+
+def _reference_modules():
+    """(QuaternionLinear, LoRAQuaternionLinear) of the unmodified reference
+    package installed under baseline/_ref, or None when it is absent."""
+    root = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "quaternion")):
+        return None
+    if root not in sys.path:
+        sys.path.insert(0, root)
+    try:
+        from quaternion.linear import QuaternionLinear  # the reference package (CPU torch)
+        from quaternion.lora import LoRAQuaternionLinear
+    except ImportError:
+        return None
+    return QuaternionLinear, LoRAQuaternionLinear
+
+
+def reference_cpu_call(lay):
+    """The reference's own module path on CPU torch, in the layer's dtype:
+    QuaternionLinear.forward (quaternion/linear.py:120-124), wrapped in
+    LoRAQuaternionLinear.forward (quaternion/lora.py:60-63) when the layer has
+    LoRA.  Returns call(rows) or None when the reference is not installed."""
+    mods = _reference_modules()
+    if mods is None:
+        return None
+    import torch
+
+    QL, LQL = mods
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
+    base = QL(4 * lay.K_g, 4 * lay.N_g, bias=lay.bias is not None, dtype=dt)
+    with torch.no_grad():
+        for n, a in zip(("wr", "wi", "wj", "wk"), lay.weights):
+            getattr(base, n).copy_(torch.from_numpy(a))
+        if lay.bias is not None:
+            base.bias.copy_(torch.from_numpy(lay.bias))
+    mod = base
+    if lay.lora_a is not None:
+        mod = LQL(base, rank=lay.lora_a.shape[0])
+        with torch.no_grad():
+            mod.lora_A.copy_(torch.from_numpy(lay.lora_a))
+            mod.lora_B.copy_(torch.from_numpy(lay.lora_b))
+    mod.eval()
+    x = torch.from_numpy(lay.x).to(dt)
+
+    def call(rows):
+        with torch.inference_mode():
+            return mod(x[: len(rows)])
+
+    return call
+
 
 def cpu_port_call(oracle, lay, rows):
     """quaternion/planar.py:39-61 (+ bias, + lora.py:60-63) in float32 BLAS."""
@@ -568,43 +690,108 @@ def cpu_port_call(oracle, lay, rows):
     return y
 
 
-def time_cpu(lay, budget_s=10.0, max_steps=None, warmup=1):
-    """Bounded CPU sample; returns (us_per_call, threads, sample description)."""
+def cpu_sample(fn, M, steps, warmup, budget_s):
+    """The one CPU sample policy: a step runs fn on the first `rows` tokens,
+    rows = M unless one call of M tokens would exceed 0.25 s (then as many
+    tokens as fit, the time scaled to M); `warmup` untimed steps, then up to
+    `steps` timed ones, stopping once `budget_s` has passed (at least 3).
+    Returns (us per call of M tokens, timed steps, rows)."""
+    probe = min(M, 8)
+    t0 = time.perf_counter()
+    fn(np.arange(probe))
+    per_row = max((time.perf_counter() - t0) / probe, 1e-7)
+    rows_n = M if per_row * M <= 0.25 else max(1, min(M, int(0.25 / per_row)))
+    rows = np.arange(rows_n)
+    for _ in range(warmup):
+        fn(rows)
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < steps:
+        t0 = time.perf_counter()
+        fn(rows)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 3 and time.perf_counter() - t_start > budget_s:
+            break
+    return statistics.median(times) * (M / rows_n) * 1e6, len(times), rows_n
+
+
+def cpu_baselines(lay, steps, warmup, budget_s):
+    """(primary, port): the reference module on CPU torch (kind "reference")
+    when installed, else the port; and the port itself (kind "port")."""
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
     oracle = _oracle()
     try:
         from threadpoolctl import threadpool_limits
+        ctx = threadpool_limits(limits=threads)
     except ImportError:  # pragma: no cover
-        threadpool_limits = None
-    threads = os.cpu_count() or 1
-    ctx = threadpool_limits(limits=threads) if threadpool_limits else None
-    # row sample sized so one step stays near 50 ms of CPU work
-    probe_rows = min(lay.M, 8)
-    t0 = time.perf_counter()
-    cpu_port_call(oracle, lay, np.arange(probe_rows))
-    per_row = max((time.perf_counter() - t0) / probe_rows, 1e-7)
-    rows_n = lay.M if per_row * lay.M <= 0.05 else max(1, min(lay.M, int(0.05 / per_row)))
-    rows = np.arange(rows_n)
-    for _ in range(warmup):
-        cpu_port_call(oracle, lay, rows)
-    times = []
-    t_start = time.perf_counter()
-    while True:
-        t0 = time.perf_counter()
-        cpu_port_call(oracle, lay, rows)
-        times.append(time.perf_counter() - t0)
-        if max_steps is not None and len(times) >= max_steps:
-            break
-        if max_steps is None and time.perf_counter() - t_start > budget_s:
-            break
-    if ctx is not None:
-        ctx.unregister() if hasattr(ctx, "unregister") else None
-    per_call = statistics.median(times) * (lay.M / rows_n)
-    sample = (f"{len(times)} calls of the numpy/OpenBLAS float32 K1 restatement on {rows_n} of "
-              f"{lay.M} token rows, scaled to the full batch")
-    return per_call * 1e6, threads, sample, len(times)
+        ctx = None
+    port_us, n, rows = cpu_sample(lambda r: cpu_port_call(oracle, lay, r), lay.M, steps, warmup, budget_s)
+    port = {"value": port_us, "unit": "us/call", "cores": threads, "kind": "port",
+            "sample": f"{n} calls of the oracle's numpy/OpenBLAS float32 restatement of the reference K1 "
+                      f"operator (+bias, +LoRA) on {rows} of {lay.M} token rows, scaled to the batch"}
+    if ctx is not None and hasattr(ctx, "unregister"):
+        ctx.unregister()
+    ref_fn = reference_cpu_call(lay)
+    if ref_fn is None:
+        return port, port
+    ref_us, n, rows = cpu_sample(ref_fn, lay.M, steps, warmup, budget_s)
+    ref = {"value": ref_us, "unit": "us/call", "cores": threads, "kind": "reference",
+           "sample": f"{n} calls of the unmodified reference module (QuaternionLinear"
+                     f"{' + LoRAQuaternionLinear' if lay.lora_a is not None else ''}, CPU torch "
+                     f"{torch.__version__}, {lay.dtype}) on {rows} of {lay.M} token rows, scaled to the batch"}
+    return ref, port
 
 
 # ---------------------------------------------------------------------------
+
+def _roofline(bound, nbytes, flops, us, peaks, peak_src=None, launches=None, workload=None):
+    if bound == "hbm":
+        a = nbytes / (us * 1e-6) / 1e9
+        r = {"bound": "hbm", "achieved": a, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": a / peaks["hbm_gbs"]}
+    elif bound == "fp32":
+        a = flops / (us * 1e-6) / 1e12
+        r = {"bound": "fp32 CUDA cores", "achieved": a, "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s",
+             "frac": a / FP32_NOMINAL_TFLOPS, "peak_source": "nominal"}
+    else:
+        a = flops / (us * 1e-6) / 1e12
+        r = {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+             "frac": a / peaks["bf16_tflops"]}
+    if workload is not None:
+        traffic, tsrc = _traffic(workload)
+        r["traffic"] = traffic
+        r["traffic_source"] = tsrc
+        r["basis"] = (f"{nbytes} algorithmic bytes" if bound == "hbm" else f"{flops:.4g} dense-equivalent FLOP") + \
+            f" per call / device time per call ({launches} launches per call)"
+    if peak_src is not None and "peak_source" not in r:
+        r["peak_source"] = peak_src
+    return r
+
+
+def _entry(qb, wl, torch, dev, name, K, W, peaks, with_clocks=False):
+    """Compact record of one secondary workload: device us/call, roofline,
+    cuBLAS dense of the same logical shape (same graph-replay timing)."""
+    lay = _layer(wl, name)
+    bound = WORKLOADS[name]["bound"]
+    kk = K if bound == "hbm" else max(3, min(K, 100))
+    if with_clocks:
+        with ClockSampler(dev.index) as clk:
+            ms, _, plan = time_device(qb, lay, torch, dev, kk, W)
+        clocks = clk.summary()
+    else:
+        ms, _, plan = time_device(qb, lay, torch, dev, kk, W)
+        clocks = None
+    us = ms * 1e3 / kk
+    nb, fl = algorithmic_work(lay)
+    e = {"value": us, "unit": "us/call", "steps": kk, "launches": plan["launches"], "algo": plan["algo"],
+         "roofline": _roofline(bound, nb, fl, us, peaks),
+         "dense_cublas_us": time_dense(lay, torch, dev, kk, W)}
+    if clocks is not None:
+        e["clocks"] = clocks
+    return e
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -614,7 +801,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default=DEFAULT, choices=sorted(WORKLOADS))
     ap.add_argument("--no-extra", action="store_true", help="skip the secondary workloads")
-    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--shard-m", type=int, default=8192,
+                    help="tokens of the column-partitioned headline at --gpus N > 1")
     args = ap.parse_args()
     K, W = args.steps, max(args.warmup, 3)
 
@@ -623,23 +812,23 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
     qb, wl = _pkg()
-    lay = _layer(wl, args.workload)
     metric = "QuaternionLinear us/call (bf16), % of HBM/TC roofline"
 
     if args.impl == "reference":
         if rank != 0:
             return
-        us, threads, sample, n = time_cpu(lay, budget_s=1e9, max_steps=K, warmup=W)
-        cfg = workload_config(args.workload, lay, 1)
+        lay = _layer(wl, args.workload)
+        ref, port = cpu_baselines(lay, K, W, budget_s=60.0)
+        # the same config record as the device arm's (it does not rotate
+        # copies, but the workload is identical)
+        cfg = dict(workload_config(args.workload, lay, _ncopy(lay)), parallelism="single")
         print(json.dumps({
-            "impl": "reference", "metric": metric, "value": us, "unit": "us/call",
-            "n_gpus": args.gpus, "steps": K, "warmup": W, "ms_per_step": us / 1e3,
+            "impl": "reference", "metric": metric, "value": ref["value"], "unit": "us/call",
+            "n_gpus": args.gpus, "steps": K, "warmup": W, "ms_per_step": ref["value"] / 1e3,
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32 (numpy port of the reference K1 operator)", "data": "synthetic",
-            "config": cfg,
-            "cpu_baseline": {"value": us, "unit": "us/call", "cores": threads, "kind": "port",
-                             "sample": sample},
-            "e2e": {"value": us, "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "dtype": f"{lay.dtype} (CPU)", "data": "synthetic", "config": cfg,
+            "cpu_baseline": ref, "cpu_port": port,
+            "e2e": {"value": ref["value"], "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }), flush=True)
         return
 
@@ -673,120 +862,108 @@ def main():
     torch.cuda.set_device(dev)
     peaks, peak_src = _peaks()
 
+    if dist is not None:
+        result = main_partitioned(qb, wl, torch, dev, dist, world, rank, K, W, args.shard_m, metric, peaks,
+                                  peak_src)
+        dist.barrier()
+        dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+        return
+
+    lay = _layer(wl, args.workload)
     nbytes, flops = algorithmic_work(lay)
     with ClockSampler(local) as clk:
-        ms, ncopy, plan = time_device(qb, lay, torch, dev, K, W, dist)
+        ms, ncopy, plan = time_device(qb, lay, torch, dev, K, W)
     launches = plan["launches"]
     us_call = ms * 1e3 / K
-    clocks = clk.summary()
     bound = WORKLOADS[args.workload]["bound"]
-    if bound == "hbm":
-        achieved = nbytes / (us_call * 1e-6) / 1e9
-        traffic, tsrc = _traffic(args.workload)
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic, "traffic_source": tsrc,
-                "basis": f"{nbytes} algorithmic bytes per call / device time per call "
-                         f"({launches} launches per call)",
-                "peak_source": peak_src}
-    else:
-        achieved = flops / (us_call * 1e-6) / 1e12
-        traffic, tsrc = _traffic(args.workload)
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,
-                "traffic_source": tsrc,
-                "basis": f"{flops:.4g} dense-equivalent FLOP per call / device time per call",
-                "peak_source": peak_src}
-
     result = {
-        "metric": metric, "value": us_call / world, "unit": "us/call", "n_gpus": world,
+        "metric": metric, "value": us_call, "unit": "us/call", "n_gpus": 1,
         "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": lay.dtype, "data": "synthetic",
-        "config": dict(workload_config(args.workload, lay, ncopy),
-                       parallelism=f"replicas{world}" if world > 1 else "single"),
-        "per_gpu_us_per_call": us_call,
-        "roofline": roof,
-        "clocks": clocks,
+        "config": dict(workload_config(args.workload, lay, ncopy), parallelism="single"),
+        "roofline": _roofline(bound, nbytes, flops, us_call, peaks, peak_src, launches, args.workload),
+        "clocks": clk.summary(),
         "gpu_launches": K * launches,
         "plan": plan,
     }
-
     # Same workload with the weights declared static (inference): each call
     # streams its weights while the previous call's kernels finish.
-    sms, _, _ = time_device(qb, lay, torch, dev, K, W, dist, flags=qb._lib.FLAG_STATIC_WEIGHTS)
-    result["static_weights_us_per_call"] = sms * 1e3 / K / world
-    if plan["algo"] == "gemv":
-        # context: the same calls forced onto the tensor-core kernel
-        tms, _, _ = time_device(qb, lay, torch, dev, K, W, dist, algo=qb._lib.ALGO_TC)
-        result["tensor_core_kernel_us_per_call"] = tms * 1e3 / K / world
-
+    sms, _, _ = time_device(qb, lay, torch, dev, K, W, flags=qb._lib.FLAG_STATIC_WEIGHTS)
+    result["static_weights_us_per_call"] = sms * 1e3 / K
     e2e_us, h2d, d2h = time_e2e(qb, lay, torch, dev, K, W)
-    if dist is not None:
-        t = torch.tensor([e2e_us], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_us = float(t.item())
-    result["e2e"] = {"value": e2e_us / world, "unit": "us/call", "h2d_bytes_per_step": h2d,
-                     "d2h_bytes_per_step": d2h}
-
-    if world == 1 and rank == 0:
-        us, threads, sample, _ = time_cpu(lay, budget_s=args.cpu_budget)
-        result["cpu_baseline"] = {"value": us, "unit": "us/call", "cores": threads, "kind": "port",
-                                  "sample": sample}
-        result["dense_cublas_us"] = time_dense(lay, torch, dev, K, W)
-        if not args.no_extra:
-            also = {}
-            for name in WORKLOADS:
-                if name == args.workload:
-                    continue
-                xl = _layer(wl, name)
-                kk = K if WORKLOADS[name]["bound"] == "hbm" else max(3, min(K, 100))
-                xms, xcopy, xplan = time_device(qb, xl, torch, dev, kk, W)
-                xus = xms * 1e3 / kk
-                xb, xf = algorithmic_work(xl)
-                entry = {"us_per_call": xus, "steps": kk, "plan": xplan,
-                         "config": workload_config(name, xl, xcopy),
-                         "dense_cublas_us": time_dense(xl, torch, dev, kk, W)}
-                if WORKLOADS[name]["bound"] == "hbm":
-                    a = xb / (xus * 1e-6) / 1e9
-                    entry["roofline"] = {"bound": "hbm", "achieved": a, "peak": peaks["hbm_gbs"],
-                                         "unit": "GB/s", "frac": a / peaks["hbm_gbs"]}
-                elif WORKLOADS[name]["bound"] == "fp32":
-                    a = xf / (xus * 1e-6) / 1e12
-                    entry["roofline"] = {"bound": "fp32 CUDA cores", "achieved": a,
-                                         "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s",
-                                         "frac": a / FP32_NOMINAL_TFLOPS, "peak_source": "nominal"}
-                else:
-                    a = xf / (xus * 1e-6) / 1e12
-                    entry["roofline"] = {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"],
-                                         "unit": "TFLOP/s", "frac": a / peaks["bf16_tflops"]}
-                also[name] = entry
-            sus, sflops, ncalls, splans = time_stack(qb, wl, torch, dev, 20, W)
-            a = sflops / (sus * 1e-6) / 1e12
-            also["gpt2_stack"] = {
-                "us_per_forward": sus, "linears": ncalls, "replays": 20, "plans": splans,
-                "config": {"workload": "gpt2_small_stack_12x4_linears_bf16_m8192", "M": 8192,
-                           "blocks": 12, "linears": "qkv 768->2304, proj 768->768, fc 768->3072, "
-                                                    "fc2 3072->768",
-                           "inputs": "seeded synthetic N(0,1) activations, N(0,1/in) weights"},
-                "roofline": {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"],
-                             "unit": "TFLOP/s", "frac": a / peaks["bf16_tflops"]},
-            }
-            result["also"] = also
-    if dist is not None:
-        # the large layer column-partitioned over all ranks (out/4 rows per
-        # rank, NCCL all-gather of the outputs)
-        peak_hbm, peak_tc = peaks["hbm_gbs"], peaks["bf16_tflops"]
-        sh = time_sharded(qb, wl, torch, dev, dist, world, rank, W)
-        for v in sh.values():
-            r = v["roofline"]
-            r["frac_per_gpu"] = r["achieved_per_gpu"] / (peak_hbm if r["bound"] == "hbm" else peak_tc)
-        result["sharded_large"] = {
-            "config": {"workload": "qlinear_5120x27648_bf16_column_partitioned", "gpus": world,
-                       "parallelism": f"column{world} + NCCL all-gather"},
-            **sh}
-        dist.barrier()
-        dist.destroy_process_group()
+    result["e2e"] = {"value": e2e_us, "unit": "us/call", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    result["dense_cublas_us"] = time_dense(lay, torch, dev, K, W)
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        ref, port = cpu_baselines(lay, K, W, budget_s=args.cpu_budget)
+        result["cpu_baseline"] = ref
+        result["cpu_port"] = port
+    if not args.no_extra:
+        also = {}
+        for name in ("fp32_m128", "large_m1", "large_m16", "large_m512", "large_m8192"):
+            if name != args.workload:
+                also[name] = _entry(qb, wl, torch, dev, name, K, W, peaks)
+        sus, sflops, ncalls, _ = time_stack(qb, wl, torch, dev, 20, W)
+        a = sflops / (sus * 1e-6) / 1e12
+        also["gpt2_stack"] = {"us_per_forward": sus, "linears": ncalls, "M": 8192,
+                              "roofline": {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"],
+                                           "unit": "TFLOP/s", "frac": a / peaks["bf16_tflops"]}}
+        result["also"] = also
+        # the metric's other halves, last so that they end the line
+        for name in ("decode_m16", "prefill_m2048"):
+            if name != args.workload:
+                result[name] = _entry(qb, wl, torch, dev, name, K, W, peaks, with_clocks=True)
+    print(json.dumps(result), flush=True)
+
+
+def main_partitioned(qb, wl, torch, dev, dist, world, rank, K, W, M, metric, peaks, peak_src):
+    """--gpus N > 1: the 5120 -> 27648 layer column-partitioned over the N
+    ranks (out/4 rows per rank) at M tokens, the full output assembled on
+    every rank inside the timed region (strong scaling: the layer and batch
+    are fixed, N GPUs share them).  value = device us per call, max over
+    ranks, of the path the module takes at this M (fused NVLink all-gather
+    for M >= 64, else NCCL)."""
+    with ClockSampler(dev.index) as clk:
+        head = time_sharded(qb, wl, torch, dev, dist, world, rank, W, [(M, K)])[M]
+    clocks = clk.summary()
+    fused = M >= 64
+    us = head["us_fused"] if fused else head["us_nccl"]
+    lay = wl.sharded_27648(M)
+    n = head["shard_rows"]
+    flops = 2.0 * M * 4 * lay.K_g * 4 * n
+    nbytes = 2 * (4 * n * lay.K_g + M * 4 * lay.K_g + M * 4 * n)
+    roof = _roofline("tensor" if M > 16 else "hbm", nbytes, flops, us, peaks, peak_src)
+    roof["basis"] = "one rank's shard FLOP (or bytes) / call time incl. the output all-gather"
+    # the same layer unpartitioned on this GPU (the N = 1 point of the sweep)
+    one_ms, _, _ = time_device(qb, lay, torch, dev, K, W, dist)
+    single_us = one_ms * 1e3 / K
+    e2e_us, h2d, d2h = time_sharded_e2e(qb, wl, torch, dev, dist, world, M, min(K, 20), W)
+    others = time_sharded(qb, wl, torch, dev, dist, world, rank, W,
+                          [(m, 200 if m <= 16 else 20) for m in (1, 16, 512, 8192) if m != M])
+    # independent decode replicas (one per GPU), max over ranks
+    dlay = _layer(wl, "decode_m1")
+    dms, _, _ = time_device(qb, dlay, torch, dev, K, W, dist)
+    launches = head["launches_fused"] if fused else None
+    return {
+        "metric": metric, "value": us, "unit": "us/call", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"qlinear_5120x27648_bf16_m{M}_column_partitioned", "M": M,
+                   "in_features": 5120, "out_features": 27648, "shard_rows_per_gpu": n,
+                   "parallelism": f"column{world} (out/4 quaternion rows) + "
+                                  + ("fused NVLink all-gather" if fused else "NCCL all-gather"),
+                   "inputs": "seeded synthetic N(0,1) activations, N(0,1/in) weights (variance)",
+                   "l2": "inputs larger than L2: rotating weight shard copies"},
+        "roofline": roof,
+        "clocks": clocks,
+        "gpu_launches": K * (launches or 2),
+        "e2e": {"value": e2e_us, "unit": "us/call", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "single_gpu_us_per_call": single_us,
+        "decode_replicas_us_per_call": dms * 1e3 / K,
+        "sharded_other_m": {f"m{m}": v for m, v in others.items()},
+        "partitioned": head,
+    }
 
 
 if __name__ == "__main__":

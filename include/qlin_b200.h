@@ -171,13 +171,18 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flag
  *               process (CUDA IPC), to every rank's full output [M, ld_out]
  *               (outs[world_rank] is this rank's own);
  *   flag_arrays host array [world] of device pointers to every rank's
- *               barrier flags, unsigned[world], zero before the first call;
- *   epoch_word  this rank's call counter (device, zero before the first call).
- * A one-warp barrier kernel follows: on return of the stream work every
+ *               barrier flags, unsigned[2 * world], zero before the first call;
+ *   epoch_word  this rank's two call counters, unsigned[2] (device, zero
+ *               before the first call).
+ * Two one-warp barrier kernels bracket the shard kernel: the entry barrier
+ * keeps every rank from storing into a peer's output before that peer has
+ * finished the work it queued on its stream after the previous call (for
+ * example reading or copying that output); after the exit barrier every
  * rank's full output holds all ranks' columns.  Every rank must make the
  * same sequence of calls.  16-bit types, tensor-core path only; waits are
- * bounded (QLIN_ERR_TIMEOUT via qlin_get_device_error).  The other
- * arguments are those of qlin_forward_ex (algo is the tensor-core kernel).
+ * bounded (2 s; QLIN_ERR_TIMEOUT via qlin_get_device_error, after which the
+ * outputs of that call are undefined).  The other arguments are those of
+ * qlin_forward_ex (algo is the tensor-core kernel).
  */
 int qlin_forward_allgather(int dtype,
                            const void* x, int64_t ld_x,
@@ -222,9 +227,12 @@ int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank);
  * fixed buffer of QLIN_NOALLOC_SCRATCH_BYTES compiled into the library, which
  * every GPU that loads the library holds until the process exits.
  *
- *  - Problems whose qlin_workspace_size exceeds QLIN_NOALLOC_SCRATCH_BYTES
- *    (8 MiB: decode-sized layers; M * in_features up to about 4 Mi elements
- *    when M > 64) are refused with QLIN_ERR_WORKSPACE before any device work.
+ *  - A problem is accepted when qlin_workspace_size() for it is at most
+ *    QLIN_NOALLOC_SCRATCH_BYTES (8 MiB; decode-sized layers fit), and refused
+ *    with QLIN_ERR_WORKSPACE before any device work otherwise.  Ask
+ *    qlin_workspace_size() rather than estimating: the scratch holds the
+ *    planar copy of x (M * in_features elements when M > 64), the LoRA down
+ *    projection, fp32 split-K partials and 4096 counter bytes.
  *  - The first call on a device looks up the buffer's device address
  *    (cudaGetSymbolAddress) with that device current; make that first call
  *    before any stream capture.

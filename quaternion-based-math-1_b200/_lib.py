@@ -212,6 +212,9 @@ def _ptr(t):
 # so they may share it; each call leaves its counter bytes at zero.
 _ZEROED_MAX_TOKENS = 4
 _zeroed_ws: dict[tuple[int, int], torch.Tensor] = {}
+# Buffers replaced by larger ones are never released: a CUDA graph captured
+# earlier on the same stream still holds their addresses.
+_zeroed_retired: list[torch.Tensor] = []
 
 
 def _uses_zeroed_workspace(dtype: torch.dtype, M: int) -> bool:
@@ -228,6 +231,8 @@ def zeroed_workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
         return buf
     if torch.cuda.is_current_stream_capturing():
         return None
+    if buf is not None:
+        _zeroed_retired.append(buf)
     buf = torch.zeros(max(nbytes, 64 * 1024), dtype=torch.uint8, device=device)
     _zeroed_ws[key] = buf
     return buf

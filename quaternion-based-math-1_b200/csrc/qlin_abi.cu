@@ -799,7 +799,7 @@ const char* qlin_status_string(int status) {
   }
 }
 
-int qlin_abi_version(void) { return 101; }
+int qlin_abi_version(void) { return 102; }
 
 int qlin_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, size_t* bytes) {
   if (!bytes) return QLIN_ERR_ARG;
@@ -903,12 +903,25 @@ int qlin_forward_allgather(int dtype, const void* x, int64_t ld_x, const void* w
   for (int q = 0; q < world; ++q)
     if (q != world_rank) peers.y[peers.n++] = static_cast<uint8_t*>(outs[q]) + col_offset * 2;
   void* y = static_cast<uint8_t*>(outs[world_rank]) + col_offset * 2;
-  int st = forward_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
-                          ld_out, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_TC, flags, stream, peers);
-  if (st != QLIN_OK || M == 0 || world == 1) return st;
+  int st = validate(dtype, x, ld_x, wr, wi, wj, wk, ld_w, lora_a, lora_b, rank, y, ld_out, M, K_g, N_g);
+  if (st != QLIN_OK || M == 0) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   PeerFlags pf;
   for (int q = 0; q < world; ++q) pf.f[q] = flag_arrays[q];
-  qlin_peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(pf, epoch_word, world_rank, world);
+  if (world > 1) {
+    // Entry barrier (slots [world, 2*world), epoch word 1): no rank stores
+    // into a peer's output while that peer's work queued after the previous
+    // call (reading that output) may still be running.
+    cudaGetLastError();
+    qlin_peer_barrier_kernel<<<1, 32, 0, s>>>(pf, epoch_word + 1, world_rank, world, world);
+    if (cudaGetLastError() != cudaSuccess) return QLIN_ERR_LAUNCH;
+  }
+  st = forward_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
+                      ld_out, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_TC, flags, stream, peers);
+  if (st != QLIN_OK || world == 1) return st;
+  // Exit barrier (slots [0, world), epoch word 0): every rank's columns are
+  // in every rank's output.
+  qlin_peer_barrier_kernel<<<1, 32, 0, s>>>(pf, epoch_word, world_rank, world, 0);
   return cudaGetLastError() == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
 }
 
@@ -1051,6 +1064,6 @@ extern "C" int qlin_forward_noalloc(int dtype, const void* x, int64_t ld_x, cons
   // bytes are zero between calls.  Every other byte a call reads was written
   // earlier in the same call.
   return qlin_forward_ex(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
-                         ld_y, M, K_g, N_g, ws, ws ? (size_t)QLIN_NOALLOC_SCRATCH_BYTES : 0,
+                         ld_y, M, K_g, N_g, ws, ws ? need : 0,
                          QLIN_ALGO_AUTO, ws ? QLIN_FLAG_ZEROED_WORKSPACE : 0, stream);
 }

@@ -322,21 +322,24 @@ qlin_gather_kernel(const E* __restrict__ src, E* __restrict__ dst, int64_t G, in
   }
 }
 
-// Cross-rank barrier of the column-partitioned layer, after each rank's
-// kernels stored its output columns into every rank's output.  One warp:
-// lane p (p != rank) writes this call's epoch into slot `rank` of rank p's
-// flag array (release, system scope), then waits -- bounded -- until slot p
-// of this rank's array holds the epoch (acquire, system scope).  The epoch
-// is a per-rank device counter advanced here, so every rank, taking the
-// same sequence of calls, agrees on it without host involvement (CUDA
-// graphs replay it unchanged).  A wait that runs out records
-// QLIN_ERR_TIMEOUT and returns.
+// Cross-rank barrier of the column-partitioned layer.  It runs twice per
+// call: before the shard kernel (entry: every rank has finished the work it
+// queued after the previous call, so nobody still reads an output that this
+// call overwrites) and after it (exit: every rank's columns have landed in
+// every rank's output).  One warp: lane p (p != rank) writes this barrier's
+// epoch into slot `slot0 + rank` of rank p's flag array (release, system
+// scope), then waits -- bounded -- until slot `slot0 + p` of this rank's
+// array holds the epoch (acquire, system scope).  Each barrier has its own
+// slots and its own per-rank device counter, advanced here, so every rank,
+// taking the same sequence of calls, agrees on the epochs without host
+// involvement (CUDA graphs replay them unchanged).  A wait that runs out
+// records QLIN_ERR_TIMEOUT and returns.
 struct PeerFlags {
-  unsigned* f[kMaxPeers + 1];  // flag array [world] of every rank, by rank
+  unsigned* f[kMaxPeers + 1];  // flag array [2 * world] of every rank, by rank
 };
 
 __global__ void __launch_bounds__(32) qlin_peer_barrier_kernel(const PeerFlags pf, unsigned* epoch_word,
-                                                               int rank, int world) {
+                                                               int rank, int world, int slot0) {
   __shared__ unsigned e;
   if (threadIdx.x == 0) {
     e = *epoch_word + 1u;
@@ -347,11 +350,11 @@ __global__ void __launch_bounds__(32) qlin_peer_barrier_kernel(const PeerFlags p
   const int p = threadIdx.x;
   if (p < world && p != rank) {
     fence_sys();
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(pf.f[p] + rank), "r"(ep) : "memory");
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(pf.f[p] + slot0 + rank), "r"(ep) : "memory");
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
       unsigned v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(pf.f[rank] + p) : "memory");
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(pf.f[rank] + slot0 + p) : "memory");
       if ((int)(v - ep) >= 0) break;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         record_error(7);

@@ -14,6 +14,9 @@
 // stream are ordered and leave its counter bytes at zero); a buffer that
 // must grow while the stream is being captured into a CUDA graph is not
 // grown -- that call takes a plain workspace from the caching allocator.
+// A buffer that is replaced by a larger one is never released: a CUDA graph
+// captured earlier on that stream still holds its address and would write
+// its counters and partial sums into whatever memory reused it.
 #include <torch/extension.h>
 
 #include <ATen/cuda/CUDAContext.h>
@@ -46,6 +49,7 @@ constexpr int64_t kZeroedMaxTokens = 4;
 
 std::mutex g_ws_mutex;
 std::map<std::pair<int, uintptr_t>, at::Tensor> g_zeroed;
+std::vector<at::Tensor> g_zeroed_retired;  // superseded buffers, kept alive for captured graphs
 
 at::Tensor zeroed_workspace(const at::Device& dev, cudaStream_t stream, size_t bytes) {
   const auto key = std::make_pair(static_cast<int>(dev.index()), reinterpret_cast<uintptr_t>(stream));
@@ -55,6 +59,7 @@ at::Tensor zeroed_workspace(const at::Device& dev, cudaStream_t stream, size_t b
   if (c10::cuda::currentStreamCaptureStatusMayInitCtx() != c10::cuda::CaptureStatus::None) return at::Tensor();
   at::Tensor buf = at::zeros({static_cast<int64_t>(std::max<size_t>(bytes, 64 * 1024))},
                              at::TensorOptions().dtype(at::kByte).device(dev));
+  if (it != g_zeroed.end()) g_zeroed_retired.push_back(it->second);
   g_zeroed[key] = buf;
   return buf;
 }

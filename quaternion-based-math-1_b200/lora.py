@@ -32,13 +32,14 @@ __all__ = [
 
 
 class LoRAQuaternionLinear(nn.Module):
-    """Frozen quaternion linear layer plus a trainable low-rank correction."""
+    """A ``QuaternionLinear`` whose weights stay fixed, with a learnable rank-r
+    residual ``scale * B (A x)`` added on the same fused device call."""
 
     def __init__(self, base: QuaternionLinear, rank: int = 8, alpha: float | None = None,
                  dropout: float = 0.0):
         super().__init__()
         if rank <= 0:
-            raise ValueError("rank must be positive")
+            raise ValueError(f"LoRA rank must be at least 1, got {rank}")
         self.base = base
         for p in self.base.parameters():
             p.requires_grad_(False)

@@ -21,8 +21,10 @@ for calls of at least 64 tokens, where it measured faster: 2 GPUs, 5120→27648,
 M=512 98 vs 175 us, M=8192 1054 vs 2103 us; at M=1 and 16 the NCCL path was
 slightly faster): every rank's full output is
 mapped into every other rank (CUDA IPC, exchanged once per output shape),
-each rank's epilogue stores its columns into all of them over NVLink, and a
-bounded cross-rank flag barrier ends the call (``qlin_forward_allgather``).
+each rank's epilogue stores its columns into all of them over NVLink, and
+bounded cross-rank flag barriers open the call (no rank writes into an
+output that a peer may still be copying from) and end it
+(``qlin_forward_allgather``).
 """
 
 from __future__ import annotations
@@ -71,8 +73,9 @@ class PeerOutputs:
     """Every rank's full ``[M, cols]`` output, mapped into this process.
 
     Built collectively (every rank of ``group`` constructs it with the same
-    shape): each rank allocates its output and its barrier flags ``[world]``
-    plus call counter with ``qlin_ipc_alloc`` (plain cudaMalloc, zero-filled),
+    shape): each rank allocates its output and its barrier flags
+    ``[2 * world]`` (entry and exit barrier) plus two call counters with
+    ``qlin_ipc_alloc`` (plain cudaMalloc, zero-filled),
     the CUDA IPC handles are exchanged with ``all_gather_object``, and the
     peers' buffers are mapped with this rank's GPU current (``qlin_ipc_open``:
     plain peer mappings, no multicast objects).  The buffers must outlive
@@ -90,10 +93,11 @@ class PeerOutputs:
         self._mapped = []  # peers' mapped bases (qlin_ipc_open)
         with torch.cuda.device(self.device):
             out_ptr, out_h = self._alloc(lib, M * cols * elem)
-            flag_ptr, flag_h = self._alloc(lib, 4 * (self.world + 1))  # flags[world] + call counter
+            # flags[2 * world] (exit, entry) + the two barriers' call counters
+            flag_ptr, flag_h = self._alloc(lib, 4 * (2 * self.world + 2))
         self.out = _device_view(out_ptr, (M, cols), dtype, self.device, self)
-        self.flags = _device_view(flag_ptr, (self.world,), torch.int32, self.device, self)
-        self.epoch = _device_view(flag_ptr + 4 * self.world, (1,), torch.int32, self.device, self)
+        self.flags = _device_view(flag_ptr, (2 * self.world,), torch.int32, self.device, self)
+        self.epoch = _device_view(flag_ptr + 8 * self.world, (2,), torch.int32, self.device, self)
         everyone = [None] * self.world
         dist.all_gather_object(everyone, (out_h, flag_h), group=group)
         outs, flags = [], []

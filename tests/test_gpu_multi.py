@@ -7,7 +7,9 @@ barrier; qlin_forward_allgather) must give the same [M, out] output on every
 rank, agreeing with each other (to fp32 summation order: the two paths may
 run different device kernels) and within the bf16 tolerance of the
 unpartitioned layer.  Output widths that do not divide by the world size exercise the
-padded last shard; repeated calls exercise the barrier's call counter.
+padded last shard; repeated calls exercise the barriers' call counters, and
+back-to-back calls on different inputs the entry barrier (no rank overwrites
+a peer's output before that peer has copied out the previous result).
 Ranks are child processes (spawn) with a short process-group timeout; the
 parent bounds their lifetime."""
 
@@ -74,6 +76,17 @@ def _rank_main(rank, port, out_q):
             # tokens), the fused path the tensor-core kernel: fp32 summation
             # order differs, so agreement, not bit equality
             diff = ((y_plain.float() - y_fused.float()).norm() / y_fused.float().norm()).item()
+            # back-to-back fused calls on different inputs, no host sync in
+            # between: each call's stores into a peer's output must wait
+            # until that peer has copied out the previous call's result
+            xs = [torch.randn(M, fin, generator=g).to(dev, torch.bfloat16) for _ in range(4)]
+            wants = [qb.fused_quaternion_linear(xi, full.wr, full.wi, full.wj, full.wk, full.bias, la, lb, scale)
+                     for xi in xs]
+            gots = [fused(xi) for xi in xs]
+            torch.cuda.synchronize()
+            for gi, wi in zip(gots, wants):
+                e = ((gi.float() - wi.float()).norm() / wi.float().norm()).item()
+                err = max(err, e)
             results.append((M, fout, diff <= 4e-3, err))
         results.append(("device_error", qb.device_error(dev)))
         out_q.put((rank, results))

@@ -190,13 +190,45 @@ def test_config_gpt2_layers_sampled(qb, oracle, workloads, cuda, li):
     assert rel_err(oracle, got[torch.from_numpy(rows).to(cuda)].cpu().numpy(), want) <= 1e-2
 
 
-@pytest.mark.parametrize("M", [1, 16, 512])
+@pytest.mark.parametrize("M", [1, 16, 512, 8192])
 def test_config_sharded_layer_sampled(qb, oracle, workloads, cuda, M):
     lay = workloads.sharded_27648(M)
-    got = run(qb, to_device(lay, cuda)).float()
+    d = to_device(lay, cuda)
+    got = run(qb, d).float()
     rows = sample_rows(lay.M, 6)
     want = oracle_rows(oracle, lay, rows)
     assert rel_err(oracle, got[torch.from_numpy(rows).to(cuda)].cpu().numpy(), want) <= 1e-2
+    if M == 8192:
+        # every row: agreement with the independent CUDA-core kernel
+        simt = run(qb, d, ALGO_SIMT).float()
+        assert float(torch.linalg.norm(got - simt) / torch.linalg.norm(simt)) <= 1e-2
+
+
+@pytest.mark.parametrize("M", [16, 512])
+@pytest.mark.parametrize("G", [2, 4, 8])
+def test_config_sharded_layer_every_shard(qb, oracle, workloads, cuda, G, M):
+    """The 5120->27648 layer cut into G column shards (6912 / G = 3456, 1728 or
+    864 output quaternions per rank; 864 is not a multiple of the 128-row
+    tile), each shard run on this GPU as its rank would run it
+    (local_forward); the shards side by side equal the oracle."""
+    lay = workloads.sharded_27648(M)
+    d = to_device(lay, cuda)
+    full = qb.QuaternionLinear(5120, 27648, device=cuda, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for name, w in zip(("wr", "wi", "wj", "wk"), d["w"]):
+            getattr(full, name).copy_(w)
+    parts = []
+    for r in range(G):
+        shard = qb.ColumnParallelQuaternionLinear.from_full(full, world_size=G, rank=r)
+        assert shard.shard == 6912 // G
+        parts.append(shard.local_forward(d["x"])[:, :4 * (shard.end - shard.begin)])
+    got = torch.cat(parts, 1).float()
+    assert got.shape == (M, 27648)
+    rows = sample_rows(lay.M, 4)
+    want = oracle_rows(oracle, lay, rows)
+    assert rel_err(oracle, got[torch.from_numpy(rows).to(cuda)].cpu().numpy(), want) <= 1e-2
+    whole = run(qb, d).float()
+    assert float(torch.linalg.norm(got - whole) / torch.linalg.norm(whole)) <= 1e-2
 
 
 def test_no_device_error_recorded(qb, cuda):

@@ -174,3 +174,33 @@ def test_plan_reports_the_decode_split(qb, cuda):
     assert plan["split_k"] == 1 and plan["launches"] == 2
     assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 64, flags=0)["launches"] == 2
     assert qb._lib.plan(torch.bfloat16, 1, 1024, 1024, 0, flags=0)["launches"] == 1
+
+
+def test_graph_replay_after_zeroed_workspace_grows(qb, cuda):
+    """Decode-sized calls use a zero-filled workspace kept per stream.  A
+    graph captured while the stream's buffer was small must still replay
+    correctly after a larger layer made that buffer grow: the superseded
+    buffer stays alive (its memory is not handed to other tensors)."""
+    small, x = _layers(qb, cuda, 2, 512, 3, True)
+    big, xb = _layers(qb, cuda, 1, 4096, 4, True)
+    want = _reference(qb, small, x)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.no_grad():
+        with torch.cuda.stream(s):
+            _chain(qb, small, x, False)  # creates the stream's zero-filled buffer
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            out = _chain(qb, small, x, False)
+        with torch.cuda.stream(s):
+            _chain(qb, big, xb, False)  # needs a larger buffer: the small one is replaced
+        s.synchronize()
+        # fill whatever memory the allocator hands out now with non-zero bytes
+        junk = [torch.full((1 << 16,), 255, dtype=torch.uint8, device=cuda) for _ in range(64)]
+        torch.cuda.synchronize()
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, want)
+    del junk, graph
+    assert qb.device_error(cuda) == 0
