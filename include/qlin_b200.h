@@ -78,8 +78,14 @@ enum {
  * zeroed workspace may serve problems of any size: every non-zero
  * qlin_workspace_size() includes the counter bytes at its start, which no
  * other use of the workspace touches.
+ *
+ * QLIN_FLAG_NO_PAIR (comparisons and diagnostics): run prefill-sized
+ * problems on the one-CTA tensor-core kernel (component planes from a
+ * prologue kernel) instead of the CTA-pair kernel that QLIN_ALGO_AUTO and
+ * QLIN_ALGO_TC otherwise use for them (more than 64 tokens, no LoRA, an even
+ * number of output quaternions, ld_y a multiple of 8 and a 16-byte aligned y).
  */
-enum { QLIN_FLAG_STATIC_WEIGHTS = 1, QLIN_FLAG_ZEROED_WORKSPACE = 2 };
+enum { QLIN_FLAG_STATIC_WEIGHTS = 1, QLIN_FLAG_ZEROED_WORKSPACE = 2, QLIN_FLAG_NO_PAIR = 4 };
 #define QLIN_WORKSPACE_COUNTER_BYTES 4096u
 
 /* Human-readable name of a status code (static storage). */
@@ -147,11 +153,15 @@ int qlin_forward_ex(int dtype,
                     void* workspace, size_t workspace_bytes,
                     int algo, int flags, void* stream);
 
+/* qlin_plan's algo for the tensor-core path run on the CTA-pair kernel
+ * (persistent, two SMs per tile, 2-SM tcgen05 UMMA); not an input value. */
+#define QLIN_PLAN_TC_PAIR 4
+
 /*
  * Launch plan qlin_forward_ex uses for this problem with these flags on the
  * current device (diagnostics; no reference counterpart; flags 0 is
  * qlin_forward's plan).  Fills every non-null output:
- * algo (QLIN_ALGO_*, assuming aligned pointers), tokens per tensor-core tile,
+ * algo (QLIN_ALGO_* or QLIN_PLAN_TC_PAIR, assuming aligned pointers), tokens per tensor-core tile,
  * K split (CTAs sharing one output tile), kernel launches per call, and how
  * many CTAs of the tensor-core kernel the device keeps resident at once.
  */

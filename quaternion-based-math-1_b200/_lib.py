@@ -23,6 +23,8 @@ F32, BF16, F16 = 0, 1, 2
 ALGO_AUTO, ALGO_SIMT, ALGO_TC, ALGO_GEMV = 0, 1, 2, 3
 FLAG_STATIC_WEIGHTS = 1
 FLAG_ZEROED_WORKSPACE = 2
+FLAG_NO_PAIR = 4
+PLAN_TC_PAIR = 4
 
 OK = 0
 ERR_SHAPE = 1
@@ -198,7 +200,8 @@ def plan(dtype: torch.dtype, M: int, K_g: int, N_g: int, rank: int, flags: int |
                            *(ctypes.byref(o) for o in outs)),
           "qlin_plan")
     algo, tok, split, launches, resident = (o.value for o in outs)
-    return {"algo": {ALGO_SIMT: "simt", ALGO_TC: "tcgen05", ALGO_GEMV: "gemv"}.get(algo, str(algo)),
+    return {"algo": {ALGO_SIMT: "simt", ALGO_TC: "tcgen05", ALGO_GEMV: "gemv",
+                     PLAN_TC_PAIR: "tcgen05-pair"}.get(algo, str(algo)),
             "tile_tokens": tok, "split_k": split, "launches": launches, "resident_ctas": resident}
 
 

@@ -18,6 +18,7 @@
 #include "../../include/qlin_b200.h"
 #include "qlin_gemv.cuh"
 #include "qlin_simt.cuh"
+#include "qlin_pair.cuh"
 #include "qlin_tc.cuh"
 
 namespace {
@@ -38,6 +39,9 @@ struct DeviceInfo {
   int cluster_cap[2][3][kTcClusterMax + 1];
   // CUDA-core decode kernel: shared-memory limit raised, by [dtype][MT][LoRA][peers]
   bool gemv_attr_set[2][3][2][2] = {};
+  // CTA-pair prefill kernel: attributes set and how many pairs fit at once, by [dtype][peers]
+  bool pair_attr_set[2][2] = {};
+  int pair_cap[2][2] = {};
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mutex;
@@ -426,11 +430,110 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
   return QLIN_OK;
 }
 
+// The CTA-pair kernel (qlin_pair.cuh) takes prefill-sized problems without
+// LoRA or peer outputs: more than kStackMaxTokens tokens, 16-byte output
+// pieces (ld_y a multiple of 8, 16-byte aligned y, an even number of output
+// quaternions) on top of the tensor-core path's TMA rules.
+bool pair_eligible(int64_t M, int64_t N_g, int rank, const void* y, int64_t ld_y, const PeerOut& peers,
+                   int flags) {
+  return M > kStackMaxTokens && rank == 0 && peers.n == 0 && !(flags & QLIN_FLAG_NO_PAIR) && N_g % 2 == 0 &&
+         ld_y % 8 == 0 && aligned(y, 16);
+}
+
+template <typename T, bool PEERS>
+int pair_attrs(DeviceInfo* dev, int* cap) {
+  const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
+  const int pi = PEERS ? 1 : 0;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!dev->pair_attr_set[di][pi]) {
+    auto kernel = qlin_pair_kernel<T, PEERS>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes) != cudaSuccess)
+      return QLIN_ERR_LAUNCH;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPairSmemBytes;
+    cudaLaunchAttribute a;
+    a.id = cudaLaunchAttributeClusterDimension;
+    a.val.clusterDim.x = 2;
+    a.val.clusterDim.y = 1;
+    a.val.clusterDim.z = 1;
+    cfg.attrs = &a;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      return QLIN_ERR_LAUNCH;
+    }
+    dev->pair_cap[di][pi] = n;
+    dev->pair_attr_set[di][pi] = true;
+  }
+  *cap = dev->pair_cap[di][pi];
+  return QLIN_OK;
+}
+
+// Tiles of the CTA-pair kernel: 256 real outputs x 128 tokens.
+inline int64_t pair_tiles(int64_t M, int64_t N_g) { return ((4 * N_g + 255) / 256) * ((M + 127) / 128); }
+
+template <typename T>
+int run_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
+             T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, cudaStream_t stream) {
+  if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
+  int cap = 0;
+  int st = pair_attrs<T, false>(dev, &cap);
+  if (st != QLIN_OK) return st;
+  const CUtensorMapDataType dt =
+      std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)(4 * K_g), (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld_x * 2)};
+    cuuint32_t box[2] = {64, (cuuint32_t)kPairHalfTokens};
+    if (encode(&map, dt, 2, const_cast<T*>(x), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+      return QLIN_ERR_ALIGN;
+  }
+  const int64_t tiles = pair_tiles(M, N_g);
+  if (tiles > INT32_MAX) return QLIN_ERR_SHAPE;
+  PairParams prm{};
+  for (int p = 0; p < 4; ++p) prm.w[p] = w[p];
+  prm.ld_w = ld_w;
+  prm.bias = bias;
+  prm.y = y;
+  prm.ld_y = ld_y;
+  prm.M = (int)M;
+  prm.N_g = (int)N_g;
+  prm.K_g = (int)K_g;
+  prm.stages = (int)((K_g + 31) / 32);
+  prm.nb_tiles = (int)((4 * N_g + 255) / 256);
+  prm.tiles = (int)tiles;
+  prm.peers.n = 0;
+  const int64_t pairs = std::min<int64_t>(tiles, cap);
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  attrs[1].id = cudaLaunchAttributeClusterDimension;
+  attrs[1].val.clusterDim.x = 2;
+  attrs[1].val.clusterDim.y = 1;
+  attrs[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, qlin_pair_kernel<T, false>, map, prm) == cudaSuccess ? QLIN_OK
+                                                                                      : QLIN_ERR_LAUNCH;
+}
+
 template <typename T>
 int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
            const T* bias, const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y,
            int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, uint8_t* ws, int flags,
            const PeerOut& peers, cudaStream_t stream) {
+  if (pair_eligible(M, N_g, rank, y, ld_y, peers, flags))
+    return run_pair<T>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, stream);
   if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -735,7 +838,7 @@ static int forward_common(int dtype, const void* x, int64_t ld_x, const void* wr
   if (st != QLIN_OK) return st;
   if (M == 0) return QLIN_OK;
   if (algo < QLIN_ALGO_AUTO || algo > QLIN_ALGO_GEMV) return QLIN_ERR_ARG;
-  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE)) return QLIN_ERR_ARG;
+  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE | QLIN_FLAG_NO_PAIR)) return QLIN_ERR_ARG;
   if (rank == 0) lora_a = lora_b = nullptr;
   DeviceInfo* dev = nullptr;
   st = device_info(&dev);
@@ -817,7 +920,7 @@ int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
 int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flags, int* algo,
               int* tile_tokens, int* split_k, int* launches, int* resident_ctas) {
   if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
-  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE)) return QLIN_ERR_ARG;
+  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE | QLIN_FLAG_NO_PAIR)) return QLIN_ERR_ARG;
   if (M <= 0 || K_g <= 0 || N_g <= 0 || rank < 0) return QLIN_ERR_SHAPE;
   DeviceInfo* dev = nullptr;
   int st = device_info(&dev);
@@ -838,6 +941,16 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flag
       per_sm = 0;
     cudaGetLastError();
     res = per_sm * dev->num_sms;
+  } else if (a == QLIN_ALGO_TC && M > kStackMaxTokens && rank == 0 && N_g % 2 == 0 &&
+             !(flags & QLIN_FLAG_NO_PAIR)) {
+    // the CTA-pair kernel (assuming a 16-byte aligned output)
+    int cap = 0;
+    st = dtype == QLIN_BF16 ? pair_attrs<__nv_bfloat16, false>(dev, &cap) : pair_attrs<__half, false>(dev, &cap);
+    if (st != QLIN_OK) return st;
+    a = QLIN_PLAN_TC_PAIR;
+    nt = kPairTokens;
+    nl = 1;
+    res = 2 * (int)std::min<int64_t>(pair_tiles(M, N_g), cap);
   } else if (a == QLIN_ALGO_TC) {
     nt = n_tok_for(M);
     const bool bf = dtype == QLIN_BF16;

@@ -1,0 +1,502 @@
+// Prefill-sized quaternion linear forward on a pair of SMs (sm_100a):
+// persistent, 2-SM tcgen05 UMMA (cta_group::2) with the weight operand
+// expanded into tensor memory.
+//
+// The layer is y = x Wd^T with the real block matrix
+//
+//     Wd[4o + a, 4i + q] = s(a, a^q) * W_{a^q}[o, i]
+//
+// (reference quaternion/packing.py:18-21 and quaternion/linear.py:66-69: row
+// block a of the 4x4 block matrix holds W_{a^q} in column block q, negated
+// where the table has a minus).  Wd is four times the weight bytes, so it is
+// never stored anywhere: the builder warps read W_p rows straight from global
+// memory (a quarter of a dense layer's weight traffic), apply the component
+// swap and the sign in registers, and write the Wd rows of the current K
+// stage into tensor memory with tcgen05.st, where the UMMA reads them as its
+// A operand.  x is the B operand exactly as the caller stores it ([M, K]
+// rows, K-major, loaded by TMA with 128-byte swizzling): no component planes,
+// no prologue kernel.
+//
+// Tile of one CTA pair (a 2-CTA cluster): 256 real outputs (64 output
+// quaternions; 128 rows of Wd in each CTA's tensor memory) x 128 tokens
+// (64 tokens of x in each CTA's shared memory).  One UMMA of M = 256,
+// N = 128, K = 16 per step, issued by the pair's even CTA, reads A from both
+// CTAs' tensor memory and B from both CTAs' shared memory and accumulates
+// into both CTAs' tensor memory (each CTA's 128 rows).  Per SM and UMMA step
+// the shared-memory traffic is the x half-tile once written by TMA and once
+// read by the UMMA (64 B/clk at full tensor rate, half the SM's bandwidth);
+// the weight operand costs tensor-memory stores, not shared memory.
+//
+// Tensor memory of each CTA (512 columns): two accumulators of 128 columns
+// (tile t accumulates into buffer t % 2 while the epilogue drains the other)
+// and four A stages of 64 columns (128 real inputs each).  The pair walks the
+// tiles tile = pair, pair + pairs, ... (persistent grid of one pair per two
+// SMs).
+//
+// Roles (320 threads per CTA):
+//   warp 0, lane 0   TMA producer of this CTA's x half-tiles (both CTAs)
+//   warp 1           tensor-memory allocation (both CTAs); lane 0 issues the
+//                    UMMAs in the even CTA, and in the odd CTA forwards "my
+//                    x stage and my A stage are ready" to the even CTA
+//   warps 2-5        builders: expanded weight rows into tensor memory
+//                    (warp w writes lanes 32 (w % 4) .. +31)
+//   warps 6-9        epilogue: accumulator -> bias -> one rounding -> y
+//                    (warp w reads lanes 32 (w % 4) .. +31)
+// Every mbarrier wait is bounded; a wait that runs out records
+// QLIN_ERR_TIMEOUT, the CTA stops issuing work, and both CTAs still meet at
+// the final cluster barrier and release their tensor memory.
+#pragma once
+
+#include <type_traits>
+
+#include "qlin_common.cuh"
+
+namespace qlin {
+
+constexpr int kPairThreads = 320;
+constexpr int kPairRows = 128;          // real outputs per CTA (UMMA M = 256 per pair)
+constexpr int kPairTokens = 128;        // tokens per pair tile (UMMA N)
+constexpr int kPairHalfTokens = 64;     // tokens of x per CTA
+constexpr int kPairStageK = 128;        // real inputs per stage (32 input quaternions)
+constexpr int kPairStages = 4;
+constexpr int kPairXAtomBytes = kPairHalfTokens * 128;        // 8 KB: 64 rows x 128 B (64 inputs)
+constexpr int kPairXStageBytes = 2 * kPairXAtomBytes;         // 16 KB
+constexpr int kPairACols = kPairStageK / 2;                   // 64 tensor-memory columns per A stage
+constexpr int kPairDCols = kPairTokens;                       // 128 columns per accumulator
+constexpr int kPairAColBase = 2 * kPairDCols;                 // A stages after the two accumulators
+constexpr int kPairEpiTokens = 16;                            // tokens per epilogue group
+constexpr int kPairEpiBufBytes = kPairEpiTokens * kPairRows * 2;  // 4 KB staging (bf16/f16)
+constexpr int kPairEpiBar = 2;                                // named barrier of the epilogue warps
+constexpr int kPairPrefetch = 3;                              // builder W stages in flight
+// Shared memory: x stages, two epilogue staging buffers, barriers; padded so
+// that only one CTA fits an SM (each CTA takes the whole tensor memory).
+constexpr int kPairXOffset = 0;
+constexpr int kPairEpiOffset = kPairStages * kPairXStageBytes;
+constexpr int kPairBarOffset = kPairEpiOffset + 2 * kPairEpiBufBytes;
+constexpr int kPairSmemBytes = 120 * 1024;
+static_assert(kPairBarOffset + 512 + 1024 <= kPairSmemBytes, "pair kernel shared memory");
+static_assert(kPairAColBase + kPairStages * kPairACols <= 512, "tensor memory budget");
+
+struct PairParams {
+  const void* w[4];    // W_p [N_g, ld_w]
+  int64_t ld_w;
+  const void* bias;    // [4*N_g] or null
+  void* y;             // [M, ld_y]
+  int64_t ld_y;
+  int M, N_g, K_g;
+  int stages;          // K stages per tile: ceil(K_g / 32)
+  int nb_tiles;        // tiles along the outputs: ceil(4*N_g / 256)
+  int tiles;           // nb_tiles * ceil(M / 128)
+  PeerOut peers;       // column-partitioned layer: every output also stored to these
+};
+
+// ---------------------------------------------------------------------------
+// 2-SM tcgen05 helpers (inline PTX)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+               ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D(tmem, both CTAs) (+)= A(tmem, both CTAs) * B(smem desc, both CTAs)^T, kind::f16.
+__device__ __forceinline__ void umma_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive once on the mbarrier at this shared-memory offset in every CTA of
+// cta_mask when all UMMAs issued so far by this thread have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(smem_u32(bar)), "h"(cta_mask) : "memory");
+}
+
+// 32 lanes x 32 bit, 32 consecutive columns per thread (warp-collective).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// mbarrier wait whose acquire is at cluster scope (the barrier may be
+// completed by the other CTA of the pair: a remote arrive or a multicast
+// UMMA commit).  Bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (globaltimer_ns() - t0 > limit_ns) {
+      record_error(7);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Arrive (release, cluster scope) on the mbarrier at this shared-memory
+// offset in CTA `cta` of the cluster.
+__device__ __forceinline__ void mbar_arrive_cta(uint64_t* bar, uint32_t cta) {
+  const uint32_t remote = map_peer_smem(smem_u32(bar), cta);
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+
+// UMMA shared-memory descriptor of a K-major operand tile written by TMA with
+// 128-byte swizzling: 128-byte rows, 8-row groups of 1024 bytes (stride
+// byte offset), leading byte offset unused, version 1, layout code 2.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
+  const uint64_t addr = smem_u32(tile);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;
+  d |= 1ull << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
+// W_p[o, i0 .. i0+32) of this lane's (o, p): 64 bytes as four 16-byte loads
+// (zeros past K_g or past N_g; K_g is a multiple of 8).
+template <typename T>
+__device__ __forceinline__ void pair_load_w(uint4 (&v)[4], const PairParams& prm, int p, int o, int i0) {
+  const T* row = reinterpret_cast<const T*>(prm.w[p]) + (int64_t)o * prm.ld_w;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int i = i0 + 8 * c;
+    if (o < prm.N_g && i < prm.K_g) {
+      uint4 r;
+      asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                   : "l"(row + i));
+      v[c] = r;
+    } else {
+      v[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+template <typename T, bool PEERS>
+__global__ void __launch_bounds__(kPairThreads, 1)
+qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const PairParams prm) {
+  constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  constexpr uint32_t kIdesc = make_idesc_f16(256, kPairTokens, kFmt, false);
+  constexpr int S = kPairStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + kPairBarOffset);
+  uint64_t* afull = xfull + S;
+  uint64_t* empty = afull + S;
+  uint64_t* ready = empty + S;    // even CTA: the odd CTA's stage is ready
+  uint64_t* dfull = ready + S;    // [2]
+  uint64_t* dempty = dfull + 2;   // [2], even CTA: both CTAs' epilogues drained the buffer
+  uint64_t* drain = dempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* issued = const_cast<int*>(abort_flag) + 1;  // producer: x stage loads issued
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_ctarank();     // 0: issues the UMMAs
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int my_tiles = pair < prm.tiles ? (prm.tiles - 1 - pair) / pairs + 1 : 0;
+  const int nk = prm.stages;
+
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&afull[s], 4);
+      mbar_init(&empty[s], 1);
+      mbar_init(&ready[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&dfull[b], 1);
+      mbar_init(&dempty[b], 8);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *issued = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&map_x);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers initialised, tensor memory allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // Everything below reads what earlier kernels of the stream wrote (x, W,
+  // bias) or writes what they may read (y).
+  pdl_wait_prior();
+
+  auto tile_coords = [&](int t, int& n0, int& m0) {
+    const int nb = t % prm.nb_tiles, tb = t / prm.nb_tiles;
+    n0 = nb * 256 + (int)cta * kPairRows;  // this CTA's first real output
+    m0 = tb * kPairTokens;                 // the pair's first token
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer: this CTA's 64 tokens of x ----------------
+    if (lane == 0) {
+      int g = 0;
+      for (int j = 0; j < my_tiles && !*abort_flag; ++j) {
+        int n0, m0;
+        tile_coords(pair + j * pairs, n0, m0);
+        const int mrow = m0 + (int)cta * kPairHalfTokens;
+        for (int k = 0; k < nk; ++k, ++g) {
+          const int s = g % S, n = g / S;
+          if (n > 0 && !mbar_wait_cl(&empty[s], (n - 1) & 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* dst = smem + kPairXOffset + s * kPairXStageBytes;
+          mbar_arrive_expect_tx(&xfull[s], kPairXStageBytes);
+          tma_load_2d(dst, &map_x, &xfull[s], k * kPairStageK, mrow);
+          tma_load_2d(dst + kPairXAtomBytes, &map_x, &xfull[s], k * kPairStageK + 64, mrow);
+          *issued = g + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int g = 0, tc = 0;
+      bool ok = true;
+      if (cta == 0) {
+        // ---------------- UMMA issuer (even CTA) ----------------
+        for (int j = 0; j < my_tiles && ok; ++j, ++tc) {
+          const int b = tc & 1, u = tc >> 1;
+          if (u > 0 && !mbar_wait_cl(&dempty[b], (u - 1) & 1)) ok = false;
+          tc_fence_after();
+          for (int k = 0; k < nk && ok; ++k, ++g) {
+            const int s = g % S, n = g / S;
+            if (!mbar_wait_cl(&xfull[s], n & 1) || !mbar_wait_cl(&afull[s], n & 1) ||
+                !mbar_wait_cl(&ready[s], n & 1)) {
+              ok = false;
+              break;
+            }
+            if (*abort_flag) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t bdesc0 = smem_desc_sw128(smem + kPairXOffset + s * kPairXStageBytes);
+#pragma unroll
+            for (int kk = 0; kk < kPairStageK / 16; ++kk) {
+              // K16 step kk: B bytes 32 (kk % 4) into swizzle atom kk / 4; A columns 8 kk
+              const uint64_t bdesc = bdesc0 + (uint64_t)((kk >> 2) * (kPairXAtomBytes >> 4)) + 2 * (kk & 3);
+              umma_pair_ts(tmem + b * kPairDCols, tmem + kPairAColBase + s * kPairACols + 8 * kk, bdesc, kIdesc,
+                           (k > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit_pair(&empty[s], 0x3);
+          }
+          if (ok) umma_commit_pair(&dfull[b], 0x3);
+        }
+        if (!ok) *abort_flag = 1;
+        // every UMMA issued above has completed before the teardown
+        umma_commit_pair(drain, 0x1);
+        mbar_wait_cl(drain, 0, 50000000ull);
+      } else {
+        // ---------------- odd CTA: forward stage readiness ----------------
+        for (int j = 0; j < my_tiles && ok; ++j) {
+          for (int k = 0; k < nk; ++k, ++g) {
+            const int s = g % S, n = g / S;
+            if (!mbar_wait_cl(&xfull[s], n & 1) || !mbar_wait_cl(&afull[s], n & 1) || *abort_flag) {
+              ok = false;
+              break;
+            }
+            tc_fence_before();
+            mbar_arrive_cta(&ready[s], 0);
+          }
+        }
+        if (!ok) *abort_flag = 1;
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------- builders: expanded weight rows into tensor memory ----------------
+    // Lane l of builder warp w writes tensor-memory lane r = 32 (w % 4) + l,
+    // i.e. real output n0 + r = 4 o + a with o = n0/4 + 8 (w % 4) + l/4 and
+    // a = l % 4.  It loads W_a[o, stage's 32 inputs] and takes W_{a^q} for
+    // q = 1..3 from the lanes of its output quaternion (shuffles).
+    const int quarter = warp & 3;
+    const int a = lane & 3;
+    const int o_local = 8 * quarter + (lane >> 2);
+    // sign bits of the four values of an input quaternion in this row:
+    // value q is s(a, a^q) * W_{a^q}
+    uint32_t sg01 = 0, sg23 = 0;
+    {
+      auto neg = [&](int q) {
+        const int p = a ^ q;
+        return (a == 0 && p != 0) || (a == 1 && p == 3) || (a == 2 && p == 1) || (a == 3 && p == 2);
+      };
+      sg01 = (neg(0) ? 0x8000u : 0u) | (neg(1) ? 0x80000000u : 0u);
+      sg23 = (neg(2) ? 0x8000u : 0u) | (neg(3) ? 0x80000000u : 0u);
+    }
+    const int total = my_tiles * nk;
+    auto item = [&](int g, int& o, int& i0) {
+      const int j = g / nk, k = g - j * nk;
+      int n0, m0;
+      tile_coords(pair + j * pairs, n0, m0);
+      o = n0 / 4 + o_local;
+      i0 = k * (kPairStageK / 4);
+    };
+    uint4 wbuf[kPairPrefetch][4];
+#pragma unroll
+    for (int d = 0; d < kPairPrefetch; ++d) {
+      if (d < total) {
+        int o, i0;
+        item(d, o, i0);
+        pair_load_w<T>(wbuf[d], prm, a, o, i0);
+      }
+    }
+    for (int g0 = 0; g0 < total; g0 += kPairPrefetch) {
+#pragma unroll
+      for (int d = 0; d < kPairPrefetch; ++d) {
+        const int g = g0 + d;
+        if (g < total && !*abort_flag) {
+          const int s = g % S, n = g / S;
+          // W_{a^q} words of this row's output quaternion (q = 0 is this lane's own)
+          uint32_t wq[4][16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            wq[0][4 * c + 0] = wbuf[d][c].x;
+            wq[0][4 * c + 1] = wbuf[d][c].y;
+            wq[0][4 * c + 2] = wbuf[d][c].z;
+            wq[0][4 * c + 3] = wbuf[d][c].w;
+          }
+#pragma unroll
+          for (int q = 1; q < 4; ++q)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) wq[q][e] = __shfl_sync(0xffffffffu, wq[0][e], lane ^ q);
+          // refill: the item kPairPrefetch further on reuses this buffer
+          if (g + kPairPrefetch < total) {
+            int o, i0;
+            item(g + kPairPrefetch, o, i0);
+            pair_load_w<T>(wbuf[d], prm, a, o, i0);
+          }
+          if (n > 0 && !mbar_wait_cl(&empty[s], (n - 1) & 1)) *abort_flag = 1;
+          if (!*abort_flag) {
+            // columns 2i, 2i+1 of input quaternion i: (v0, v1), (v2, v3)
+            const uint32_t col = tmem + ((uint32_t)(32 * quarter) << 16) + kPairAColBase + s * kPairACols;
+#pragma unroll
+            for (int hblk = 0; hblk < 2; ++hblk) {
+              uint32_t r[32];
+#pragma unroll
+              for (int ii = 0; ii < 16; ++ii) {
+                const int i = 16 * hblk + ii;  // input quaternion within the stage
+                const int e = i >> 1;
+                const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
+                r[2 * ii] = __byte_perm(wq[0][e], wq[1][e], sel) ^ sg01;
+                r[2 * ii + 1] = __byte_perm(wq[2][e], wq[3][e], sel) ^ sg23;
+              }
+              tmem_st32(col + 32 * hblk, r);
+            }
+            tmem_st_wait();
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&afull[s]);
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int quarter = warp & 3;
+    const int et = threadIdx.x - 192;  // 0..127
+    const int n_local = 32 * quarter + lane;
+    T* __restrict__ y = reinterpret_cast<T*>(prm.y);
+    const T* __restrict__ bias = reinterpret_cast<const T*>(prm.bias);
+    for (int j = 0, tc = 0; j < my_tiles; ++j, ++tc) {
+      const int b = tc & 1, u = tc >> 1;
+      int n0, m0;
+      tile_coords(pair + j * pairs, n0, m0);
+      const bool got = !*abort_flag && mbar_wait_cl(&dfull[b], u & 1);
+      if (!got) *abort_flag = 1;
+      tc_fence_after();
+      const int n = n0 + n_local;
+      const float bv = (bias && n < 4 * prm.N_g) ? to_f32(bias[n]) : 0.f;
+#pragma unroll 1
+      for (int grp = 0; grp < kPairTokens / kPairEpiTokens; ++grp) {
+        T* stage = reinterpret_cast<T*>(smem + kPairEpiOffset + (grp & 1) * kPairEpiBufBytes);
+        if (got) {
+          float v[16];
+          __syncwarp();
+          tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + b * kPairDCols + kPairEpiTokens * grp, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int t = 0; t < kPairEpiTokens; ++t) stage[t * kPairRows + n_local] = from_f32<T>(v[t] + bv);
+        }
+        asm volatile("bar.sync %0, %1;" ::"n"(kPairEpiBar), "n"(128) : "memory");
+        if (got) {
+          // 16 tokens x 128 outputs = 256 pieces of 16 bytes, two per thread
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int c = et + 128 * h, t = c >> 4, cc = c & 15;
+            const int m = m0 + kPairEpiTokens * grp + t, nn = n0 + 8 * cc;
+            if (m < prm.M && nn < 4 * prm.N_g) {
+              const uint4 v = *reinterpret_cast<const uint4*>(stage + t * kPairRows + 8 * cc);
+              const int64_t off = (int64_t)m * prm.ld_y + nn;
+              *reinterpret_cast<uint4*>(y + off) = v;
+              if constexpr (PEERS) {
+                for (int pp = 0; pp < prm.peers.n; ++pp)
+                  *reinterpret_cast<uint4*>(reinterpret_cast<T*>(prm.peers.y[pp]) + off) = v;
+              }
+            }
+          }
+        }
+      }
+      // this warp has read its lanes of buffer b: the even CTA may reuse it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(&dempty[b], 0);
+    }
+    if (PEERS) fence_sys();
+  }
+
+  // ---------------- teardown ----------------
+  __syncwarp();
+  if (threadIdx.x == 0 && *abort_flag) {
+    // let issued x loads land before the shared memory goes away
+    const int g1 = *issued;
+    for (int g = g1 - S > 0 ? g1 - S : 0; g < g1; ++g) mbar_wait_cl(&xfull[g % S], (g / S) & 1, 50000000ull);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while the other may still use its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+}  // namespace qlin

@@ -64,7 +64,7 @@ def test_shape_errors_are_reported_before_device_use(qb):
     code = lib.qlin_forward(1, 1, 10, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, P)
     assert code == 1
     # unknown flag bits are refused (after the shape checks, before any device use)
-    code = lib.qlin_forward_ex(1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 4, P)
+    code = lib.qlin_forward_ex(1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 8, P)
     assert code == 8
     # kernel choices: AUTO, SIMT, TC, GEMV (0-3); anything else is refused before device use
     for algo in (-1, 4):

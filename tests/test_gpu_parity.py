@@ -218,10 +218,11 @@ def test_config_sharded_layer_every_shard(qb, oracle, workloads, cuda, G, M):
         for name, w in zip(("wr", "wi", "wj", "wk"), d["w"]):
             getattr(full, name).copy_(w)
     parts = []
-    for r in range(G):
-        shard = qb.ColumnParallelQuaternionLinear.from_full(full, world_size=G, rank=r)
-        assert shard.shard == 6912 // G
-        parts.append(shard.local_forward(d["x"])[:, :4 * (shard.end - shard.begin)])
+    with torch.no_grad():
+        for r in range(G):
+            shard = qb.ColumnParallelQuaternionLinear.from_full(full, world_size=G, rank=r)
+            assert shard.shard == 6912 // G
+            parts.append(shard.local_forward(d["x"])[:, :4 * (shard.end - shard.begin)])
     got = torch.cat(parts, 1).float()
     assert got.shape == (M, 27648)
     rows = sample_rows(lay.M, 4)
