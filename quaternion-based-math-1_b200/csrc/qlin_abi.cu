@@ -484,20 +484,29 @@ int run_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], 
   if (st != QLIN_OK) return st;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap map;
-  std::memset(&map, 0, sizeof(map));
+  // x [M, 4*K_g]: 64-element x 64-token boxes, 128-byte swizzle (the UMMA B
+  // operand); W_p [N_g, K_g]: 32-element x 32-row boxes, 64-byte swizzle (read
+  // by the builder warps).  Out-of-range rows and columns read as zero.
+  CUtensorMap maps[5];
+  std::memset(maps, 0, sizeof(maps));
   {
     cuuint64_t dims[2] = {(cuuint64_t)(4 * K_g), (cuuint64_t)M};
     cuuint64_t strides[1] = {(cuuint64_t)(ld_x * 2)};
     cuuint32_t box[2] = {64, (cuuint32_t)kPairHalfTokens};
-    if (encode(&map, dt, 2, const_cast<T*>(x), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+    if (encode(&maps[0], dt, 2, const_cast<T*>(x), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+      return QLIN_ERR_ALIGN;
+  }
+  for (int p = 0; p < 4; ++p) {
+    cuuint64_t dims[2] = {(cuuint64_t)K_g, (cuuint64_t)N_g};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld_w * 2)};
+    cuuint32_t box[2] = {32, 32};
+    if (encode(&maps[1 + p], dt, 2, const_cast<void*>(w[p]), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B) !=
+        CUDA_SUCCESS)
       return QLIN_ERR_ALIGN;
   }
   const int64_t tiles = pair_tiles(M, N_g);
   if (tiles > INT32_MAX) return QLIN_ERR_SHAPE;
   PairParams prm{};
-  for (int p = 0; p < 4; ++p) prm.w[p] = w[p];
-  prm.ld_w = ld_w;
   prm.bias = bias;
   prm.y = y;
   prm.ld_y = ld_y;
@@ -523,8 +532,10 @@ int run_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], 
   cfg.stream = stream;
   cfg.attrs = attrs;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, qlin_pair_kernel<T, false>, map, prm) == cudaSuccess ? QLIN_OK
-                                                                                      : QLIN_ERR_LAUNCH;
+  return cudaLaunchKernelEx(&cfg, qlin_pair_kernel<T, false>, maps[0], maps[1], maps[2], maps[3], maps[4], prm) ==
+                 cudaSuccess
+             ? QLIN_OK
+             : QLIN_ERR_LAUNCH;
 }
 
 template <typename T>

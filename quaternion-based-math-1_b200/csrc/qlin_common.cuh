@@ -49,6 +49,28 @@ __device__ __forceinline__ void store_out(T* y, const PeerOut& peers, int64_t of
   }
 }
 
+// 16-byte global loads that stay in program order with the dependency wait
+// (griddepcontrol.wait) and with mbarrier waits: volatile asm with a memory
+// clobber, L2 only (.cg).  A plain __ldg of a const __restrict__ pointer may
+// be scheduled above the dependency wait and read what the previous kernel of
+// the stream has not finished writing.
+__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+__device__ __forceinline__ float4 ld_cg_f4(const void* p) {
+  float4 r;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+
 // Orders this thread's earlier stores (peer memory included) before any
 // later signal at system scope.
 __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }

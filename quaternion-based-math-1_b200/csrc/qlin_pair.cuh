@@ -9,9 +9,9 @@
 // (reference quaternion/packing.py:18-21 and quaternion/linear.py:66-69: row
 // block a of the 4x4 block matrix holds W_{a^q} in column block q, negated
 // where the table has a minus).  Wd is four times the weight bytes, so it is
-// never stored anywhere: the builder warps read W_p rows straight from global
-// memory (a quarter of a dense layer's weight traffic), apply the component
-// swap and the sign in registers, and write the Wd rows of the current K
+// never stored anywhere: TMA brings W_p tiles (a quarter of a dense layer's
+// weight traffic) into shared memory, the builder warps apply the component
+// swap and the sign in registers and write the Wd rows of the current K
 // stage into tensor memory with tcgen05.st, where the UMMA reads them as its
 // A operand.  x is the B operand exactly as the caller stores it ([M, K]
 // rows, K-major, loaded by TMA with 128-byte swizzling): no component planes,
@@ -23,25 +23,30 @@
 // N = 128, K = 16 per step, issued by the pair's even CTA, reads A from both
 // CTAs' tensor memory and B from both CTAs' shared memory and accumulates
 // into both CTAs' tensor memory (each CTA's 128 rows).  Per SM and UMMA step
-// the shared-memory traffic is the x half-tile once written by TMA and once
-// read by the UMMA (64 B/clk at full tensor rate, half the SM's bandwidth);
-// the weight operand costs tensor-memory stores, not shared memory.
+// the shared-memory traffic is the x half-tile written by TMA and read by the
+// UMMA plus a quarter of that for W (80 B/clk at full tensor rate, of 128);
+// the expanded weight operand costs tensor-memory stores, not shared memory.
 //
-// Tensor memory of each CTA (512 columns): two accumulators of 128 columns
-// (tile t accumulates into buffer t % 2 while the epilogue drains the other)
-// and four A stages of 64 columns (128 real inputs each).  The pair walks the
-// tiles tile = pair, pair + pairs, ... (persistent grid of one pair per two
-// SMs).
+// Memory: an 8-stage shared-memory ring (x and W of 32 input quaternions per
+// stage, about 2 us of UMMA work in flight), and in each CTA's tensor memory
+// (512 columns) two accumulators of 128 columns (tile t accumulates into
+// buffer t % 2 while the epilogue drains the other) and a 4-stage ring of
+// expanded weight rows (64 columns per stage).  The pair walks the tiles
+// tile = pair, pair + pairs, ... (persistent grid of one pair per two SMs).
 //
 // Roles (320 threads per CTA):
-//   warp 0, lane 0   TMA producer of this CTA's x half-tiles (both CTAs)
+//   warp 0, lane 0   TMA producer of this CTA's x half-tiles and W tiles
 //   warp 1           tensor-memory allocation (both CTAs); lane 0 issues the
-//                    UMMAs in the even CTA, and in the odd CTA forwards "my
-//                    x stage and my A stage are ready" to the even CTA
+//                    UMMAs in the even CTA, and in the odd CTA tells the even
+//                    CTA that a stage of its shared memory has landed
 //   warps 2-5        builders: expanded weight rows into tensor memory
 //                    (warp w writes lanes 32 (w % 4) .. +31)
 //   warps 6-9        epilogue: accumulator -> bias -> one rounding -> y
 //                    (warp w reads lanes 32 (w % 4) .. +31)
+// Tensor-memory lane 32 q + l of a CTA holds real output
+// n0 + 32 q + 4 (l % 8) + l / 8 (output quaternion 8 q + l % 8, component
+// l / 8), so that a builder warp's shared-memory reads of the swizzled W
+// tiles are free of bank conflicts.
 // Every mbarrier wait is bounded; a wait that runs out records
 // QLIN_ERR_TIMEOUT, the CTA stops issuing work, and both CTAs still meet at
 // the final cluster barrier and release their tensor memory.
@@ -58,28 +63,27 @@ constexpr int kPairRows = 128;          // real outputs per CTA (UMMA M = 256 pe
 constexpr int kPairTokens = 128;        // tokens per pair tile (UMMA N)
 constexpr int kPairHalfTokens = 64;     // tokens of x per CTA
 constexpr int kPairStageK = 128;        // real inputs per stage (32 input quaternions)
-constexpr int kPairStages = 4;
+constexpr int kPairStages = 8;          // shared-memory ring (x + W)
+constexpr int kPairAStages = 4;         // tensor-memory ring of expanded weight rows
 constexpr int kPairXAtomBytes = kPairHalfTokens * 128;        // 8 KB: 64 rows x 128 B (64 inputs)
-constexpr int kPairXStageBytes = 2 * kPairXAtomBytes;         // 16 KB
+constexpr int kPairXBytes = 2 * kPairXAtomBytes;              // 16 KB
+constexpr int kPairWTileBytes = 32 * 64;                      // one component: 32 rows x 32 inputs
+constexpr int kPairStageBytes = kPairXBytes + 4 * kPairWTileBytes;  // 24 KB
 constexpr int kPairACols = kPairStageK / 2;                   // 64 tensor-memory columns per A stage
 constexpr int kPairDCols = kPairTokens;                       // 128 columns per accumulator
 constexpr int kPairAColBase = 2 * kPairDCols;                 // A stages after the two accumulators
 constexpr int kPairEpiTokens = 16;                            // tokens per epilogue group
 constexpr int kPairEpiBufBytes = kPairEpiTokens * kPairRows * 2;  // 4 KB staging (bf16/f16)
 constexpr int kPairEpiBar = 2;                                // named barrier of the epilogue warps
-constexpr int kPairPrefetch = 3;                              // builder W stages in flight
-// Shared memory: x stages, two epilogue staging buffers, barriers; padded so
-// that only one CTA fits an SM (each CTA takes the whole tensor memory).
-constexpr int kPairXOffset = 0;
-constexpr int kPairEpiOffset = kPairStages * kPairXStageBytes;
+// Shared memory: ring stages, two epilogue staging buffers, barriers.
+constexpr int kPairEpiOffset = kPairStages * kPairStageBytes;
 constexpr int kPairBarOffset = kPairEpiOffset + 2 * kPairEpiBufBytes;
-constexpr int kPairSmemBytes = 120 * 1024;
+constexpr int kPairSmemBytes = 204 * 1024;
 static_assert(kPairBarOffset + 512 + 1024 <= kPairSmemBytes, "pair kernel shared memory");
-static_assert(kPairAColBase + kPairStages * kPairACols <= 512, "tensor memory budget");
+static_assert(kPairSmemBytes <= 232448, "fits the 227 KB opt-in shared memory");
+static_assert(kPairAColBase + kPairAStages * kPairACols <= 512, "tensor memory budget");
 
 struct PairParams {
-  const void* w[4];    // W_p [N_g, ld_w]
-  int64_t ld_w;
   const void* bias;    // [4*N_g] or null
   void* y;             // [M, ld_y]
   int64_t ld_y;
@@ -136,37 +140,22 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// mbarrier wait whose acquire is at cluster scope (the barrier may be
-// completed by the other CTA of the pair: a remote arrive or a multicast
-// UMMA commit).  Bounded like mbar_wait.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
+// Bounded mbarrier wait of this kernel.  The barrier may be completed from
+// the other CTA of the pair (a remote arrive or a multicast UMMA commit); the
+// default (CTA-scope) acquire of try_wait is used, as with the remote arrive
+// below: the data a phase announces is either written by TMA or by
+// tcgen05.st that the arriving thread has waited for, or read by UMMAs that
+// the commit reports complete.
 __device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait_cluster(bar, parity)) {
-    if (globaltimer_ns() - t0 > limit_ns) {
-      record_error(7);
-      return false;
-    }
-  }
-  return true;
+  return mbar_wait(bar, parity, limit_ns);
 }
 
-// Arrive (release, cluster scope) on the mbarrier at this shared-memory
-// offset in CTA `cta` of the cluster.
+// Arrive on the mbarrier at this shared-memory offset in CTA `cta` of the
+// cluster (default semantics: release at CTA scope; a cluster-scope release
+// here measured about 600 ns per arrive, serialising the builder warps).
 __device__ __forceinline__ void mbar_arrive_cta(uint64_t* bar, uint32_t cta) {
   const uint32_t remote = map_peer_smem(smem_u32(bar), cta);
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
 }
 
 // UMMA shared-memory descriptor of a K-major operand tile written by TMA with
@@ -183,59 +172,46 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
   return d;
 }
 
-// W_p[o, i0 .. i0+32) of this lane's (o, p): 64 bytes as four 16-byte loads
-// (zeros past K_g or past N_g; K_g is a multiple of 8).
-template <typename T>
-__device__ __forceinline__ void pair_load_w(uint4 (&v)[4], const PairParams& prm, int p, int o, int i0) {
-  const T* row = reinterpret_cast<const T*>(prm.w[p]) + (int64_t)o * prm.ld_w;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int i = i0 + 8 * c;
-    if (o < prm.N_g && i < prm.K_g) {
-      uint4 r;
-      asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                   : "l"(row + i));
-      v[c] = r;
-    } else {
-      v[c] = make_uint4(0u, 0u, 0u, 0u);
-    }
-  }
-}
-
 template <typename T, bool PEERS>
 __global__ void __launch_bounds__(kPairThreads, 1)
-qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const PairParams prm) {
+qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_wr,
+                 const __grid_constant__ CUtensorMap map_wi, const __grid_constant__ CUtensorMap map_wj,
+                 const __grid_constant__ CUtensorMap map_wk, const PairParams prm) {
   constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   constexpr uint32_t kIdesc = make_idesc_f16(256, kPairTokens, kFmt, false);
-  constexpr int S = kPairStages;
+  constexpr int S = kPairStages, SA = kPairAStages;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + kPairBarOffset);
-  uint64_t* afull = xfull + S;
-  uint64_t* empty = afull + S;
-  uint64_t* ready = empty + S;    // even CTA: the odd CTA's stage is ready
-  uint64_t* dfull = ready + S;    // [2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPairBarOffset);  // [S] x and W landed
+  uint64_t* empty = full + S;     // [S] the UMMAs of the stage completed (both CTAs)
+  uint64_t* xready = empty + S;   // [S] even CTA: the odd CTA's stage landed
+  uint64_t* afull = xready + S;   // [SA] even CTA: both CTAs' builders wrote the A stage
+  uint64_t* aempty = afull + SA;  // [SA] the UMMAs reading the A stage completed (both CTAs)
+  uint64_t* dfull = aempty + SA;  // [2]
   uint64_t* dempty = dfull + 2;   // [2], even CTA: both CTAs' epilogues drained the buffer
   uint64_t* drain = dempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* issued = const_cast<int*>(abort_flag) + 1;  // producer: x stage loads issued
+  int* issued = const_cast<int*>(abort_flag) + 1;  // producer: ring stages issued
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t cta = cluster_ctarank();     // 0: issues the UMMAs
   const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
   const int my_tiles = pair < prm.tiles ? (prm.tiles - 1 - pair) / pairs + 1 : 0;
   const int nk = prm.stages;
+  const int total = my_tiles * nk;  // ring items of this pair
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&xfull[s], 1);
-      mbar_init(&afull[s], 4);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&ready[s], 1);
+      mbar_init(&xready[s], 1);
+    }
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(&afull[s], 8);
+      mbar_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&dfull[b], 1);
@@ -246,6 +222,10 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const PairParams prm
     *issued = 0;
     fence_mbar_init();
     tma_prefetch_desc(&map_x);
+    tma_prefetch_desc(&map_wr);
+    tma_prefetch_desc(&map_wi);
+    tma_prefetch_desc(&map_wj);
+    tma_prefetch_desc(&map_wk);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, 512);
@@ -267,8 +247,9 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const PairParams prm
   };
 
   if (warp == 0) {
-    // ---------------- TMA producer: this CTA's 64 tokens of x ----------------
+    // ---------------- TMA producer: this CTA's x half-tile and W tiles ----------------
     if (lane == 0) {
+      const CUtensorMap* wmap[4] = {&map_wr, &map_wi, &map_wj, &map_wk};
       int g = 0;
       for (int j = 0; j < my_tiles && !*abort_flag; ++j) {
         int n0, m0;
@@ -280,45 +261,46 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const PairParams prm
             *abort_flag = 1;
             break;
           }
-          uint8_t* dst = smem + kPairXOffset + s * kPairXStageBytes;
-          mbar_arrive_expect_tx(&xfull[s], kPairXStageBytes);
-          tma_load_2d(dst, &map_x, &xfull[s], k * kPairStageK, mrow);
-          tma_load_2d(dst + kPairXAtomBytes, &map_x, &xfull[s], k * kPairStageK + 64, mrow);
+          uint8_t* dst = smem + s * kPairStageBytes;
+          mbar_arrive_expect_tx(&full[s], kPairStageBytes);
+          tma_load_2d(dst, &map_x, &full[s], k * kPairStageK, mrow);
+          tma_load_2d(dst + kPairXAtomBytes, &map_x, &full[s], k * kPairStageK + 64, mrow);
+#pragma unroll
+          for (int p = 0; p < 4; ++p)
+            tma_load_2d(dst + kPairXBytes + p * kPairWTileBytes, wmap[p], &full[s], k * (kPairStageK / 4), n0 / 4);
           *issued = g + 1;
         }
+        if (*abort_flag) break;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      int g = 0, tc = 0;
       bool ok = true;
       if (cta == 0) {
         // ---------------- UMMA issuer (even CTA) ----------------
-        for (int j = 0; j < my_tiles && ok; ++j, ++tc) {
+        int g = 0;
+        for (int j = 0, tc = 0; j < my_tiles && ok; ++j, ++tc) {
           const int b = tc & 1, u = tc >> 1;
           if (u > 0 && !mbar_wait_cl(&dempty[b], (u - 1) & 1)) ok = false;
           tc_fence_after();
           for (int k = 0; k < nk && ok; ++k, ++g) {
-            const int s = g % S, n = g / S;
-            if (!mbar_wait_cl(&xfull[s], n & 1) || !mbar_wait_cl(&afull[s], n & 1) ||
-                !mbar_wait_cl(&ready[s], n & 1)) {
-              ok = false;
-              break;
-            }
-            if (*abort_flag) {
+            const int s = g % S, n = g / S, sa = g % SA, na = g / SA;
+            if (!mbar_wait_cl(&full[s], n & 1) || !mbar_wait_cl(&xready[s], n & 1) ||
+                !mbar_wait_cl(&afull[sa], na & 1) || *abort_flag) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint64_t bdesc0 = smem_desc_sw128(smem + kPairXOffset + s * kPairXStageBytes);
+            const uint64_t bdesc0 = smem_desc_sw128(smem + s * kPairStageBytes);
 #pragma unroll
             for (int kk = 0; kk < kPairStageK / 16; ++kk) {
               // K16 step kk: B bytes 32 (kk % 4) into swizzle atom kk / 4; A columns 8 kk
               const uint64_t bdesc = bdesc0 + (uint64_t)((kk >> 2) * (kPairXAtomBytes >> 4)) + 2 * (kk & 3);
-              umma_pair_ts(tmem + b * kPairDCols, tmem + kPairAColBase + s * kPairACols + 8 * kk, bdesc, kIdesc,
+              umma_pair_ts(tmem + b * kPairDCols, tmem + kPairAColBase + sa * kPairACols + 8 * kk, bdesc, kIdesc,
                            (k > 0 || kk > 0) ? 1u : 0u);
             }
             umma_commit_pair(&empty[s], 0x3);
+            umma_commit_pair(&aempty[sa], 0x3);
           }
           if (ok) umma_commit_pair(&dfull[b], 0x3);
         }
@@ -327,33 +309,28 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const PairParams prm
         umma_commit_pair(drain, 0x1);
         mbar_wait_cl(drain, 0, 50000000ull);
       } else {
-        // ---------------- odd CTA: forward stage readiness ----------------
-        for (int j = 0; j < my_tiles && ok; ++j) {
-          for (int k = 0; k < nk; ++k, ++g) {
-            const int s = g % S, n = g / S;
-            if (!mbar_wait_cl(&xfull[s], n & 1) || !mbar_wait_cl(&afull[s], n & 1) || *abort_flag) {
-              ok = false;
-              break;
-            }
-            tc_fence_before();
-            mbar_arrive_cta(&ready[s], 0);
+        // ---------------- odd CTA: tell the even CTA its stages landed ----------------
+        for (int g = 0; g < total; ++g) {
+          const int s = g % S, n = g / S;
+          if (*abort_flag || !mbar_wait_cl(&full[s], n & 1)) {
+            ok = false;
+            break;
           }
+          mbar_arrive_cta(&xready[s], 0);
         }
         if (!ok) *abort_flag = 1;
       }
     }
   } else if (warp < 6) {
     // ---------------- builders: expanded weight rows into tensor memory ----------------
-    // Lane l of builder warp w writes tensor-memory lane r = 32 (w % 4) + l,
-    // i.e. real output n0 + r = 4 o + a with o = n0/4 + 8 (w % 4) + l/4 and
-    // a = l % 4.  It loads W_a[o, stage's 32 inputs] and takes W_{a^q} for
-    // q = 1..3 from the lanes of its output quaternion (shuffles).
+    // Lane l of builder warp w writes tensor-memory lane 32 q + l (q = w % 4):
+    // output quaternion o = n0/4 + 8 q + l % 8, component a = l / 8.  It reads
+    // W_a[o, stage's 32 inputs] from the stage's swizzled W tile and takes
+    // W_{a^q'} (q' = 1..3) from lanes l ^ 8 q' (same o).
     const int quarter = warp & 3;
-    const int a = lane & 3;
-    const int o_local = 8 * quarter + (lane >> 2);
-    // sign bits of the four values of an input quaternion in this row:
-    // value q is s(a, a^q) * W_{a^q}
-    uint32_t sg01 = 0, sg23 = 0;
+    const int a = lane >> 3;
+    const int row = 8 * quarter + (lane & 7);  // row of the 32-row W tiles
+    uint32_t sg01, sg23;  // sign bits of values q = 0..3 of an input quaternion: s(a, a^q)
     {
       auto neg = [&](int q) {
         const int p = a ^ q;
@@ -362,78 +339,55 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const PairParams prm
       sg01 = (neg(0) ? 0x8000u : 0u) | (neg(1) ? 0x80000000u : 0u);
       sg23 = (neg(2) ? 0x8000u : 0u) | (neg(3) ? 0x80000000u : 0u);
     }
-    const int total = my_tiles * nk;
-    auto item = [&](int g, int& o, int& i0) {
-      const int j = g / nk, k = g - j * nk;
-      int n0, m0;
-      tile_coords(pair + j * pairs, n0, m0);
-      o = n0 / 4 + o_local;
-      i0 = k * (kPairStageK / 4);
-    };
-    uint4 wbuf[kPairPrefetch][4];
+    const uint32_t tm_lane = (uint32_t)(32 * quarter) << 16;
+    for (int g = 0; g < total; ++g) {
+      const int s = g % S, n = g / S, sa = g % SA, na = g / SA;
+      bool ok = !*abort_flag && mbar_wait_cl(&full[s], n & 1);
+      if (ok && na > 0) ok = mbar_wait_cl(&aempty[sa], (na - 1) & 1);
+      if (!ok) *abort_flag = 1;
+      if (!*abort_flag) {
+        // W_a[o, 32 inputs]: 64 bytes, chunk c at chunk c ^ ((row >> 1) & 3) (64-byte swizzle)
+        const uint32_t wrow = smem_u32(smem + s * kPairStageBytes + kPairXBytes + a * kPairWTileBytes + row * 64);
+        uint32_t w0[16];
 #pragma unroll
-    for (int d = 0; d < kPairPrefetch; ++d) {
-      if (d < total) {
-        int o, i0;
-        item(d, o, i0);
-        pair_load_w<T>(wbuf[d], prm, a, o, i0);
-      }
-    }
-    for (int g0 = 0; g0 < total; g0 += kPairPrefetch) {
-#pragma unroll
-      for (int d = 0; d < kPairPrefetch; ++d) {
-        const int g = g0 + d;
-        if (g < total && !*abort_flag) {
-          const int s = g % S, n = g / S;
-          // W_{a^q} words of this row's output quaternion (q = 0 is this lane's own)
-          uint32_t wq[4][16];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            wq[0][4 * c + 0] = wbuf[d][c].x;
-            wq[0][4 * c + 1] = wbuf[d][c].y;
-            wq[0][4 * c + 2] = wbuf[d][c].z;
-            wq[0][4 * c + 3] = wbuf[d][c].w;
-          }
-#pragma unroll
-          for (int q = 1; q < 4; ++q)
-#pragma unroll
-            for (int e = 0; e < 16; ++e) wq[q][e] = __shfl_sync(0xffffffffu, wq[0][e], lane ^ q);
-          // refill: the item kPairPrefetch further on reuses this buffer
-          if (g + kPairPrefetch < total) {
-            int o, i0;
-            item(g + kPairPrefetch, o, i0);
-            pair_load_w<T>(wbuf[d], prm, a, o, i0);
-          }
-          if (n > 0 && !mbar_wait_cl(&empty[s], (n - 1) & 1)) *abort_flag = 1;
-          if (!*abort_flag) {
-            // columns 2i, 2i+1 of input quaternion i: (v0, v1), (v2, v3)
-            const uint32_t col = tmem + ((uint32_t)(32 * quarter) << 16) + kPairAColBase + s * kPairACols;
-#pragma unroll
-            for (int hblk = 0; hblk < 2; ++hblk) {
-              uint32_t r[32];
-#pragma unroll
-              for (int ii = 0; ii < 16; ++ii) {
-                const int i = 16 * hblk + ii;  // input quaternion within the stage
-                const int e = i >> 1;
-                const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
-                r[2 * ii] = __byte_perm(wq[0][e], wq[1][e], sel) ^ sg01;
-                r[2 * ii + 1] = __byte_perm(wq[2][e], wq[3][e], sel) ^ sg23;
-              }
-              tmem_st32(col + 32 * hblk, r);
-            }
-            tmem_st_wait();
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&afull[s]);
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t addr = wrow + ((c ^ ((row >> 1) & 3)) << 4);
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(w0[4 * c]), "=r"(w0[4 * c + 1]), "=r"(w0[4 * c + 2]), "=r"(w0[4 * c + 3])
+                       : "r"(addr)
+                       : "memory");
         }
+        const uint32_t col = tmem + tm_lane + kPairAColBase + sa * kPairACols;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          // input quaternions 16 h .. 16 h + 15: words 8 h .. 8 h + 7
+          uint32_t r[32];
+#pragma unroll
+          for (int e8 = 0; e8 < 8; ++e8) {
+            const int e = 8 * h + e8;
+            const uint32_t v0 = w0[e];
+            const uint32_t v1 = __shfl_xor_sync(0xffffffffu, v0, 8);
+            const uint32_t v2 = __shfl_xor_sync(0xffffffffu, v0, 16);
+            const uint32_t v3 = __shfl_xor_sync(0xffffffffu, v0, 24);
+            // word e holds input quaternions 2e (low half) and 2e + 1 (high half)
+            r[4 * e8 + 0] = __byte_perm(v0, v1, 0x5410) ^ sg01;
+            r[4 * e8 + 1] = __byte_perm(v2, v3, 0x5410) ^ sg23;
+            r[4 * e8 + 2] = __byte_perm(v0, v1, 0x7632) ^ sg01;
+            r[4 * e8 + 3] = __byte_perm(v2, v3, 0x7632) ^ sg23;
+          }
+          tmem_st32(col + 32 * h, r);
+        }
+        tmem_st_wait();
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(&afull[sa], 0);
     }
   } else {
     // ---------------- epilogue ----------------
     const int quarter = warp & 3;
     const int et = threadIdx.x - 192;  // 0..127
-    const int n_local = 32 * quarter + lane;
+    const int n_local = 32 * quarter + 4 * (lane & 7) + (lane >> 3);
     T* __restrict__ y = reinterpret_cast<T*>(prm.y);
     const T* __restrict__ bias = reinterpret_cast<const T*>(prm.bias);
     for (int j = 0, tc = 0; j < my_tiles; ++j, ++tc) {
@@ -486,9 +440,9 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const PairParams prm
   // ---------------- teardown ----------------
   __syncwarp();
   if (threadIdx.x == 0 && *abort_flag) {
-    // let issued x loads land before the shared memory goes away
+    // let issued TMA loads land before the shared memory goes away
     const int g1 = *issued;
-    for (int g = g1 - S > 0 ? g1 - S : 0; g < g1; ++g) mbar_wait_cl(&xfull[g % S], (g / S) & 1, 50000000ull);
+    for (int g = g1 - S > 0 ? g1 - S : 0; g < g1; ++g) mbar_wait_cl(&full[g % S], (g / S) & 1, 50000000ull);
   }
   tc_fence_before();
   __syncthreads();

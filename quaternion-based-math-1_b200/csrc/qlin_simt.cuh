@@ -169,7 +169,7 @@ qlin_planarize_kernel(const T* __restrict__ x, int64_t ld_x, T* __restrict__ xp,
   uint32_t w[16];
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    const uint4 v = __ldg(src + c);
+    const uint4 v = ld_cg_v4(src + c);
     w[4 * c + 0] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
   }
   // word 2j holds components (r, i) of quaternion j, word 2j+1 holds (j, k).
@@ -219,7 +219,7 @@ qlin_prologue_kernel(const T* __restrict__ x, int64_t ld_x, T* __restrict__ xp, 
     uint32_t w[16];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const uint4 v = __ldg(src + c);
+      const uint4 v = ld_cg_v4(src + c);
       w[4 * c + 0] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
     }
     const int64_t plane = M * K_g;
@@ -258,7 +258,7 @@ qlin_prologue_kernel(const T* __restrict__ x, int64_t ld_x, T* __restrict__ xp, 
 #pragma unroll
       for (int r = 0; r < RR; ++r)
         ua[h][r] = (v < nvec && r0 + r < rank)
-                       ? __ldcg(reinterpret_cast<const uint4*>(lora_a + (int64_t)(r0 + r) * K) + v)
+                       ? ld_cg_v4(reinterpret_cast<const uint4*>(lora_a + (int64_t)(r0 + r) * K) + v)
                        : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
@@ -268,7 +268,7 @@ qlin_prologue_kernel(const T* __restrict__ x, int64_t ld_x, T* __restrict__ xp, 
 #pragma unroll
       for (int h = 0; h < U; ++h) {
         const int64_t v = v0 + h * (int64_t)blockDim.x;
-        ux[h] = v < nvec ? __ldcg(reinterpret_cast<const uint4*>(x + (m0 + t) * ld_x) + v)
+        ux[h] = v < nvec ? ld_cg_v4(reinterpret_cast<const uint4*>(x + (m0 + t) * ld_x) + v)
                          : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll

@@ -475,7 +475,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
             const bool live = m < prm.M && gbase < prm.K_g;
             const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(live ? m : 0) * prm.ld_x + 4 * (live ? gbase : 0));
 #pragma unroll
-            for (int c = 0; c < 4; ++c) ld[k][c] = live ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
+            for (int c = 0; c < 4; ++c) ld[k][c] = live ? ld_cg_v4(src + c) : make_uint4(0u, 0u, 0u, 0u);
           }
 #pragma unroll
           for (int k = 0; k < kBatch; ++k) {
@@ -577,7 +577,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
       for (int j = 0; j < 2; ++j) {
         const int eo = 256 * j + 8 * lane, e = ebase + eo;
         xv[m][j] = (m < m_tile && eo < E && e < lim)
-                       ? __ldg(reinterpret_cast<const uint4*>(x + (int64_t)(t0 + m) * prm.ld_x + e))
+                       ? ld_cg_v4(x + (int64_t)(t0 + m) * prm.ld_x + e)
                        : make_uint4(0u, 0u, 0u, 0u);
       }
     // the lora_a slice: [piece j][rank][256 elements], rows past rank zero
@@ -763,7 +763,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
             float4 vs[kTcMaxSplit];
   #pragma unroll
             for (int sp = 0; sp < kTcMaxSplit; ++sp)
-              vs[sp] = sp < prm.split_k ? __ldcg(prm.partials + (size_t)sp * slot_stride + tile_off +
+              vs[sp] = sp < prm.split_k ? ld_cg_f4(prm.partials + (size_t)sp * slot_stride + tile_off +
                                                  tok * kTcBlockO + o_local)
                                         : make_float4(0.f, 0.f, 0.f, 0.f);
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);

@@ -43,7 +43,8 @@ def _reference(qb, layers, x):
     return x
 
 
-@pytest.mark.parametrize("M,lora", [(1, False), (1, True), (2, True), (16, True), (100, False), (200, True)])
+@pytest.mark.parametrize("M,lora", [(1, False), (1, True), (2, True), (3, True), (4, True), (16, True),
+                                    (100, False), (200, True), (300, False)])
 @pytest.mark.parametrize("static", [False, True])
 def test_dependent_chain_eager_and_graph(qb, cuda, M, lora, static):
     layers, x = _layers(qb, cuda, 12, 512, M, lora)
@@ -60,10 +61,13 @@ def test_dependent_chain_eager_and_graph(qb, cuda, M, lora, static):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         out = _chain(qb, layers, x, static)
+    # checked after the first replay: later replays would find each layer's
+    # input already holding the right values and could hide a layer that
+    # reads its input before the previous layer has written it
     for _ in range(3):
         graph.replay()
-    torch.cuda.synchronize()
-    assert torch.equal(out, want)
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
     assert qb.device_error(cuda) == 0
 
 
