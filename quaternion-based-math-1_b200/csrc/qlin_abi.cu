@@ -39,9 +39,9 @@ struct DeviceInfo {
   int cluster_cap[2][3][kTcClusterMax + 1];
   // CUDA-core decode kernel: shared-memory limit raised, by [dtype][MT][LoRA][peers]
   bool gemv_attr_set[2][3][2][2] = {};
-  // CTA-pair prefill kernel: attributes set and how many pairs fit at once, by [dtype][peers]
-  bool pair_attr_set[2][2] = {};
-  int pair_cap[2][2] = {};
+  // CTA-pair prefill kernel: attributes set and how many pairs fit at once, by [dtype][peers][tile]
+  bool pair_attr_set[2][2][2] = {};
+  int pair_cap[2][2][2] = {};
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mutex;
@@ -440,13 +440,13 @@ bool pair_eligible(int64_t M, int64_t N_g, int rank, const void* y, int64_t ld_y
          ld_y % 8 == 0 && aligned(y, 16);
 }
 
-template <typename T, bool PEERS>
+template <typename T, bool PEERS, int NTOK>
 int pair_attrs(DeviceInfo* dev, int* cap) {
   const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
-  const int pi = PEERS ? 1 : 0;
+  const int pi = PEERS ? 1 : 0, ti = NTOK == 256 ? 1 : 0;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (!dev->pair_attr_set[di][pi]) {
-    auto kernel = qlin_pair_kernel<T, PEERS>;
+  if (!dev->pair_attr_set[di][pi][ti]) {
+    auto kernel = qlin_pair_kernel<T, PEERS, NTOK>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes) != cudaSuccess)
       return QLIN_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
@@ -465,34 +465,40 @@ int pair_attrs(DeviceInfo* dev, int* cap) {
       cudaGetLastError();
       return QLIN_ERR_LAUNCH;
     }
-    dev->pair_cap[di][pi] = n;
-    dev->pair_attr_set[di][pi] = true;
+    dev->pair_cap[di][pi][ti] = n;
+    dev->pair_attr_set[di][pi][ti] = true;
   }
-  *cap = dev->pair_cap[di][pi];
+  *cap = dev->pair_cap[di][pi][ti];
   return QLIN_OK;
 }
 
-// Tiles of the CTA-pair kernel: 256 real outputs x 128 tokens.
-inline int64_t pair_tiles(int64_t M, int64_t N_g) { return ((4 * N_g + 255) / 256) * ((M + 127) / 128); }
+// Tokens per tile of the CTA-pair kernel: 256 (one accumulator, 128 cycles
+// per UMMA) above 128 tokens, else 128.
+inline int pair_tokens(int64_t M) { return M > 128 ? 256 : 128; }
 
-template <typename T>
-int run_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
-             T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, cudaStream_t stream) {
-  if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
+// Tiles of the CTA-pair kernel: 256 real outputs x pair_tokens(M) tokens.
+inline int64_t pair_tiles(int64_t M, int64_t N_g) {
+  const int64_t nt = pair_tokens(M);
+  return ((4 * N_g + 255) / 256) * ((M + nt - 1) / nt);
+}
+
+template <typename T, int NTOK>
+int launch_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
+                T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, cudaStream_t stream) {
   int cap = 0;
-  int st = pair_attrs<T, false>(dev, &cap);
+  int st = pair_attrs<T, false, NTOK>(dev, &cap);
   if (st != QLIN_OK) return st;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  // x [M, 4*K_g]: 64-element x 64-token boxes, 128-byte swizzle (the UMMA B
-  // operand); W_p [N_g, K_g]: 32-element x 32-row boxes, 64-byte swizzle (read
-  // by the builder warps).  Out-of-range rows and columns read as zero.
+  // x [M, 4*K_g]: 64-element x NTOK/2-token boxes, 128-byte swizzle (the UMMA
+  // B operand); W_p [N_g, K_g]: 32-element x 32-row boxes, 64-byte swizzle
+  // (read by the builder warps).  Out-of-range rows and columns read as zero.
   CUtensorMap maps[5];
   std::memset(maps, 0, sizeof(maps));
   {
     cuuint64_t dims[2] = {(cuuint64_t)(4 * K_g), (cuuint64_t)M};
     cuuint64_t strides[1] = {(cuuint64_t)(ld_x * 2)};
-    cuuint32_t box[2] = {64, (cuuint32_t)kPairHalfTokens};
+    cuuint32_t box[2] = {64, (cuuint32_t)PairCfg<NTOK>::kHalf};
     if (encode(&maps[0], dt, 2, const_cast<T*>(x), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
       return QLIN_ERR_ALIGN;
   }
@@ -532,10 +538,18 @@ int run_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], 
   cfg.stream = stream;
   cfg.attrs = attrs;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, qlin_pair_kernel<T, false>, maps[0], maps[1], maps[2], maps[3], maps[4], prm) ==
-                 cudaSuccess
+  return cudaLaunchKernelEx(&cfg, qlin_pair_kernel<T, false, NTOK>, maps[0], maps[1], maps[2], maps[3], maps[4],
+                            prm) == cudaSuccess
              ? QLIN_OK
              : QLIN_ERR_LAUNCH;
+}
+
+template <typename T>
+int run_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
+             T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, cudaStream_t stream) {
+  if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
+  return pair_tokens(M) == 256 ? launch_pair<T, 256>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, stream)
+                               : launch_pair<T, 128>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, stream);
 }
 
 template <typename T>
@@ -956,10 +970,13 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flag
              !(flags & QLIN_FLAG_NO_PAIR)) {
     // the CTA-pair kernel (assuming a 16-byte aligned output)
     int cap = 0;
-    st = dtype == QLIN_BF16 ? pair_attrs<__nv_bfloat16, false>(dev, &cap) : pair_attrs<__half, false>(dev, &cap);
+    const bool big = pair_tokens(M) == 256;
+    st = dtype == QLIN_BF16 ? (big ? pair_attrs<__nv_bfloat16, false, 256>(dev, &cap)
+                                   : pair_attrs<__nv_bfloat16, false, 128>(dev, &cap))
+                            : (big ? pair_attrs<__half, false, 256>(dev, &cap) : pair_attrs<__half, false, 128>(dev, &cap));
     if (st != QLIN_OK) return st;
     a = QLIN_PLAN_TC_PAIR;
-    nt = kPairTokens;
+    nt = pair_tokens(M);
     nl = 1;
     res = 2 * (int)std::min<int64_t>(pair_tiles(M, N_g), cap);
   } else if (a == QLIN_ALGO_TC) {

@@ -18,29 +18,36 @@
 // no prologue kernel.
 //
 // Tile of one CTA pair (a 2-CTA cluster): 256 real outputs (64 output
-// quaternions; 128 rows of Wd in each CTA's tensor memory) x 128 tokens
-// (64 tokens of x in each CTA's shared memory).  One UMMA of M = 256,
-// N = 128, K = 16 per step, issued by the pair's even CTA, reads A from both
+// quaternions; 128 rows of Wd in each CTA's tensor memory) x NTOK tokens
+// (NTOK / 2 tokens of x in each CTA's shared memory).  One UMMA of M = 256,
+// N = NTOK, K = 16 per step, issued by the pair's even CTA, reads A from both
 // CTAs' tensor memory and B from both CTAs' shared memory and accumulates
 // into both CTAs' tensor memory (each CTA's 128 rows).  Per SM and UMMA step
 // the shared-memory traffic is the x half-tile written by TMA and read by the
-// UMMA plus a quarter of that for W (80 B/clk at full tensor rate, of 128);
+// UMMA plus a small W tile (at most 80 B/clk at full tensor rate, of 128);
 // the expanded weight operand costs tensor-memory stores, not shared memory.
 //
-// Memory: an 8-stage shared-memory ring (x and W of 32 input quaternions per
-// stage, about 2 us of UMMA work in flight), and in each CTA's tensor memory
-// (512 columns) two accumulators of 128 columns (tile t accumulates into
-// buffer t % 2 while the epilogue drains the other) and a 4-stage ring of
-// expanded weight rows (64 columns per stage).  The pair walks the tiles
+// The issuing thread spends about 60-130 cycles on every tcgen05
+// instruction, barrier wait and fence (measured), so the bookkeeping per
+// stage is kept to one barrier wait and two commits around eight UMMAs, and
+// the large tile (NTOK = 256, 128 cycles per UMMA) is the prefill shape:
+// its single accumulator (256 columns) is drained into registers by the
+// epilogue first and released before the stores, so the next tile's UMMAs
+// wait only for that drain.  NTOK = 128 keeps two accumulators for smaller
+// token counts.  Tensor memory (512 columns per CTA): the accumulator(s),
+// then a 4-stage ring of expanded weight rows (64 columns = 32 input
+// quaternions per stage).  Shared memory: a ring of x half-tiles and W tiles
+// (4 stages at NTOK = 256, 8 at 128).  The pair walks the tiles
 // tile = pair, pair + pairs, ... (persistent grid of one pair per two SMs).
 //
 // Roles (320 threads per CTA):
 //   warp 0, lane 0   TMA producer of this CTA's x half-tiles and W tiles
-//   warp 1           tensor-memory allocation (both CTAs); lane 0 issues the
-//                    UMMAs in the even CTA, and in the odd CTA tells the even
-//                    CTA that a stage of its shared memory has landed
-//   warps 2-5        builders: expanded weight rows into tensor memory
-//                    (warp w writes lanes 32 (w % 4) .. +31)
+//   warp 1           tensor-memory allocation (both CTAs); lane 0 of the even
+//                    CTA issues the UMMAs
+//   warps 2-5        builders: wait for their own CTA's stage (x and W), write
+//                    expanded weight rows into tensor memory (warp w writes
+//                    lanes 32 (w % 4) .. +31) and arrive on the even CTA's
+//                    barrier -- so its one wait covers both CTAs' x and A
 //   warps 6-9        epilogue: accumulator -> bias -> one rounding -> y
 //                    (warp w reads lanes 32 (w % 4) .. +31)
 // Tensor-memory lane 32 q + l of a CTA holds real output
@@ -60,28 +67,31 @@ namespace qlin {
 
 constexpr int kPairThreads = 320;
 constexpr int kPairRows = 128;          // real outputs per CTA (UMMA M = 256 per pair)
-constexpr int kPairTokens = 128;        // tokens per pair tile (UMMA N)
-constexpr int kPairHalfTokens = 64;     // tokens of x per CTA
 constexpr int kPairStageK = 128;        // real inputs per stage (32 input quaternions)
-constexpr int kPairStages = 8;          // shared-memory ring (x + W)
 constexpr int kPairAStages = 4;         // tensor-memory ring of expanded weight rows
-constexpr int kPairXAtomBytes = kPairHalfTokens * 128;        // 8 KB: 64 rows x 128 B (64 inputs)
-constexpr int kPairXBytes = 2 * kPairXAtomBytes;              // 16 KB
 constexpr int kPairWTileBytes = 32 * 64;                      // one component: 32 rows x 32 inputs
-constexpr int kPairStageBytes = kPairXBytes + 4 * kPairWTileBytes;  // 24 KB
 constexpr int kPairACols = kPairStageK / 2;                   // 64 tensor-memory columns per A stage
-constexpr int kPairDCols = kPairTokens;                       // 128 columns per accumulator
-constexpr int kPairAColBase = 2 * kPairDCols;                 // A stages after the two accumulators
-constexpr int kPairEpiTokens = 16;                            // tokens per epilogue group
+constexpr int kPairEpiTokens = 16;                            // tokens per epilogue store group
 constexpr int kPairEpiBufBytes = kPairEpiTokens * kPairRows * 2;  // 4 KB staging (bf16/f16)
 constexpr int kPairEpiBar = 2;                                // named barrier of the epilogue warps
-// Shared memory: ring stages, two epilogue staging buffers, barriers.
-constexpr int kPairEpiOffset = kPairStages * kPairStageBytes;
-constexpr int kPairBarOffset = kPairEpiOffset + 2 * kPairEpiBufBytes;
 constexpr int kPairSmemBytes = 204 * 1024;
-static_assert(kPairBarOffset + 512 + 1024 <= kPairSmemBytes, "pair kernel shared memory");
-static_assert(kPairSmemBytes <= 232448, "fits the 227 KB opt-in shared memory");
-static_assert(kPairAColBase + kPairAStages * kPairACols <= 512, "tensor memory budget");
+
+template <int NTOK>
+struct PairCfg {
+  static_assert(NTOK == 128 || NTOK == 256, "pair tile tokens");
+  static constexpr int kHalf = NTOK / 2;                        // tokens of x per CTA
+  static constexpr int kXAtomBytes = kHalf * 128;               // kHalf rows x 128 B (64 inputs)
+  static constexpr int kXBytes = 2 * kXAtomBytes;
+  static constexpr int kStageBytes = kXBytes + 4 * kPairWTileBytes;
+  static constexpr int kStages = NTOK == 256 ? 4 : 8;           // shared-memory ring (x + W)
+  static constexpr int kDBufs = NTOK == 256 ? 1 : 2;            // accumulators
+  static constexpr int kAColBase = kDBufs * NTOK;               // A stages after the accumulator(s)
+  static constexpr int kEpiOffset = kStages * kStageBytes;
+  static constexpr int kBarOffset = kEpiOffset + 2 * kPairEpiBufBytes;
+  static_assert(kBarOffset + 512 + 1024 <= kPairSmemBytes, "pair kernel shared memory");
+  static_assert(kPairSmemBytes <= 232448, "fits the 227 KB opt-in shared memory");
+  static_assert(kAColBase + kPairAStages * kPairACols <= 512, "tensor memory budget");
+};
 
 struct PairParams {
   const void* bias;    // [4*N_g] or null
@@ -90,7 +100,7 @@ struct PairParams {
   int M, N_g, K_g;
   int stages;          // K stages per tile: ceil(K_g / 32)
   int nb_tiles;        // tiles along the outputs: ceil(4*N_g / 256)
-  int tiles;           // nb_tiles * ceil(M / 128)
+  int tiles;           // nb_tiles * ceil(M / NTOK)
   PeerOut peers;       // column-partitioned layer: every output also stored to these
 };
 
@@ -172,25 +182,49 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
   return d;
 }
 
-template <typename T, bool PEERS>
+// 32 lanes x 32 bit, 32 consecutive columns per thread (warp-collective load).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Two fp32 values -> two 16-bit values in one word (low half = a).
+template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T, bool PEERS, int NTOK>
 __global__ void __launch_bounds__(kPairThreads, 1)
 qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_wr,
                  const __grid_constant__ CUtensorMap map_wi, const __grid_constant__ CUtensorMap map_wj,
                  const __grid_constant__ CUtensorMap map_wk, const PairParams prm) {
+  using Cfg = PairCfg<NTOK>;
   constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-  constexpr uint32_t kIdesc = make_idesc_f16(256, kPairTokens, kFmt, false);
-  constexpr int S = kPairStages, SA = kPairAStages;
+  constexpr uint32_t kIdesc = make_idesc_f16(256, NTOK, kFmt, false);
+  constexpr int S = Cfg::kStages, SA = kPairAStages, NB = Cfg::kDBufs;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPairBarOffset);  // [S] x and W landed
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);  // [S] x and W of this CTA landed
   uint64_t* empty = full + S;     // [S] the UMMAs of the stage completed (both CTAs)
-  uint64_t* xready = empty + S;   // [S] even CTA: the odd CTA's stage landed
-  uint64_t* afull = xready + S;   // [SA] even CTA: both CTAs' builders wrote the A stage
+  uint64_t* afull = empty + S;    // [SA] even CTA: both CTAs' builders wrote the A stage
   uint64_t* aempty = afull + SA;  // [SA] the UMMAs reading the A stage completed (both CTAs)
-  uint64_t* dfull = aempty + SA;  // [2]
-  uint64_t* dempty = dfull + 2;   // [2], even CTA: both CTAs' epilogues drained the buffer
-  uint64_t* drain = dempty + 2;
+  uint64_t* dfull = aempty + SA;  // [NB]
+  uint64_t* dempty = dfull + NB;  // [NB], even CTA: both CTAs' epilogues drained the accumulator
+  uint64_t* drain = dempty + NB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued = const_cast<int*>(abort_flag) + 1;  // producer: ring stages issued
@@ -207,13 +241,12 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&xready[s], 1);
     }
     for (int s = 0; s < SA; ++s) {
       mbar_init(&afull[s], 8);
       mbar_init(&aempty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       mbar_init(&dfull[b], 1);
       mbar_init(&dempty[b], 8);
     }
@@ -243,7 +276,7 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
   auto tile_coords = [&](int t, int& n0, int& m0) {
     const int nb = t % prm.nb_tiles, tb = t / prm.nb_tiles;
     n0 = nb * 256 + (int)cta * kPairRows;  // this CTA's first real output
-    m0 = tb * kPairTokens;                 // the pair's first token
+    m0 = tb * NTOK;                        // the pair's first token
   };
 
   if (warp == 0) {
@@ -254,72 +287,60 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
       for (int j = 0; j < my_tiles && !*abort_flag; ++j) {
         int n0, m0;
         tile_coords(pair + j * pairs, n0, m0);
-        const int mrow = m0 + (int)cta * kPairHalfTokens;
+        const int mrow = m0 + (int)cta * Cfg::kHalf;
         for (int k = 0; k < nk; ++k, ++g) {
           const int s = g % S, n = g / S;
-          if (n > 0 && !mbar_wait_cl(&empty[s], (n - 1) & 1)) {
+          if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1)) {
             *abort_flag = 1;
             break;
           }
-          uint8_t* dst = smem + s * kPairStageBytes;
-          mbar_arrive_expect_tx(&full[s], kPairStageBytes);
+          uint8_t* dst = smem + s * Cfg::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
           tma_load_2d(dst, &map_x, &full[s], k * kPairStageK, mrow);
-          tma_load_2d(dst + kPairXAtomBytes, &map_x, &full[s], k * kPairStageK + 64, mrow);
+          tma_load_2d(dst + Cfg::kXAtomBytes, &map_x, &full[s], k * kPairStageK + 64, mrow);
 #pragma unroll
           for (int p = 0; p < 4; ++p)
-            tma_load_2d(dst + kPairXBytes + p * kPairWTileBytes, wmap[p], &full[s], k * (kPairStageK / 4), n0 / 4);
+            tma_load_2d(dst + Cfg::kXBytes + p * kPairWTileBytes, wmap[p], &full[s], k * (kPairStageK / 4), n0 / 4);
           *issued = g + 1;
         }
         if (*abort_flag) break;
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && cta == 0) {
+      // ---------------- UMMA issuer (even CTA) ----------------
       bool ok = true;
-      if (cta == 0) {
-        // ---------------- UMMA issuer (even CTA) ----------------
-        int g = 0;
-        for (int j = 0, tc = 0; j < my_tiles && ok; ++j, ++tc) {
-          const int b = tc & 1, u = tc >> 1;
-          if (u > 0 && !mbar_wait_cl(&dempty[b], (u - 1) & 1)) ok = false;
-          tc_fence_after();
-          for (int k = 0; k < nk && ok; ++k, ++g) {
-            const int s = g % S, n = g / S, sa = g % SA, na = g / SA;
-            if (!mbar_wait_cl(&full[s], n & 1) || !mbar_wait_cl(&xready[s], n & 1) ||
-                !mbar_wait_cl(&afull[sa], na & 1) || *abort_flag) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint64_t bdesc0 = smem_desc_sw128(smem + s * kPairStageBytes);
-#pragma unroll
-            for (int kk = 0; kk < kPairStageK / 16; ++kk) {
-              // K16 step kk: B bytes 32 (kk % 4) into swizzle atom kk / 4; A columns 8 kk
-              const uint64_t bdesc = bdesc0 + (uint64_t)((kk >> 2) * (kPairXAtomBytes >> 4)) + 2 * (kk & 3);
-              umma_pair_ts(tmem + b * kPairDCols, tmem + kPairAColBase + sa * kPairACols + 8 * kk, bdesc, kIdesc,
-                           (k > 0 || kk > 0) ? 1u : 0u);
-            }
-            umma_commit_pair(&empty[s], 0x3);
-            umma_commit_pair(&aempty[sa], 0x3);
-          }
-          if (ok) umma_commit_pair(&dfull[b], 0x3);
-        }
-        if (!ok) *abort_flag = 1;
-        // every UMMA issued above has completed before the teardown
-        umma_commit_pair(drain, 0x1);
-        mbar_wait_cl(drain, 0, 50000000ull);
-      } else {
-        // ---------------- odd CTA: tell the even CTA its stages landed ----------------
-        for (int g = 0; g < total; ++g) {
-          const int s = g % S, n = g / S;
-          if (*abort_flag || !mbar_wait_cl(&full[s], n & 1)) {
+      int g = 0;
+      for (int j = 0; j < my_tiles && ok; ++j) {
+        const int b = j % NB, u = j / NB;
+        if (u > 0 && !mbar_wait(&dempty[b], (u - 1) & 1)) ok = false;
+        tc_fence_after();
+        for (int k = 0; k < nk && ok; ++k, ++g) {
+          const int s = g % S, sa = g % SA, na = g / SA;
+          // both CTAs' builders arrive only after their own CTA's x and W of
+          // this stage landed: this one wait covers the B operand too
+          if (!mbar_wait(&afull[sa], na & 1) || *abort_flag) {
             ok = false;
             break;
           }
-          mbar_arrive_cta(&xready[s], 0);
+          tc_fence_after();
+          const uint64_t bdesc0 = smem_desc_sw128(smem + s * Cfg::kStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kPairStageK / 16; ++kk) {
+            // K16 step kk: B bytes 32 (kk % 4) into swizzle atom kk / 4; A columns 8 kk
+            const uint64_t bdesc = bdesc0 + (uint64_t)((kk >> 2) * (Cfg::kXAtomBytes >> 4)) + 2 * (kk & 3);
+            umma_pair_ts(tmem + b * NTOK, tmem + Cfg::kAColBase + sa * kPairACols + 8 * kk, bdesc, kIdesc,
+                         (k > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[s], 0x3);
+          umma_commit_pair(&aempty[sa], 0x3);
         }
-        if (!ok) *abort_flag = 1;
+        if (ok) umma_commit_pair(&dfull[b], 0x3);
       }
+      if (!ok) *abort_flag = 1;
+      // every UMMA issued above has completed before the teardown
+      umma_commit_pair(drain, 0x1);
+      mbar_wait(drain, 0, 50000000ull);
     }
   } else if (warp < 6) {
     // ---------------- builders: expanded weight rows into tensor memory ----------------
@@ -342,12 +363,13 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
     const uint32_t tm_lane = (uint32_t)(32 * quarter) << 16;
     for (int g = 0; g < total; ++g) {
       const int s = g % S, n = g / S, sa = g % SA, na = g / SA;
-      bool ok = !*abort_flag && mbar_wait_cl(&full[s], n & 1);
-      if (ok && na > 0) ok = mbar_wait_cl(&aempty[sa], (na - 1) & 1);
+      bool ok = !*abort_flag && mbar_wait(&full[s], n & 1);
+      if (ok && na > 0) ok = mbar_wait(&aempty[sa], (na - 1) & 1);
       if (!ok) *abort_flag = 1;
       if (!*abort_flag) {
         // W_a[o, 32 inputs]: 64 bytes, chunk c at chunk c ^ ((row >> 1) & 3) (64-byte swizzle)
-        const uint32_t wrow = smem_u32(smem + s * kPairStageBytes + kPairXBytes + a * kPairWTileBytes + row * 64);
+        const uint32_t wrow =
+            smem_u32(smem + s * Cfg::kStageBytes + Cfg::kXBytes + a * kPairWTileBytes + row * 64);
         uint32_t w0[16];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -357,7 +379,7 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
                        : "r"(addr)
                        : "memory");
         }
-        const uint32_t col = tmem + tm_lane + kPairAColBase + sa * kPairACols;
+        const uint32_t col = tmem + tm_lane + Cfg::kAColBase + sa * kPairACols;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           // input quaternions 16 h .. 16 h + 15: words 8 h .. 8 h + 7
@@ -385,30 +407,53 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
     }
   } else {
     // ---------------- epilogue ----------------
+    // Drain the accumulator into registers (bias added, rounded, two tokens
+    // per word), release it to the UMMA issuer, then store through a
+    // shared-memory transpose: 16 tokens x 128 outputs per group, 16 bytes per
+    // thread and store.
     const int quarter = warp & 3;
     const int et = threadIdx.x - 192;  // 0..127
     const int n_local = 32 * quarter + 4 * (lane & 7) + (lane >> 3);
     T* __restrict__ y = reinterpret_cast<T*>(prm.y);
     const T* __restrict__ bias = reinterpret_cast<const T*>(prm.bias);
-    for (int j = 0, tc = 0; j < my_tiles; ++j, ++tc) {
-      const int b = tc & 1, u = tc >> 1;
+    for (int j = 0; j < my_tiles; ++j) {
+      const int b = j % NB, u = j / NB;
       int n0, m0;
       tile_coords(pair + j * pairs, n0, m0);
-      const bool got = !*abort_flag && mbar_wait_cl(&dfull[b], u & 1);
+      const bool got = !*abort_flag && mbar_wait(&dfull[b], u & 1);
       if (!got) *abort_flag = 1;
       tc_fence_after();
       const int n = n0 + n_local;
       const float bv = (bias && n < 4 * prm.N_g) ? to_f32(bias[n]) : 0.f;
-#pragma unroll 1
-      for (int grp = 0; grp < kPairTokens / kPairEpiTokens; ++grp) {
-        T* stage = reinterpret_cast<T*>(smem + kPairEpiOffset + (grp & 1) * kPairEpiBufBytes);
-        if (got) {
-          float v[16];
-          __syncwarp();
-          tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + b * kPairDCols + kPairEpiTokens * grp, v);
-          tmem_ld_wait();
+      uint32_t packed[NTOK / 2];
 #pragma unroll
-          for (int t = 0; t < kPairEpiTokens; ++t) stage[t * kPairRows + n_local] = from_f32<T>(v[t] + bv);
+      for (int c = 0; c < NTOK / 32; ++c) {
+        uint32_t v[32];
+        if (got) {
+          __syncwarp();
+          tmem_ld32(tmem + ((uint32_t)(32 * quarter) << 16) + b * NTOK + 32 * c, v);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) v[t] = 0u;
+        }
+#pragma unroll
+        for (int t = 0; t < 16; ++t)
+          packed[16 * c + t] = pack2<T>(__uint_as_float(v[2 * t]) + bv, __uint_as_float(v[2 * t + 1]) + bv);
+      }
+      // this warp has read its lanes of the accumulator: the even CTA may reuse it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(&dempty[b], 0);
+#pragma unroll
+      for (int grp = 0; grp < NTOK / kPairEpiTokens; ++grp) {
+        T* stage = reinterpret_cast<T*>(smem + Cfg::kEpiOffset + (grp & 1) * kPairEpiBufBytes);
+        unsigned short* st16 = reinterpret_cast<unsigned short*>(stage);
+#pragma unroll
+        for (int t2 = 0; t2 < kPairEpiTokens / 2; ++t2) {
+          const uint32_t wv = packed[(kPairEpiTokens / 2) * grp + t2];
+          st16[(2 * t2) * kPairRows + n_local] = (unsigned short)(wv & 0xffffu);
+          st16[(2 * t2 + 1) * kPairRows + n_local] = (unsigned short)(wv >> 16);
         }
         asm volatile("bar.sync %0, %1;" ::"n"(kPairEpiBar), "n"(128) : "memory");
         if (got) {
@@ -429,10 +474,6 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
           }
         }
       }
-      // this warp has read its lanes of buffer b: the even CTA may reuse it
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cta(&dempty[b], 0);
     }
     if (PEERS) fence_sys();
   }
@@ -442,7 +483,7 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
   if (threadIdx.x == 0 && *abort_flag) {
     // let issued TMA loads land before the shared memory goes away
     const int g1 = *issued;
-    for (int g = g1 - S > 0 ? g1 - S : 0; g < g1; ++g) mbar_wait_cl(&full[g % S], (g / S) & 1, 50000000ull);
+    for (int g = g1 - S > 0 ? g1 - S : 0; g < g1; ++g) mbar_wait(&full[g % S], (g / S) & 1, 50000000ull);
   }
   tc_fence_before();
   __syncthreads();
