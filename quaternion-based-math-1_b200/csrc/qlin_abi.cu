@@ -431,13 +431,17 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
 }
 
 // The CTA-pair kernel (qlin_pair.cuh) takes prefill-sized problems without
-// LoRA or peer outputs: more than kStackMaxTokens tokens, 16-byte output
-// pieces (ld_y a multiple of 8, 16-byte aligned y, an even number of output
-// quaternions) on top of the tensor-core path's TMA rules.
+// LoRA: more than kStackMaxTokens tokens, 16-byte output pieces (ld_y a
+// multiple of 8, 16-byte aligned y and peer outputs, an even number of
+// output quaternions) on top of the tensor-core path's TMA rules.
 bool pair_eligible(int64_t M, int64_t N_g, int rank, const void* y, int64_t ld_y, const PeerOut& peers,
                    int flags) {
-  return M > kStackMaxTokens && rank == 0 && peers.n == 0 && !(flags & QLIN_FLAG_NO_PAIR) && N_g % 2 == 0 &&
-         ld_y % 8 == 0 && aligned(y, 16);
+  if (M <= kStackMaxTokens || rank != 0 || (flags & QLIN_FLAG_NO_PAIR) || N_g % 2 != 0 || ld_y % 8 != 0 ||
+      !aligned(y, 16))
+    return false;
+  for (int p = 0; p < peers.n; ++p)
+    if (!aligned(peers.y[p], 16)) return false;
+  return true;
 }
 
 template <typename T, bool PEERS, int NTOK>
@@ -482,11 +486,12 @@ inline int64_t pair_tiles(int64_t M, int64_t N_g) {
   return ((4 * N_g + 255) / 256) * ((M + nt - 1) / nt);
 }
 
-template <typename T, int NTOK>
+template <typename T, bool PEERS, int NTOK>
 int launch_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
-                T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, cudaStream_t stream) {
+                T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, const PeerOut& peers,
+                cudaStream_t stream) {
   int cap = 0;
-  int st = pair_attrs<T, false, NTOK>(dev, &cap);
+  int st = pair_attrs<T, PEERS, NTOK>(dev, &cap);
   if (st != QLIN_OK) return st;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -522,7 +527,7 @@ int launch_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4
   prm.stages = (int)((K_g + 31) / 32);
   prm.nb_tiles = (int)((4 * N_g + 255) / 256);
   prm.tiles = (int)tiles;
-  prm.peers.n = 0;
+  prm.peers = peers;
   const int64_t pairs = std::min<int64_t>(tiles, cap);
   cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -538,18 +543,24 @@ int launch_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4
   cfg.stream = stream;
   cfg.attrs = attrs;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, qlin_pair_kernel<T, false, NTOK>, maps[0], maps[1], maps[2], maps[3], maps[4],
+  return cudaLaunchKernelEx(&cfg, qlin_pair_kernel<T, PEERS, NTOK>, maps[0], maps[1], maps[2], maps[3], maps[4],
                             prm) == cudaSuccess
              ? QLIN_OK
              : QLIN_ERR_LAUNCH;
 }
 
+// Peer outputs (column-partitioned layer) get the kernel variant that also
+// stores every output piece into them.
 template <typename T>
 int run_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
-             T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, cudaStream_t stream) {
+             T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, const PeerOut& peers, cudaStream_t stream) {
   if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
-  return pair_tokens(M) == 256 ? launch_pair<T, 256>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, stream)
-                               : launch_pair<T, 128>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, stream);
+  const bool big = pair_tokens(M) == 256;
+  if (peers.n > 0)
+    return big ? launch_pair<T, true, 256>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, peers, stream)
+               : launch_pair<T, true, 128>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, peers, stream);
+  return big ? launch_pair<T, false, 256>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, peers, stream)
+             : launch_pair<T, false, 128>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, peers, stream);
 }
 
 template <typename T>
@@ -558,7 +569,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
            int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, uint8_t* ws, int flags,
            const PeerOut& peers, cudaStream_t stream) {
   if (pair_eligible(M, N_g, rank, y, ld_y, peers, flags))
-    return run_pair<T>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, stream);
+    return run_pair<T>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, peers, stream);
   if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

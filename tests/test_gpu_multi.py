@@ -48,7 +48,9 @@ def _rank_main(rank, port, out_q):
     ok = False
     try:
         results = []
-        for (M, fin, fout, rank_l) in [(1, 1024, 1024, 16), (16, 512, 520, 0), (300, 768, 1040, 8)]:
+        # the last case runs the fused path on the CTA-pair kernel (no LoRA, > 64 tokens)
+        for (M, fin, fout, rank_l) in [(1, 1024, 1024, 16), (16, 512, 520, 0), (300, 768, 1040, 8),
+                                       (600, 512, 2080, 0)]:
             g = torch.Generator().manual_seed(fin + fout)
             full = qb.QuaternionLinear(fin, fout, bias=True, device=dev, dtype=torch.bfloat16)
             with torch.no_grad():
