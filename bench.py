@@ -786,7 +786,7 @@ def _entry(qb, wl, torch, dev, name, K, W, peaks, with_clocks=False):
     us = ms * 1e3 / kk
     nb, fl = algorithmic_work(lay)
     e = {"value": us, "unit": "us/call", "steps": kk, "launches": plan["launches"], "algo": plan["algo"],
-         "roofline": _roofline(bound, nb, fl, us, peaks),
+         "roofline": _roofline(bound, nb, fl, us, peaks, None, plan["launches"], name),
          "dense_cublas_us": time_dense(lay, torch, dev, kk, W)}
     if clocks is not None:
         e["clocks"] = clocks
