@@ -122,6 +122,17 @@ struct WsLayout {
 // reduction kernel spreads that work over the device.
 constexpr int64_t kFusedReduceMaxTokens = 4;
 
+// K split of the fp32 CUDA-core kernel (qlin_simt_splitk_kernel): enough CTAs
+// of 64 tokens x 32 output quaternions to cover the SMs, each split keeping at
+// least one 8-quaternion step, at most 8; none when the tiles alone cover
+// half the SMs.
+int f32_split_for(int64_t M, int64_t K_g, int64_t N_g, int64_t sms) {
+  const int64_t tiles = ((M + kSkBM - 1) / kSkBM) * ((N_g + kSkBO - 1) / kSkBO);
+  const int64_t steps = (K_g + kSkBK - 1) / kSkBK;
+  if (tiles == 0 || tiles * 2 > sms) return 1;
+  return (int)std::max<int64_t>(1, std::min<int64_t>({8, steps, sms / tiles}));
+}
+
 WsLayout ws_layout(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
   WsLayout w;
   // The first QLIN_WORKSPACE_COUNTER_BYTES of every non-empty workspace are
@@ -153,6 +164,15 @@ WsLayout ws_layout(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
     w.tf_off = off;
     w.tf_bytes = (size_t)(M * rank * 4);
     off = (size_t)round_up((int64_t)(off + w.tf_bytes), 256);
+  }
+  if (dtype == QLIN_F32) {
+    // fp32 partials of the K split [split][M][4 N_g]
+    const int split = f32_split_for(M, K_g, N_g, kMaxSms);
+    if (split > 1) {
+      w.part_off = off;
+      w.part_bytes = (size_t)(split * M * 4 * N_g * 4);
+      off = (size_t)round_up((int64_t)(off + w.part_bytes), 256);
+    }
   }
   // A problem that needs no scratch needs no counters either.
   w.total = (M == 0 || off == w.cnt_bytes) ? 0 : off;
@@ -705,6 +725,28 @@ int run_simt(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], 
   const T* wi = static_cast<const T*>(w[1]);
   const T* wj = static_cast<const T*>(w[2]);
   const T* wk = static_cast<const T*>(w[3]);
+  if constexpr (std::is_same<T, float>::value) {
+    // fp32 with 16-byte aligned rows: the K-split kernel (float4 loads)
+    bool vec = aligned(x, 16) && aligned(y, 16) && ld_x % 4 == 0 && ld_w % 4 == 0 && ld_y % 4 == 0;
+    for (int p = 0; p < 4; ++p) vec = vec && aligned(w[p], 16);
+    if (vec) {
+      // (never above the split the workspace was sized for)
+      const int split = std::min(f32_split_for(M, K_g, N_g, dev->num_sms), f32_split_for(M, K_g, N_g, kMaxSms));
+      float* part = split > 1 ? reinterpret_cast<float*>(ws + L.part_off) : nullptr;
+      if (split > 1 && (!ws || L.part_bytes == 0)) return QLIN_ERR_WORKSPACE;
+      dim3 grid((unsigned)((N_g + kSkBO - 1) / kSkBO), (unsigned)((M + kSkBM - 1) / kSkBM), (unsigned)split);
+      if (grid.y > 65535) return QLIN_ERR_SHAPE;
+      qlin_simt_splitk_kernel<<<grid, 256, 0, stream>>>(x, ld_x, wr, wi, wj, wk, ld_w, bias, tf, lora_b, rank,
+                                                        lora_scale, y, ld_y, part, (int)M, (int)K_g, (int)N_g,
+                                                        split);
+      if (split > 1) {
+        const int64_t n = M * N_g;
+        qlin_splitk_f32_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+            part, split, bias, tf, lora_b, rank, lora_scale, y, ld_y, (int)M, (int)N_g);
+      }
+      return QLIN_OK;
+    }
+  }
   const int64_t big_tiles = ((M + 31) / 32) * ((N_g + 31) / 32);
   if (big_tiles >= dev->num_sms) {
     dim3 grid((unsigned)((N_g + 31) / 32), (unsigned)((M + 31) / 32));
@@ -1018,7 +1060,13 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flag
     const bool prologue = M > kStackMaxTokens || (rank > 0 && lora_mode(M, rank, K_g, sp) == kLoraPrologue);
     nl = 1 + (prologue ? 1 : 0) + ((sp > 1 && !fused) ? 1 : 0);
   } else {
+    // CUDA-core kernel (+ the LoRA down projection; fp32: + the K-split reduction)
     nl = rank > 0 ? 2 : 1;
+    if (dtype == QLIN_F32) {
+      sp = std::min(f32_split_for(M, K_g, N_g, dev->num_sms), f32_split_for(M, K_g, N_g, kMaxSms));
+      nt = kSkBM;
+      if (sp > 1) nl += 1;
+    }
   }
   if (algo) *algo = a;
   if (tile_tokens) *tile_tokens = nt;

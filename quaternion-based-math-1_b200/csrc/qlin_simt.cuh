@@ -308,6 +308,174 @@ qlin_prologue_kernel(const T* __restrict__ x, int64_t ld_x, T* __restrict__ xp, 
   }
 }
 
+// fp32 Hamilton-product GEMM on CUDA cores with a K split (fp32 layers: the
+// 1e-5 relative error bound of an fp32 layer needs FFMA, not TF32).
+//
+// CTA tile: 64 tokens x 32 output quaternions; thread (tx, ty) of 16 x 16
+// owns tokens ty + 16 t (t < 4) and output quaternions tx + 16 j (j < 2): 128
+// FMAs per input quaternion from 6 shared-memory float4 reads.  Input
+// quaternions [k0, k1) of this split are walked 8 at a time through two
+// shared-memory buffers: the next step's x quaternions (one float4 each) and
+// W pieces (4 consecutive inputs of one component row, one float4) are loaded
+// into registers while the current step computes.  The fp32 partial of the
+// split goes to part[split][M][4 N_g] (or, with one split, straight to y with
+// bias and the LoRA up projection); qlin_splitk_f32_reduce_kernel sums the
+// splits in order.  Requires 16-byte aligned x and weights, ld_x and ld_w
+// multiples of 4 (float4 loads).
+constexpr int kSkBM = 64, kSkBO = 32, kSkBK = 8, kSkTM = 4, kSkTO = 2;
+
+__device__ __forceinline__ void hamilton_acc(float (&acc)[4], const float4 w, const float4 q) {
+  // w (x) q (reference quaternion/reference.py:41-44)
+  acc[0] = fmaf(w.x, q.x, acc[0]); acc[0] = fmaf(-w.y, q.y, acc[0]); acc[0] = fmaf(-w.z, q.z, acc[0]); acc[0] = fmaf(-w.w, q.w, acc[0]);
+  acc[1] = fmaf(w.x, q.y, acc[1]); acc[1] = fmaf(w.y, q.x, acc[1]); acc[1] = fmaf(w.z, q.w, acc[1]); acc[1] = fmaf(-w.w, q.z, acc[1]);
+  acc[2] = fmaf(w.x, q.z, acc[2]); acc[2] = fmaf(-w.y, q.w, acc[2]); acc[2] = fmaf(w.z, q.x, acc[2]); acc[2] = fmaf(w.w, q.y, acc[2]);
+  acc[3] = fmaf(w.x, q.w, acc[3]); acc[3] = fmaf(w.y, q.z, acc[3]); acc[3] = fmaf(-w.z, q.y, acc[3]); acc[3] = fmaf(w.w, q.x, acc[3]);
+}
+
+__global__ void __launch_bounds__(256)
+qlin_simt_splitk_kernel(const float* __restrict__ x, int64_t ld_x, const float* __restrict__ wr,
+                        const float* __restrict__ wi, const float* __restrict__ wj, const float* __restrict__ wk,
+                        int64_t ld_w, const float* __restrict__ bias, const float* __restrict__ lora_t,
+                        const float* __restrict__ lora_b, int rank, float lora_scale, float* __restrict__ y,
+                        int64_t ld_y, float* __restrict__ part, int M, int K_g, int N_g, int split) {
+  __shared__ float4 xs[2][kSkBK][kSkBM];
+  __shared__ float4 ws[2][kSkBK][kSkBO];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4, tid = threadIdx.x;
+  const int m0 = blockIdx.y * kSkBM, o0 = blockIdx.x * kSkBO, sp = blockIdx.z;
+  // whole 8-quaternion steps per split, so every float4 load is 16-byte aligned
+  const int nst = (K_g + kSkBK - 1) / kSkBK;
+  const int k0 = kSkBK * (int)((int64_t)sp * nst / split);
+  const int k1 = min(K_g, kSkBK * (int)((int64_t)(sp + 1) * nst / split));
+  // this thread's loads of one step: x quaternions (m = tid/8 + 32 h, k = tid%8)
+  // and one W piece (component p, row o, inputs kg*4 .. kg*4+3)
+  const int xm = tid >> 3, xk = tid & 7;
+  const int wpc = tid >> 6, wo = (tid >> 1) & 31, wkg = tid & 1;
+  const float* wsrc_row = wpc == 0 ? wr : (wpc == 1 ? wi : (wpc == 2 ? wj : wk));
+  float4 rx[2], rw;
+  auto load_step = [&](int kb) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int m = m0 + xm + 32 * h, k = kb + xk;
+      rx[h] = (m < M && k < k1) ? ld_cg_f4(x + (int64_t)m * ld_x + 4 * (int64_t)k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const int o = o0 + wo, k = kb + 4 * wkg;
+    const float* src = wsrc_row + (int64_t)o * ld_w + k;
+    if (o < N_g && k + 3 < k1) {
+      rw = ld_cg_f4(src);
+    } else {
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = (o < N_g && k + i < k1) ? src[i] : 0.f;
+      rw = make_float4(v[0], v[1], v[2], v[3]);
+    }
+  };
+  auto store_step = [&](int buf) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) xs[buf][xk][xm + 32 * h] = rx[h];
+    float* wsf = reinterpret_cast<float*>(&ws[buf][0][0]) + (4 * wkg * kSkBO + wo) * 4 + wpc;
+    wsf[0 * kSkBO * 4] = rw.x;
+    wsf[1 * kSkBO * 4] = rw.y;
+    wsf[2 * kSkBO * 4] = rw.z;
+    wsf[3 * kSkBO * 4] = rw.w;
+  };
+
+  float acc[kSkTM][kSkTO][4];
+#pragma unroll
+  for (int t = 0; t < kSkTM; ++t)
+#pragma unroll
+    for (int j = 0; j < kSkTO; ++j)
+#pragma unroll
+      for (int a = 0; a < 4; ++a) acc[t][j][a] = 0.f;
+
+  int buf = 0;
+  if (k0 < k1) {
+    load_step(k0);
+    store_step(0);
+  }
+  __syncthreads();
+  for (int kb = k0; kb < k1; kb += kSkBK) {
+    const bool more = kb + kSkBK < k1;
+    if (more) load_step(kb + kSkBK);  // in flight during this step's math
+#pragma unroll
+    for (int k = 0; k < kSkBK; ++k) {
+      float4 xv[kSkTM], wv[kSkTO];
+#pragma unroll
+      for (int t = 0; t < kSkTM; ++t) xv[t] = xs[buf][k][ty + 16 * t];
+#pragma unroll
+      for (int j = 0; j < kSkTO; ++j) wv[j] = ws[buf][k][tx + 16 * j];
+#pragma unroll
+      for (int t = 0; t < kSkTM; ++t)
+#pragma unroll
+        for (int j = 0; j < kSkTO; ++j) hamilton_acc(acc[t][j], wv[j], xv[t]);
+    }
+    if (more) store_step(buf ^ 1);
+    __syncthreads();
+    buf ^= 1;
+  }
+
+#pragma unroll
+  for (int t = 0; t < kSkTM; ++t) {
+    const int m = m0 + ty + 16 * t;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < kSkTO; ++j) {
+      const int o = o0 + tx + 16 * j;
+      if (o >= N_g) continue;
+      float v[4] = {acc[t][j][0], acc[t][j][1], acc[t][j][2], acc[t][j][3]};
+      if (split > 1) {
+        *reinterpret_cast<float4*>(part + ((int64_t)sp * M + m) * (4 * (int64_t)N_g) + 4 * o) =
+            make_float4(v[0], v[1], v[2], v[3]);
+        continue;
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const int64_t n = 4 * (int64_t)o + a;
+        if (bias) v[a] += bias[n];
+        if (rank > 0) {
+          float l = 0.f;
+          for (int r = 0; r < rank; ++r) l += lora_t[(int64_t)m * rank + r] * lora_b[n * rank + r];
+          v[a] += lora_scale * l;
+        }
+      }
+      *reinterpret_cast<float4*>(y + (int64_t)m * ld_y + 4 * o) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+  }
+}
+
+// y[m, 4o .. 4o+3] = sum over the splits, in order, of the fp32 partials
+// + bias + lora_scale * t[m,:] . B[4o+a,:].  One thread per output quaternion.
+__global__ void __launch_bounds__(256)
+qlin_splitk_f32_reduce_kernel(const float* __restrict__ part, int split, const float* __restrict__ bias,
+                              const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank,
+                              float lora_scale, float* __restrict__ y, int64_t ld_y, int M, int N_g) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)M * N_g) return;
+  const int m = (int)(idx / N_g), o = (int)(idx % N_g);
+  const int64_t row = 4 * (int64_t)N_g;
+  float4 acc = ld_cg_f4(part + (int64_t)m * row + 4 * o);
+  for (int s = 1; s < split; ++s) {
+    const float4 v = ld_cg_f4(part + ((int64_t)s * M + m) * row + 4 * o);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  const int64_t n0 = 4 * (int64_t)o;
+  if (bias) {
+    acc.x += bias[n0]; acc.y += bias[n0 + 1]; acc.z += bias[n0 + 2]; acc.w += bias[n0 + 3];
+  }
+  if (rank > 0) {
+    float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+    const float* tr = lora_t + (int64_t)m * rank;
+    for (int r = 0; r < rank; ++r) {
+      const float t = tr[r];
+      l0 = fmaf(t, lora_b[n0 * rank + r], l0);
+      l1 = fmaf(t, lora_b[(n0 + 1) * rank + r], l1);
+      l2 = fmaf(t, lora_b[(n0 + 2) * rank + r], l2);
+      l3 = fmaf(t, lora_b[(n0 + 3) * rank + r], l3);
+    }
+    acc.x += lora_scale * l0; acc.y += lora_scale * l1; acc.z += lora_scale * l2; acc.w += lora_scale * l3;
+  }
+  *reinterpret_cast<float4*>(y + (int64_t)m * ld_y + n0) = acc;
+}
+
 // dst[m * ld_dst + g * n + j] = src[(g * M + m) * n + j]
 template <typename E>
 __global__ void __launch_bounds__(256)

@@ -41,7 +41,9 @@ def test_status_strings(qb):
 
 def test_workspace_size(qb):
     import torch
-    assert qb._lib.workspace_size(torch.float32, 128, 256, 256, 0) == 0
+    # fp32, the 1024 layer at 128 tokens: counters + the fp32 partials of an
+    # 8-way K split (16 tiles of 64 tokens x 32 output quaternions)
+    assert qb._lib.workspace_size(torch.float32, 128, 256, 256, 0) == 4096 + 8 * 128 * 1024 * 4
     # decode-sized: LoRA t (bf16 and fp32 copies) + split-K partials, no planar x
     ws = qb._lib.workspace_size(torch.bfloat16, 16, 1024, 1024, 32)
     assert ws >= 16 * 32 * 2 + 16 * 32 * 4 + 2 * 8 * 16 * 128 * 16
@@ -54,7 +56,8 @@ def test_workspace_size(qb):
     # every non-empty workspace starts with the 4096 counter bytes of the
     # fused split-K reduction, which nothing else uses
     assert qb._lib.workspace_size(torch.bfloat16, 1, 1024, 1024, 0) >= 4096 + 16 * 16 * 8 * 128 * 16
-    assert qb._lib.workspace_size(torch.float32, 1, 1024, 1024, 8) == 4096 + 256
+    # fp32, one token: counters + LoRA t (fp32, 256-byte rounded) + a 5-way K split's partials
+    assert qb._lib.workspace_size(torch.float32, 1, 1024, 1024, 8) == 4096 + 256 + 5 * 4096 * 4
 
 
 def test_shape_errors_are_reported_before_device_use(qb):
@@ -99,7 +102,7 @@ def test_cpython_binding_matches_ctypes_on_refusals(qb):
     P = None
     cases = [
         (1, 1, 10, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 0, P),  # ld_x < 4*K_g
-        (1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 4, P),  # unknown flag
+        (1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 8, P),  # unknown flag
         (7, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 0, P),  # dtype
         (1, P, 16, P, P, P, P, 4, P, P, P, 0, 0.0, P, 16, 0, 4, 4, P, 0, 0, 0, P),  # M == 0
     ]
