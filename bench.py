@@ -370,6 +370,59 @@ def time_stack(qb, wl, torch, dev, R, W):
     return us, flops, len(calls), plans
 
 
+def time_converted_gpt2(qb, torch, dev, R, W, M=8 * 1024):
+    """The 48 quaternion linears of a converted GPT-2-small: a transformers
+    GPT2LMHeadModel built from its config (12 blocks, d=768, 12 heads, MLP
+    3072; random init, seed 0 -- no checkpoints offline) in bf16, whose
+    c_attn / c_proj / c_fc / c_proj projections convert_model (the
+    reference's matrix method) replaced with QuaternionLinear layers (the
+    least-squares quaternion components of each dense weight, biases kept).
+    One forward of every converted layer through the module API (fused
+    bias) on N(0,1) activations of M = 8 x 1024 tokens, captured as one CUDA
+    graph and replayed R times.  Returns (us per forward, FLOP, layers)."""
+    import transformers
+
+    torch.manual_seed(0)
+    cfg = transformers.GPT2Config(n_layer=12, n_embd=768, n_head=12, n_positions=1024, n_inner=3072)
+    model = transformers.GPT2LMHeadModel(cfg).to(dev, torch.bfloat16).eval()
+    _, records = qb.convert_model(model)
+    layers = [model.get_submodule(r.name) for r in records]
+    g = torch.Generator(device="cpu").manual_seed(1)
+    xs = {}
+    flops = 0.0
+    for layer in layers:
+        if layer.in_features not in xs:
+            xs[layer.in_features] = torch.randn(M, layer.in_features, generator=g).to(dev, torch.bfloat16)
+        flops += 2.0 * M * layer.in_features * layer.out_features
+
+    def forward():
+        for layer in layers:
+            layer(xs[layer.in_features])
+
+    with torch.inference_mode():
+        for _ in range(W):
+            forward()
+        torch.cuda.synchronize(dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            forward()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            forward()
+        _settle(torch, dev, graph.replay, 0.3)
+        torch.cuda.synchronize(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(R):
+            graph.replay()
+        e.record()
+        torch.cuda.synchronize(dev)
+    del graph, model
+    return s.elapsed_time(e) * 1e3 / R, flops, len(layers)
+
+
 def _time_ranks(torch, dev, dist, call, steps, W):
     """Device time per call of call(i) on every rank, max over ranks: steps
     calls captured in one CUDA graph (eager launches if capture is refused)."""
@@ -909,6 +962,16 @@ def main():
         also["gpt2_stack"] = {"us_per_forward": sus, "linears": ncalls, "M": 8192,
                               "roofline": {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"],
                                            "unit": "TFLOP/s", "frac": a / peaks["bf16_tflops"]}}
+        try:
+            cus, cflops, cn = time_converted_gpt2(qb, torch, dev, 20, W)
+            a = cflops / (cus * 1e-6) / 1e12
+            also["gpt2_converted"] = {
+                "us_per_forward": cus, "linears": cn, "M": 8192, "bias": True,
+                "weights": "transformers GPT-2-small (random init, seed 0) converted by convert_model (matrix)",
+                "roofline": {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": a / peaks["bf16_tflops"]}}
+        except ImportError:  # transformers absent
+            pass
         result["also"] = also
         # the metric's other halves, last so that they end the line
         for name in ("decode_m16", "prefill_m2048"):
