@@ -84,8 +84,20 @@ enum {
  * prologue kernel) instead of the CTA-pair kernel that QLIN_ALGO_AUTO and
  * QLIN_ALGO_TC otherwise use for them (more than 64 tokens, no LoRA, an even
  * number of output quaternions, ld_y a multiple of 8 and a 16-byte aligned y).
+ *
+ * QLIN_FLAG_NO_CLUSTER (comparisons and diagnostics): decode-sized
+ * tensor-core problems (at most 16 tokens) sum their K split through the
+ * workspace (the reduction kernel, or the last CTA of each tile on a zeroed
+ * workspace) instead of the cluster reduce-scatter through distributed shared
+ * memory that QLIN_ALGO_TC and QLIN_ALGO_AUTO otherwise use when the clusters
+ * fit.
  */
-enum { QLIN_FLAG_STATIC_WEIGHTS = 1, QLIN_FLAG_ZEROED_WORKSPACE = 2, QLIN_FLAG_NO_PAIR = 4 };
+enum {
+  QLIN_FLAG_STATIC_WEIGHTS = 1,
+  QLIN_FLAG_ZEROED_WORKSPACE = 2,
+  QLIN_FLAG_NO_PAIR = 4,
+  QLIN_FLAG_NO_CLUSTER = 8
+};
 #define QLIN_WORKSPACE_COUNTER_BYTES 4096u
 
 /* Human-readable name of a status code (static storage). */

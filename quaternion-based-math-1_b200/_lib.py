@@ -24,6 +24,7 @@ ALGO_AUTO, ALGO_SIMT, ALGO_TC, ALGO_GEMV = 0, 1, 2, 3
 FLAG_STATIC_WEIGHTS = 1
 FLAG_ZEROED_WORKSPACE = 2
 FLAG_NO_PAIR = 4
+FLAG_NO_CLUSTER = 8
 PLAN_TC_PAIR = 4
 
 OK = 0

@@ -285,7 +285,7 @@ constexpr int tc_block_threads(int lora) { return lora == kLoraSimt ? kTcMaxThre
 int split_for(int64_t M, int64_t K_g, int64_t N_g, int rank, int64_t sms, bool static_weights = false) {
   const int s = max_split_for(M, K_g, N_g, sms);
   const int64_t chunks = (K_g + kTcChunk - 1) / kTcChunk;
-  if (M <= kTcClusterTokens && s > kTcClusterMax && !(static_weights && rank == 0)) return kTcClusterMax;
+  if (M <= 2 && s > 8 && !(static_weights && rank == 0)) return 8;
   if (rank > 0 && rank <= kTcLoraInRank && M <= kTcLoraSimtTokens && s > 8 && (chunks + 7) / 8 <= 4) return 8;
   return s;
 }
@@ -301,6 +301,9 @@ int ensure_tc_attrs(DeviceInfo* dev) {
   if (dev->tc_attr_set[di][ti][li][pi][ci]) return QLIN_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
       cudaSuccess)
+    return QLIN_ERR_LAUNCH;
+  // clusters of up to 16 CTAs (the cluster K split of decode tiles)
+  if (CLUSTER && cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
     return QLIN_ERR_LAUNCH;
   // Every kernel of the call prefers the full shared-memory carveout, so the
   // SMs need no L1/shared reconfiguration between the prologue, the main
@@ -323,15 +326,12 @@ int ensure_tc_attrs(DeviceInfo* dev) {
   return QLIN_OK;
 }
 
-// Cluster K split for decode tiles: every split of a tile in one cluster
-// (at most kTcClusterMax CTAs), the partials summed through distributed
-// shared memory.  Used when at most kTcClusterTokens tokens, 2..8 splits and
-// all clusters of the grid fit on the device at once.
+// Whether every cluster of a decode grid (tiles clusters of `split` CTAs, the
+// cluster K split) fits on the device at once.
 template <typename T, int LORA>
 bool cluster_fits(DeviceInfo* dev, int split, int64_t tiles) {
-  if constexpr (LORA == kLoraTc) {
-    return false;
-  } else {
+  if (split < 2 || split > kTcClusterMax) return false;
+  {
     const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
     int cap;
     {
@@ -363,6 +363,29 @@ bool cluster_fits(DeviceInfo* dev, int split, int64_t tiles) {
   }
 }
 
+// The cluster K split a decode-sized problem uses (0: none): at most
+// kTcClusterTokens tokens (tiles of 16), the K split split_for chose (at most
+// 8 for one or two tokens: with static weights and no LoRA the 16 plain
+// splits, prefetching their weights, measured faster), when all clusters of
+// the grid fit at once; else, for at most 8 tokens, 8 CTAs per cluster when
+// that fits (and keeps the CUDA-core LoRA mode's slice of at most 4 chunks per
+// split).  Same-box measurements, 4096 layer with bias and LoRA r=32: 3, 4, 8
+// tokens 8.7, 9.8, 9.3 us/call in 8-CTA clusters against 10.3, 11.7, 10.0
+// through the workspace; at 16 tokens (16-CTA clusters did not fit) 10.6 in
+// 8-CTA clusters, whose 64 CTAs stream the weights slower, against 10.2.
+template <typename T, int LORA>
+int cluster_split(DeviceInfo* dev, int64_t M, int64_t K_g, int split, int64_t tiles) {
+  if (M > kTcClusterTokens || split < 2 || (M <= 2 && split > 8)) return 0;
+  // every owner's receive slots, (C - 1) * ceil(M / C), fit the buffer
+  auto slots_ok = [&](int c) { return (c - 1) * ((M + c - 1) / c) <= kTcClusterSlots; };
+  if (slots_ok(split) && cluster_fits<T, LORA>(dev, split, tiles)) return split;
+  const int64_t chunks = (K_g + kTcChunk - 1) / kTcChunk;
+  if (split > 8 && M <= 8 && slots_ok(8) && (LORA != kLoraSimt || (chunks + 7) / 8 <= 4) &&
+      cluster_fits<T, LORA>(dev, 8, tiles))
+    return 8;
+  return 0;
+}
+
 template <typename T, int N_TOK, int LORA>
 int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& base_prm, int64_t M,
                    int64_t K_g, int64_t N_g, float4* partials, cudaStream_t stream) {
@@ -372,22 +395,22 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
   {
     const int64_t o_blocks = (N_g + kTcBlockO - 1) / kTcBlockO, t_blocks = (M + N_TOK - 1) / N_TOK;
     const int split = split_for(M, K_g, N_g, base_prm.rank, dev->num_sms, base_prm.static_weights != 0);
-    if constexpr (N_TOK == 16 && LORA != kLoraTc) {
-      if (M <= kTcClusterTokens && split > 1 && split <= kTcClusterMax && !peers &&
-          cluster_fits<T, LORA>(dev, split, o_blocks * t_blocks)) {
+    if constexpr (N_TOK == 16) {
+      const int cs = (peers || base_prm.no_cluster) ? 0 : cluster_split<T, LORA>(dev, M, K_g, split, o_blocks * t_blocks);
+      if (cs > 0) {
         TcParams prm = base_prm;
-        prm.split_k = split;
+        prm.split_k = cs;
         prm.partials = nullptr;
         prm.fuse_reduce = 0;
         cudaLaunchAttribute attrs[2];
         attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attrs[0].val.programmaticStreamSerializationAllowed = 1;
         attrs[1].id = cudaLaunchAttributeClusterDimension;
-        attrs[1].val.clusterDim.x = (unsigned)split;
+        attrs[1].val.clusterDim.x = (unsigned)cs;
         attrs[1].val.clusterDim.y = 1;
         attrs[1].val.clusterDim.z = 1;
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)split, (unsigned)o_blocks, (unsigned)t_blocks);
+        cfg.gridDim = dim3((unsigned)cs, (unsigned)o_blocks, (unsigned)t_blocks);
         cfg.blockDim = dim3(tc_block_threads(LORA), 1, 1);
         cfg.dynamicSmemBytes = TcCfg<16, true, LORA, true>::kSmemBytes;
         cfg.stream = stream;
@@ -686,6 +709,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
   prm.split_k = 1;
   prm.partials = nullptr;
   prm.static_weights = (flags & QLIN_FLAG_STATIC_WEIGHTS) ? 1 : 0;
+  prm.no_cluster = (flags & QLIN_FLAG_NO_CLUSTER) ? 1 : 0;
   prm.counters = (flags & QLIN_FLAG_ZEROED_WORKSPACE) ? reinterpret_cast<unsigned*>(ws + L.cnt_off)
                                                        : nullptr;
   prm.fuse_reduce = 0;
@@ -916,7 +940,8 @@ static int forward_common(int dtype, const void* x, int64_t ld_x, const void* wr
   if (st != QLIN_OK) return st;
   if (M == 0) return QLIN_OK;
   if (algo < QLIN_ALGO_AUTO || algo > QLIN_ALGO_GEMV) return QLIN_ERR_ARG;
-  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE | QLIN_FLAG_NO_PAIR)) return QLIN_ERR_ARG;
+  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE | QLIN_FLAG_NO_PAIR |
+                QLIN_FLAG_NO_CLUSTER)) return QLIN_ERR_ARG;
   if (rank == 0) lora_a = lora_b = nullptr;
   DeviceInfo* dev = nullptr;
   st = device_info(&dev);
@@ -998,7 +1023,8 @@ int qlin_select_algo(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
 int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flags, int* algo,
               int* tile_tokens, int* split_k, int* launches, int* resident_ctas) {
   if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
-  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE | QLIN_FLAG_NO_PAIR)) return QLIN_ERR_ARG;
+  if (flags & ~(QLIN_FLAG_STATIC_WEIGHTS | QLIN_FLAG_ZEROED_WORKSPACE | QLIN_FLAG_NO_PAIR |
+                QLIN_FLAG_NO_CLUSTER)) return QLIN_ERR_ARG;
   if (M <= 0 || K_g <= 0 || N_g <= 0 || rank < 0) return QLIN_ERR_SHAPE;
   DeviceInfo* dev = nullptr;
   int st = device_info(&dev);
@@ -1047,14 +1073,23 @@ int qlin_plan(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int flag
     }
     if (st != QLIN_OK) return st;
     bool clustered = false;
-    if (nt == 16 && M <= kTcClusterTokens && sp > 1 && sp <= kTcClusterMax) {
+    if (nt == 16 && !(flags & QLIN_FLAG_NO_CLUSTER)) {
       const int lm = lora_mode(M, rank, K_g, sp);
       const int64_t tiles = (N_g + kTcBlockO - 1) / kTcBlockO;
+      int cs = 0;
       if (lm == kLoraSimt)
-        clustered = bf ? cluster_fits<__nv_bfloat16, kLoraSimt>(dev, sp, tiles) : cluster_fits<__half, kLoraSimt>(dev, sp, tiles);
-      else if (lm == kLoraPrologue)
-        clustered = bf ? cluster_fits<__nv_bfloat16, kLoraPrologue>(dev, sp, tiles)
-                       : cluster_fits<__half, kLoraPrologue>(dev, sp, tiles);
+        cs = bf ? cluster_split<__nv_bfloat16, kLoraSimt>(dev, M, K_g, sp, tiles)
+                : cluster_split<__half, kLoraSimt>(dev, M, K_g, sp, tiles);
+      else if (lm == kLoraTc)
+        cs = bf ? cluster_split<__nv_bfloat16, kLoraTc>(dev, M, K_g, sp, tiles)
+                : cluster_split<__half, kLoraTc>(dev, M, K_g, sp, tiles);
+      else
+        cs = bf ? cluster_split<__nv_bfloat16, kLoraPrologue>(dev, M, K_g, sp, tiles)
+                : cluster_split<__half, kLoraPrologue>(dev, M, K_g, sp, tiles);
+      if (cs > 0) {
+        clustered = true;
+        sp = cs;
+      }
     }
     const bool fused = clustered || ((flags & QLIN_FLAG_ZEROED_WORKSPACE) && M <= kFusedReduceMaxTokens);
     const bool prologue = M > kStackMaxTokens || (rank > 0 && lora_mode(M, rank, K_g, sp) == kLoraPrologue);

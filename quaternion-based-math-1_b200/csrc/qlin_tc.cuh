@@ -85,10 +85,17 @@ __host__ __device__ constexpr int tmem_cols_for(int n) {
 }
 
 // Cluster K split (decode, at most kTcClusterTokens tokens): every split of
-// a tile is one CTA of an 8-at-most CTA cluster and pushes its fp32 partial
-// into the leader CTA's receive buffer [split-1][token][128] x float4.
-constexpr int kTcClusterTokens = 2;
-constexpr int kTcClusterMax = 8;
+// a tile is one CTA of a cluster of C CTAs (C = the split, at most
+// kTcClusterMax; above 8 the non-portable cluster size).  A reduce-scatter
+// through distributed shared memory: CTA r owns the tile's tokens
+// [r * per, (r + 1) * per), per = ceil(tokens / C), receives every other
+// split's fp32 partial of those tokens into its receive buffer
+// [slot = sender (skipping itself) * per + owned token][128 rows] x float4
+// (st.async, counted on its own mbarrier) and sums them in split order.
+// (C - 1) * per stays within kTcClusterSlots for every C at up to 16 tokens.
+constexpr int kTcClusterTokens = 16;
+constexpr int kTcClusterMax = 16;
+constexpr int kTcClusterSlots = 15;
 
 template <int N_TOK, bool STACK, int LORA = kLoraPrologue, bool CLUSTER = false>
 struct TcCfg {
@@ -104,7 +111,7 @@ struct TcCfg {
   // CUDA-core LoRA: the split's lora_a slice [32 rows][<= 512 elements],
   // loaded once, ahead of the weights, as row pieces of kTcLoraSliceBox
   static constexpr int kSliceBytes = LORA == kLoraSimt ? kTcLoraInRank * kTcLoraSliceMax * 2 : 0;
-  static constexpr int kRecvBytes = CLUSTER ? (kTcClusterMax - 1) * kTcClusterTokens * kTcBlockO * 16 : 0;
+  static constexpr int kRecvBytes = CLUSTER ? kTcClusterSlots * kTcBlockO * 16 : 0;
   static constexpr int kFit = ((CLUSTER ? 212 : 200) * 1024 - kSliceBytes - kRecvBytes) / kStageBytes;
   static constexpr int kStages = kFit > 6 ? 6 : (kFit < 2 ? 2 : kFit);
   static constexpr int kSliceOffset = kStages * kStageBytes;
@@ -148,6 +155,7 @@ struct TcParams {
   int fuse_reduce;     // split_k > 1: the last CTA of a tile to arrive sums the partials
   int static_weights;  // weights/bias/LoRA B are not written by earlier work on the stream
   int after_prologue;  // launched right after this call's prologue kernel (see below)
+  int no_cluster;      // host-side choice only: QLIN_FLAG_NO_CLUSTER
   int rank;            // LoRA rank (in-kernel LoRA: ranks >= rank are zero)
   float lora_scale;    // in-kernel LoRA: t = lora_scale * x A^T
   const void* lora_a;  // CUDA-core in-kernel LoRA: A [rank, ld_a]
@@ -290,7 +298,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   auto load_bias = [&](T (&raw)[4]) {
     const int ob = o0 + (int)threadIdx.x;
     const T* __restrict__ bp = reinterpret_cast<const T*>(prm.bias);
-    const bool has = bp && (prm.split_k == 1 || prm.fuse_reduce || (CLUSTER && ks == 0)) && ob < prm.N_g &&
+    const bool has = bp && (prm.split_k == 1 || prm.fuse_reduce || CLUSTER) && ob < prm.N_g &&
                      threadIdx.x < kTcBlockO;
 #pragma unroll
     for (int a = 0; a < 4; ++a) raw[a] = has ? bp[4 * ob + a] : from_f32<T>(0.f);
@@ -307,10 +315,13 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     mbar_init(t_full, 1);
     mbar_init(red_full, 1);
     mbar_init(gather, 1);
-    // the leader arms its receive barrier before any peer can send (the
+    // every owner arms its receive barrier before any peer can send (the
     // cluster barrier below orders this before every peer's epilogue)
-    if (CLUSTER && ks == 0)
-      mbar_arrive_expect_tx(gather, (uint32_t)((prm.split_k - 1) * m_tile * kTcBlockO * 16));
+    if (CLUSTER) {
+      const int per = (m_tile + prm.split_k - 1) / prm.split_k;
+      const int n_own = min(m_tile, (ks + 1) * per) - ks * per;
+      if (n_own > 0) mbar_arrive_expect_tx(gather, (uint32_t)((prm.split_k - 1) * n_own * kTcBlockO * 16));
+    }
     *abort_flag = 0;
     *issued_count = 0;
     *consumed_count = 0;
@@ -674,43 +685,55 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
         }
       }
     } else if (CLUSTER) {
-      // Cluster K split (at most kTcClusterTokens tokens): the peers push
-      // their fp32 partial of the real tokens into the leader's receive
-      // buffer (st.async, counted on the leader's gather barrier) -- sent even
-      // after an abort so the leader's count completes -- and the leader adds
-      // them, in split order after its own, to the bias.
+      // Cluster K split (reduce-scatter, see kTcClusterTokens): this CTA's
+      // fp32 partials of the tokens other CTAs own go to their receive
+      // buffers (st.async, counted on the owner's gather barrier) -- sent even
+      // after an abort so every owner's count completes -- and the owned
+      // tokens are summed over all splits in split order, plus the bias.
+      const int C = prm.split_k;
+      const int per = (m_tile + C - 1) / C;
+      const int own0 = ks * per;
+      const int n_own = min(m_tile, own0 + per) - own0;
       float v[4][16];
 #pragma unroll
       for (int a = 0; a < 4; ++a) tmem_ld16(lane_addr + a * N_TOK, v[a]);
       tmem_ld_wait();
-      if (ks > 0) {
-        const uint32_t rbase = map_peer_smem(smem_u32(smem + Cfg::kRecvOffset), 0);
-        const uint32_t rbar = map_peer_smem(smem_u32(gather), 0);
+      const uint32_t recv_local = smem_u32(smem + Cfg::kRecvOffset);
+      const uint32_t gather_local = smem_u32(gather);
 #pragma unroll
-        for (int t = 0; t < kTcClusterTokens; ++t)
-          if (t < m_tile)
-            st_async_v4(rbase + (uint32_t)((((ks - 1) * kTcClusterTokens + t) * kTcBlockO + o_local) * 16),
-                        make_float4(v[0][t], v[1][t], v[2][t], v[3][t]), rbar);
-      } else {
+      for (int t = 0; t < kTcClusterTokens; ++t) {
+        if (t < m_tile) {
+          const int owner = t / per;
+          if (owner != ks) {
+            const int slot = (ks < owner ? ks : ks - 1) * per + (t - owner * per);
+            st_async_v4(map_peer_smem(recv_local, (uint32_t)owner) + (uint32_t)((slot * kTcBlockO + o_local) * 16),
+                        make_float4(v[0][t], v[1][t], v[2][t], v[3][t]),
+                        map_peer_smem(gather_local, (uint32_t)owner));
+          }
+        }
+      }
+      if (n_own > 0) {
         const bool got = mbar_wait(gather, 0);
         const float4* recv = reinterpret_cast<const float4*>(smem + Cfg::kRecvOffset);
         const int o = o0 + o_local;
         float b[4];
 #pragma unroll
         for (int a = 0; a < 4; ++a) b[a] = to_f32(bias_raw[a]);
+        for (int tl = 0; tl < n_own; ++tl) {
+          const int t = own0 + tl;
+          // this split's own partial of token t (registers, selected without a runtime index)
+          float4 mine = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int t = 0; t < kTcClusterTokens; ++t) {
-          if (t < m_tile) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            acc.x += v[0][t]; acc.y += v[1][t]; acc.z += v[2][t]; acc.w += v[3][t];
-            for (int sp = 1; sp < prm.split_k; ++sp) {
-              const float4 r = recv[((sp - 1) * kTcClusterTokens + t) * kTcBlockO + o_local];
-              acc.x += r.x; acc.y += r.y; acc.z += r.z; acc.w += r.w;
-            }
-            if (ok && got && o < prm.N_g)
-              store_out<T, PEERS>(y, prm.peers, (int64_t)(t0 + t) * prm.ld_y + 4 * o,
-                                  pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
+          for (int tt = 0; tt < kTcClusterTokens; ++tt)
+            if (tt == t) mine = make_float4(v[0][tt], v[1][tt], v[2][tt], v[3][tt]);
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int sp = 0; sp < C; ++sp) {
+            const float4 r = sp == ks ? mine : recv[((sp < ks ? sp : sp - 1) * per + tl) * kTcBlockO + o_local];
+            acc.x += r.x; acc.y += r.y; acc.z += r.z; acc.w += r.w;
           }
+          if (ok && got && o < prm.N_g)
+            store_out<T, PEERS>(y, prm.peers, (int64_t)(t0 + t) * prm.ld_y + 4 * o,
+                                pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
         }
       }
     } else {
@@ -821,8 +844,9 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   // ---------------- teardown ----------------
   tc_fence_before();
   __syncthreads();
-  // No CTA of a cluster leaves while another may still store into it: the
-  // leader arrives once every partial has landed, the peers after sending.
+  // No CTA of a cluster leaves while another may still store into it: an
+  // owner arrives once every partial of its tokens has landed, the others
+  // after sending.
   if (CLUSTER) {
     cluster_arrive_release();
     cluster_wait_acquire();

@@ -67,7 +67,7 @@ def test_shape_errors_are_reported_before_device_use(qb):
     code = lib.qlin_forward(1, 1, 10, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, P)
     assert code == 1
     # unknown flag bits are refused (after the shape checks, before any device use)
-    code = lib.qlin_forward_ex(1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 8, P)
+    code = lib.qlin_forward_ex(1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 16, P)
     assert code == 8
     # kernel choices: AUTO, SIMT, TC, GEMV (0-3); anything else is refused before device use
     for algo in (-1, 4):
@@ -102,7 +102,7 @@ def test_cpython_binding_matches_ctypes_on_refusals(qb):
     P = None
     cases = [
         (1, 1, 10, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 0, P),  # ld_x < 4*K_g
-        (1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 8, P),  # unknown flag
+        (1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 16, P),  # unknown flag
         (7, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 0, P),  # dtype
         (1, P, 16, P, P, P, P, 4, P, P, P, 0, 0.0, P, 16, 0, 4, 4, P, 0, 0, 0, P),  # M == 0
     ]

@@ -16,6 +16,7 @@ from gpu_helpers import rel_err, to_device
 pytestmark = pytest.mark.gpu
 
 FLAG_ZEROED = 2
+FLAG_NO_CLUSTER = 8  # the workspace reductions, not the cluster reduce-scatter
 COUNTER_BYTES = 4096
 ALGO_AUTO, ALGO_TC = 0, 2  # the fused reduction is a property of the tensor-core kernel
 
@@ -39,8 +40,8 @@ def _both(qb, workloads, cuda, dtype, M, K, N, seed, rank, bias, zeroed_ws):
     y_r = torch.empty_like(y_f)
     ws_plain = torch.empty(max(qb._lib.workspace_size(d["x"].dtype, M, K_g, N_g, rank), 1),
                            dtype=torch.uint8, device=cuda)
-    assert _call(qb, d, y_f, M, K_g, N_g, rank, zeroed_ws, FLAG_ZEROED) == 0
-    assert _call(qb, d, y_r, M, K_g, N_g, rank, ws_plain, 0) == 0
+    assert _call(qb, d, y_f, M, K_g, N_g, rank, zeroed_ws, FLAG_ZEROED | FLAG_NO_CLUSTER) == 0
+    assert _call(qb, d, y_r, M, K_g, N_g, rank, ws_plain, FLAG_NO_CLUSTER) == 0
     torch.cuda.synchronize()
     return lay, y_f, y_r
 
@@ -106,13 +107,18 @@ def test_fused_reduction_in_a_graph_and_back_to_back(qb, workloads, cuda):
 def test_plan_counts_the_fused_reduction(qb, cuda):
     # three or four tokens: the K split is summed by the last CTA of each tile
     # on a zero-filled workspace, else by the reduction kernel
-    p0 = qb._lib.plan(torch.bfloat16, 3, 1024, 1024, 0, flags=0)
-    p1 = qb._lib.plan(torch.bfloat16, 3, 1024, 1024, 0, flags=FLAG_ZEROED)
+    p0 = qb._lib.plan(torch.bfloat16, 3, 1024, 1024, 0, flags=FLAG_NO_CLUSTER)
+    p1 = qb._lib.plan(torch.bfloat16, 3, 1024, 1024, 0, flags=FLAG_ZEROED | FLAG_NO_CLUSTER)
     assert p0["split_k"] > 1
     assert p1["launches"] == p0["launches"] - 1 == 1
     # above four tokens the separate reduction kernel stays
-    p5 = qb._lib.plan(torch.bfloat16, 5, 1024, 1024, 0, flags=FLAG_ZEROED)
+    p5 = qb._lib.plan(torch.bfloat16, 5, 1024, 1024, 0, flags=FLAG_ZEROED | FLAG_NO_CLUSTER)
     assert p5["launches"] == 2
+    # by default 3..8 tokens sum the split through a cluster: one launch, no workspace use
+    for M in (3, 5, 8):
+        for rank in (0, 32):
+            p = qb._lib.plan(torch.bfloat16, M, 1024, 1024, rank, flags=0)
+            assert p["launches"] == 1 and p["split_k"] in (8, 16), (M, rank, p)
     # one or two tokens: the CUDA-core decode kernel, no K split, whatever
     # the flags; one launch, two with LoRA (the down-projection prologue)
     for M in (1, 2):
@@ -138,4 +144,34 @@ def test_module_path_keeps_its_workspace_counters_zero(qb, cuda):
     assert bufs
     for buf in bufs:
         assert int(buf[:COUNTER_BYTES].count_nonzero()) == 0
+    assert qb.device_error(cuda) == 0
+
+
+@pytest.mark.parametrize("M", [3, 4, 5, 8, 13, 16])
+@pytest.mark.parametrize("rank,bias", [(0, None), (32, "normal")])
+def test_cluster_reduce_scatter_matches_reduction_kernel(qb, oracle, workloads, cuda, M, rank, bias):
+    """Decode tiles of 3..16 tokens: the K split summed through distributed
+    shared memory (each CTA of the cluster owns some tokens, receives the
+    other splits' partials of them and adds all splits in order) against the
+    reduction kernel over the workspace.  Same split count: bit-identical."""
+    K, N = 4096, 4096
+    lay = workloads.make_layer("bf16", M, K, N, 300 + M, bias=bias, lora_rank=rank, lora_std=0.02)
+    d = to_device(lay, cuda)
+    K_g, N_g = K // 4, N // 4
+    p_c = qb._lib.plan(torch.bfloat16, M, K_g, N_g, rank, flags=0)
+    p_r = qb._lib.plan(torch.bfloat16, M, K_g, N_g, rank, flags=FLAG_NO_CLUSTER)
+    assert p_c["launches"] == 1 or M > 8  # more tokens: clusters of 16 CTAs when they fit
+    y_c = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    y_r = torch.empty_like(y_c)
+    ws = torch.empty(max(qb._lib.workspace_size(torch.bfloat16, M, K_g, N_g, rank), 1), dtype=torch.uint8,
+                     device=cuda)
+    for _ in range(2):  # twice: nothing of the first call may leak into the second
+        assert _call(qb, d, y_c, M, K_g, N_g, rank, ws, 0) == 0
+        assert _call(qb, d, y_r, M, K_g, N_g, rank, ws, FLAG_NO_CLUSTER) == 0
+        torch.cuda.synchronize()
+        if p_c["split_k"] == p_r["split_k"]:
+            assert torch.equal(y_c, y_r)
+        want = oracle.forward_rows(lay.x, *lay.weights, bias=lay.bias, lora_a=lay.lora_a,
+                                   lora_b=lay.lora_b, lora_scale=lay.lora_scale)
+        assert rel_err(oracle, y_c.float().cpu().numpy(), want) <= 1e-2
     assert qb.device_error(cuda) == 0
