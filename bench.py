@@ -219,8 +219,10 @@ def _ncopy(lay, min_bytes=2 * L2_BYTES):
     return max(2, min(64, math.ceil(min_bytes / max(nbytes, 1))))
 
 
-def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES, flags=0, algo=0):
-    """Device copies rotated to exceed L2, preallocated outputs and workspace."""
+def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES, flags=0, algo=0, packed=False):
+    """Device copies rotated to exceed L2, preallocated outputs and workspace.
+    packed: the calls go through qlin_forward_packed with the packed weight
+    cache only (no planar weights)."""
     dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
     ncopy = _ncopy(lay, min_bytes)
 
@@ -246,9 +248,25 @@ def _device_case(qb, lay, torch, dev, min_bytes=2 * L2_BYTES, flags=0, algo=0):
     code = qb._lib.dtype_code(dt)
     stream_of = qb._lib.stream_handle
 
+    if packed:
+        for c in copies:
+            c["wq"] = qb.pack_quaternion_weights(*c["w"])
+            c["w"] = None
+        torch.cuda.empty_cache()
+
     def call(i):
         c = copies[i % ncopy]
         y = ys[i % ncopy]
+        if packed:
+            st = lib.qlin_forward_packed(code, c["x"].data_ptr(), 4 * K_g, c["wq"].data_ptr(), K_g, None, None,
+                                         None, None, K_g, c["b"].data_ptr() if c["b"] is not None else None,
+                                         c["la"].data_ptr() if c["la"] is not None else None,
+                                         c["lb"].data_ptr() if c["lb"] is not None else None,
+                                         rank, float(lay.lora_scale), y.data_ptr(), 4 * N_g, M, K_g, N_g,
+                                         ws.data_ptr(), ws_bytes, flags, stream_of(dev))
+            if st != 0:
+                qb._lib.check(st, "qlin_forward_packed")
+            return
         st = lib.qlin_forward_ex(code, c["x"].data_ptr(), 4 * K_g, *(w.data_ptr() for w in c["w"]), K_g,
                                  c["b"].data_ptr() if c["b"] is not None else None,
                                  c["la"].data_ptr() if c["la"] is not None else None,
@@ -275,8 +293,8 @@ def _settle(torch, dev, fn, seconds=0.5):
         torch.cuda.synchronize(dev)
 
 
-def time_device(qb, lay, torch, dev, K, W, dist=None, flags=0, algo=0):
-    call, ncopy, copies, ys, plan = _device_case(qb, lay, torch, dev, flags=flags, algo=algo)
+def time_device(qb, lay, torch, dev, K, W, dist=None, flags=0, algo=0, packed=False):
+    call, ncopy, copies, ys, plan = _device_case(qb, lay, torch, dev, flags=flags, algo=algo, packed=packed)
     for i in range(W):
         call(i)
     torch.cuda.synchronize(dev)
@@ -838,11 +856,18 @@ def _entry(qb, wl, torch, dev, name, K, W, peaks, with_clocks=False):
         clocks = None
     us = ms * 1e3 / kk
     nb, fl = algorithmic_work(lay)
+    if name == "prefill_m2048":
+        pms, _, _ = time_device(qb, lay, torch, dev, kk, W, packed=True)
+        packed_us = pms * 1e3 / kk
+    else:
+        packed_us = None
     e = {"value": us, "unit": "us/call", "steps": kk, "launches": plan["launches"], "algo": plan["algo"],
          "roofline": _roofline(bound, nb, fl, us, peaks, None, plan["launches"], name),
          "dense_cublas_us": time_dense(lay, torch, dev, kk, W)}
     if clocks is not None:
         e["clocks"] = clocks
+    if packed_us is not None:
+        e["packed_weights_us_per_call"] = packed_us
     return e
 
 
@@ -945,6 +970,9 @@ def main():
     # streams its weights while the previous call's kernels finish.
     sms, _, _ = time_device(qb, lay, torch, dev, K, W, flags=qb._lib.FLAG_STATIC_WEIGHTS)
     result["static_weights_us_per_call"] = sms * 1e3 / K
+    # the same calls on the packed weight cache only (qlin_forward_packed)
+    pms, _, _ = time_device(qb, lay, torch, dev, K, W, packed=True)
+    result["packed_weights_us_per_call"] = pms * 1e3 / K
     e2e_us, h2d, d2h = time_e2e(qb, lay, torch, dev, K, W)
     result["e2e"] = {"value": e2e_us, "unit": "us/call", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
     result["dense_cublas_us"] = time_dense(lay, torch, dev, K, W)

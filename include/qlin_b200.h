@@ -170,6 +170,34 @@ int qlin_forward_ex(int dtype,
 #define QLIN_PLAN_TC_PAIR 4
 
 /*
+ * qlin_forward with the packed weight cache (no reference counterpart: the
+ * reference keeps only the four component tensors, quaternion/linear.py:101-104).
+ *
+ *   wq     [N_g][ld_wq][4]: wq[o][i][p] = W_p[o][i], all four components of a
+ *          weight quaternion side by side (the layout of x rows); ld_wq in
+ *          quaternions, even; 16-byte aligned; bf16/f16 only
+ *   wr..wk the planar components as in qlin_forward, or all four NULL
+ * The kernels that read the packed buffer take it: the decode GEMV (at most
+ * 2 tokens) reads one address stream per output row instead of four, and the
+ * CTA-pair prefill kernel's builder warps get all four components of an input
+ * quaternion from one 8-byte piece.  Every other path reads the planar
+ * weights; without them such a problem returns QLIN_ERR_ALIGN.  Results equal
+ * qlin_forward's on the same weights (same kernels' arithmetic).
+ * Other arguments as qlin_forward_ex with QLIN_ALGO_AUTO.
+ */
+int qlin_forward_packed(int dtype,
+                        const void* x, int64_t ld_x,
+                        const void* wq, int64_t ld_wq,
+                        const void* wr, const void* wi, const void* wj, const void* wk,
+                        int64_t ld_w,
+                        const void* bias,
+                        const void* lora_a, const void* lora_b, int rank, float lora_scale,
+                        void* y, int64_t ld_y,
+                        int64_t M, int64_t K_g, int64_t N_g,
+                        void* workspace, size_t workspace_bytes,
+                        int flags, void* stream);
+
+/*
  * Launch plan qlin_forward_ex uses for this problem with these flags on the
  * current device (diagnostics; no reference counterpart; flags 0 is
  * qlin_forward's plan).  Fills every non-null output:

@@ -16,7 +16,7 @@ The directory name is not a Python identifier, so import it with
 from . import ops
 from .convert import ConversionRecord, convert_model, eligible_modules, project_onto_quaternion
 from ._lib import device_error
-from .linear import QuaternionLinear, fused_quaternion_linear, quaternion_linear
+from .linear import QuaternionLinear, fused_quaternion_linear, pack_quaternion_weights, quaternion_linear
 from .lora import (
     LoRAQuaternionLinear,
     count_trainable,
@@ -40,6 +40,7 @@ __all__ = [
     "QuaternionLinear",
     "quaternion_linear",
     "fused_quaternion_linear",
+    "pack_quaternion_weights",
     "quaternion_linear_naive",
     "quaternion_linear_planar",
     "planar_coefficient_tensor",

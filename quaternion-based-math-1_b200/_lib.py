@@ -49,6 +49,7 @@ EXPORTED = (
     "qlin_get_device_error",
     "qlin_gather_columns",
     "qlin_forward_noalloc",
+    "qlin_forward_packed",
     "qlin_forward_allgather",
     "qlin_ipc_alloc",
     "qlin_ipc_free",
@@ -89,6 +90,9 @@ def load(path: str | None = None):
         lib.qlin_plan.restype = I
         lib.qlin_get_device_error.argtypes = [P, I, ctypes.POINTER(I)]
         lib.qlin_get_device_error.restype = I
+        lib.qlin_forward_packed.argtypes = ([I, P, I64, P, I64, P, P, P, P, I64, P, P, P, I, ctypes.c_float, P, I64,
+                                             I64, I64, I64, P, ctypes.c_size_t, I, P])
+        lib.qlin_forward_packed.restype = I
         lib.qlin_forward_noalloc.argtypes = fwd[:-2] + [P]
         lib.qlin_forward_noalloc.restype = I
         lib.qlin_gather_columns.argtypes = [I, P, P, I64, I64, I64, I64, P]
@@ -243,8 +247,10 @@ def zeroed_workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
 
 
 def forward_raw(x2, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y2, ld_y,
-                M, K_g, N_g, algo=ALGO_AUTO, flags=0):
-    """Call ``qlin_forward_ex`` on prepared 2-D device tensors (see linear.py)."""
+                M, K_g, N_g, algo=ALGO_AUTO, flags=0, packed=None):
+    """Call ``qlin_forward_ex`` (``qlin_forward_packed`` with a packed weight
+    cache and the automatic kernel choice) on prepared 2-D device tensors
+    (see linear.py)."""
     lib = _lib if _lib is not None else load()
     dev = x2.device
     ws_bytes = workspace_size(x2.dtype, M, K_g, N_g, rank)
@@ -255,6 +261,14 @@ def forward_raw(x2, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y2, l
             flags |= FLAG_ZEROED_WORKSPACE
     if ws is None and ws_bytes:
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    if packed is not None and algo == ALGO_AUTO:
+        code = lib.qlin_forward_packed(
+            _DTYPE_CODE[x2.dtype], x2.data_ptr(), ld_x, packed.data_ptr(), K_g, w[0].data_ptr(), w[1].data_ptr(),
+            w[2].data_ptr(), w[3].data_ptr(), ld_w, _ptr(bias), _ptr(lora_a), _ptr(lora_b), rank, lora_scale,
+            y2.data_ptr(), ld_y, M, K_g, N_g, _ptr(ws), ws_bytes, flags,
+            torch._C._cuda_getCurrentRawStream(dev.index))
+        check(code, "qlin_forward_packed")
+        return y2
     fn = _fast.forward_ex if _fast is not None else lib.qlin_forward_ex
     code = fn(
         _DTYPE_CODE[x2.dtype], x2.data_ptr(), ld_x, w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(),

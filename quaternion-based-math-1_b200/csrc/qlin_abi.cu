@@ -27,6 +27,14 @@ using namespace qlin;
 
 constexpr int kMaxDevices = 64;
 
+// The packed weight cache of a call: wq[o][i][p] (all four components of a
+// weight quaternion side by side, the layout of x), ld in quaternions; null
+// when the call has planar weights only.
+struct PackedW {
+  const void* w = nullptr;
+  int64_t ld = 0;
+};
+
 struct DeviceInfo {
   bool init = false;
   int cc_major = 0, cc_minor = 0, num_sms = 0;
@@ -38,10 +46,10 @@ struct DeviceInfo {
   // [dtype][LoRA mode][split] (-1: not queried yet)
   int cluster_cap[2][3][kTcClusterMax + 1];
   // CUDA-core decode kernel: shared-memory limit raised, by [dtype][MT][LoRA][peers]
-  bool gemv_attr_set[2][3][2][2] = {};
+  bool gemv_attr_set[2][3][2][2][2] = {};  // [dtype][MT][LoRA][peers][packed]
   // CTA-pair prefill kernel: attributes set and how many pairs fit at once, by [dtype][peers][tile]
-  bool pair_attr_set[2][2][2] = {};
-  int pair_cap[2][2][2] = {};
+  bool pair_attr_set[2][2][2][2] = {};  // [dtype][peers][tile][packed]
+  int pair_cap[2][2][2][2] = {};
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mutex;
@@ -181,13 +189,17 @@ WsLayout ws_layout(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank) {
 
 int validate(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi, const void* wj,
              const void* wk, int64_t ld_w, const void* lora_a, const void* lora_b, int rank,
-             const void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g) {
+             const void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, const PackedW* pw = nullptr) {
+  const bool planar = wr || wi || wj || wk;
+  const bool packed = pw && pw->w;
   if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
   if (M < 0 || K_g <= 0 || N_g <= 0 || rank < 0) return QLIN_ERR_SHAPE;
-  if (ld_x < 4 * K_g || ld_w < K_g || ld_y < 4 * N_g) return QLIN_ERR_SHAPE;
+  if (ld_x < 4 * K_g || (planar && ld_w < K_g) || ld_y < 4 * N_g) return QLIN_ERR_SHAPE;
+  if (packed && pw->ld < K_g) return QLIN_ERR_SHAPE;
   if (M > INT32_MAX || N_g > INT32_MAX / 4 || K_g > INT32_MAX / 4) return QLIN_ERR_SHAPE;
   if (M == 0) return QLIN_OK;
-  if (!x || !wr || !wi || !wj || !wk || !y) return QLIN_ERR_ARG;
+  if (!x || !y || !(packed || planar)) return QLIN_ERR_ARG;
+  if (planar && (!wr || !wi || !wj || !wk)) return QLIN_ERR_ARG;
   if (rank > 0 && (!lora_a || !lora_b)) return QLIN_ERR_ARG;
   return QLIN_OK;
 }
@@ -487,13 +499,13 @@ bool pair_eligible(int64_t M, int64_t N_g, int rank, const void* y, int64_t ld_y
   return true;
 }
 
-template <typename T, bool PEERS, int NTOK>
+template <typename T, bool PEERS, int NTOK, bool PACKED = false>
 int pair_attrs(DeviceInfo* dev, int* cap) {
   const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
-  const int pi = PEERS ? 1 : 0, ti = NTOK == 256 ? 1 : 0;
+  const int pi = PEERS ? 1 : 0, ti = NTOK == 256 ? 1 : 0, ki = PACKED ? 1 : 0;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (!dev->pair_attr_set[di][pi][ti]) {
-    auto kernel = qlin_pair_kernel<T, PEERS, NTOK>;
+  if (!dev->pair_attr_set[di][pi][ti][ki]) {
+    auto kernel = qlin_pair_kernel<T, PEERS, NTOK, PACKED>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes) != cudaSuccess)
       return QLIN_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
@@ -512,10 +524,10 @@ int pair_attrs(DeviceInfo* dev, int* cap) {
       cudaGetLastError();
       return QLIN_ERR_LAUNCH;
     }
-    dev->pair_cap[di][pi][ti] = n;
-    dev->pair_attr_set[di][pi][ti] = true;
+    dev->pair_cap[di][pi][ti][ki] = n;
+    dev->pair_attr_set[di][pi][ti][ki] = true;
   }
-  *cap = dev->pair_cap[di][pi][ti];
+  *cap = dev->pair_cap[di][pi][ti][ki];
   return QLIN_OK;
 }
 
@@ -529,12 +541,12 @@ inline int64_t pair_tiles(int64_t M, int64_t N_g) {
   return ((4 * N_g + 255) / 256) * ((M + nt - 1) / nt);
 }
 
-template <typename T, bool PEERS, int NTOK>
-int launch_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
-                T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, const PeerOut& peers,
-                cudaStream_t stream) {
+template <typename T, bool PEERS, int NTOK, bool PACKED>
+int launch_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
+                const PackedW& pw, const T* bias, T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
+                const PeerOut& peers, cudaStream_t stream) {
   int cap = 0;
-  int st = pair_attrs<T, PEERS, NTOK>(dev, &cap);
+  int st = pair_attrs<T, PEERS, NTOK, PACKED>(dev, &cap);
   if (st != QLIN_OK) return st;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -550,13 +562,23 @@ int launch_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4
     if (encode(&maps[0], dt, 2, const_cast<T*>(x), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
       return QLIN_ERR_ALIGN;
   }
-  for (int p = 0; p < 4; ++p) {
-    cuuint64_t dims[2] = {(cuuint64_t)K_g, (cuuint64_t)N_g};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld_w * 2)};
-    cuuint32_t box[2] = {32, 32};
-    if (encode(&maps[1 + p], dt, 2, const_cast<void*>(w[p]), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B) !=
+  if (PACKED) {
+    // wq [N_g][ld][4]: 64-element (16-quaternion) x 32-row boxes, 128-byte swizzle
+    cuuint64_t dims[2] = {(cuuint64_t)(4 * K_g), (cuuint64_t)N_g};
+    cuuint64_t strides[1] = {(cuuint64_t)(pw.ld * 8)};
+    cuuint32_t box[2] = {64, 32};
+    if (encode(&maps[1], dt, 2, const_cast<void*>(pw.w), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
         CUDA_SUCCESS)
       return QLIN_ERR_ALIGN;
+  } else {
+    for (int p = 0; p < 4; ++p) {
+      cuuint64_t dims[2] = {(cuuint64_t)K_g, (cuuint64_t)N_g};
+      cuuint64_t strides[1] = {(cuuint64_t)(ld_w * 2)};
+      cuuint32_t box[2] = {32, 32};
+      if (encode(&maps[1 + p], dt, 2, const_cast<void*>(w[p]), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B) !=
+          CUDA_SUCCESS)
+        return QLIN_ERR_ALIGN;
+    }
   }
   const int64_t tiles = pair_tiles(M, N_g);
   if (tiles > INT32_MAX) return QLIN_ERR_SHAPE;
@@ -586,7 +608,7 @@ int launch_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4
   cfg.stream = stream;
   cfg.attrs = attrs;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, qlin_pair_kernel<T, PEERS, NTOK>, maps[0], maps[1], maps[2], maps[3], maps[4],
+  return cudaLaunchKernelEx(&cfg, qlin_pair_kernel<T, PEERS, NTOK, PACKED>, maps[0], maps[1], maps[2], maps[3], maps[4],
                             prm) == cudaSuccess
              ? QLIN_OK
              : QLIN_ERR_LAUNCH;
@@ -594,25 +616,36 @@ int launch_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4
 
 // Peer outputs (column-partitioned layer) get the kernel variant that also
 // stores every output piece into them.
-template <typename T>
-int run_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
-             T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, const PeerOut& peers, cudaStream_t stream) {
-  if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
+template <typename T, bool PEERS>
+int run_pair_p(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const PackedW& pw,
+               const T* bias, T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, const PeerOut& peers,
+               cudaStream_t stream) {
   const bool big = pair_tokens(M) == 256;
-  if (peers.n > 0)
-    return big ? launch_pair<T, true, 256>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, peers, stream)
-               : launch_pair<T, true, 128>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, peers, stream);
-  return big ? launch_pair<T, false, 256>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, peers, stream)
-             : launch_pair<T, false, 128>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, peers, stream);
+  if (pw.w)
+    return big ? launch_pair<T, PEERS, 256, true>(dev, x, ld_x, w, ld_w, pw, bias, y, ld_y, M, K_g, N_g, peers, stream)
+               : launch_pair<T, PEERS, 128, true>(dev, x, ld_x, w, ld_w, pw, bias, y, ld_y, M, K_g, N_g, peers, stream);
+  return big ? launch_pair<T, PEERS, 256, false>(dev, x, ld_x, w, ld_w, pw, bias, y, ld_y, M, K_g, N_g, peers, stream)
+             : launch_pair<T, PEERS, 128, false>(dev, x, ld_x, w, ld_w, pw, bias, y, ld_y, M, K_g, N_g, peers, stream);
 }
 
 template <typename T>
-int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w,
+int run_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const PackedW& pw,
+             const T* bias, T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, const PeerOut& peers,
+             cudaStream_t stream) {
+  if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
+  if (peers.n > 0) return run_pair_p<T, true>(dev, x, ld_x, w, ld_w, pw, bias, y, ld_y, M, K_g, N_g, peers, stream);
+  return run_pair_p<T, false>(dev, x, ld_x, w, ld_w, pw, bias, y, ld_y, M, K_g, N_g, peers, stream);
+}
+
+template <typename T>
+int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const PackedW& pw,
            const T* bias, const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y,
            int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, uint8_t* ws, int flags,
            const PeerOut& peers, cudaStream_t stream) {
-  if (pair_eligible(M, N_g, rank, y, ld_y, peers, flags))
-    return run_pair<T>(dev, x, ld_x, w, ld_w, bias, y, ld_y, M, K_g, N_g, peers, stream);
+  if (pair_eligible(M, N_g, rank, y, ld_y, peers, flags) &&
+      (!pw.w || (aligned(pw.w, 16) && pw.ld % 2 == 0)))
+    return run_pair<T>(dev, x, ld_x, w, ld_w, pw, bias, y, ld_y, M, K_g, N_g, peers, stream);
+  if (!w[0]) return QLIN_ERR_ALIGN;  // the other tensor-core paths read planar weights
   if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -786,19 +819,19 @@ int run_simt(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], 
   return QLIN_OK;
 }
 
-template <typename T, int MT, bool LORA, bool PEERS>
+template <typename T, int MT, bool LORA, bool PEERS, bool PACKED>
 int launch_gemv(DeviceInfo* dev, GemvParams prm, cudaStream_t stream) {
-  auto kernel = qlin_gemv_kernel<T, MT, LORA, PEERS>;
+  auto kernel = qlin_gemv_kernel<T, MT, LORA, PEERS, PACKED>;
   const size_t smem = gemv_smem_bytes(MT, prm.nch, LORA);
   const int di = std::is_same<T, __nv_bfloat16>::value ? 0 : 1;
   const int ti = MT == 1 ? 0 : (MT == 2 ? 1 : 2);
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (!dev->gemv_attr_set[di][ti][LORA][PEERS]) {
+    if (!dev->gemv_attr_set[di][ti][LORA][PEERS][PACKED]) {
       if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvMaxSmem) !=
           cudaSuccess)
         return QLIN_ERR_LAUNCH;
-      dev->gemv_attr_set[di][ti][LORA][PEERS] = true;
+      dev->gemv_attr_set[di][ti][LORA][PEERS][PACKED] = true;
     }
   }
   // one output quaternion per row warp, 8 row warps (+ the LoRA warp) per CTA;
@@ -820,21 +853,28 @@ int launch_gemv(DeviceInfo* dev, GemvParams prm, cudaStream_t stream) {
 
 template <typename T, int MT>
 int launch_gemv_mt(DeviceInfo* dev, const GemvParams& prm, cudaStream_t stream) {
-  return prm.rank > 0 ? launch_gemv<T, MT, true, false>(dev, prm, stream)
-                      : launch_gemv<T, MT, false, false>(dev, prm, stream);
+  if (prm.wq)
+    return prm.rank > 0 ? launch_gemv<T, MT, true, false, true>(dev, prm, stream)
+                        : launch_gemv<T, MT, false, false, true>(dev, prm, stream);
+  return prm.rank > 0 ? launch_gemv<T, MT, true, false, false>(dev, prm, stream)
+                      : launch_gemv<T, MT, false, false, false>(dev, prm, stream);
 }
 
 // CUDA-core decode kernel: one launch; with LoRA after the down-projection
 // prologue, whose t is in the workspace.
 template <typename T>
-int run_gemv(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const T* bias,
-             const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y, int64_t ld_y, int64_t M,
-             int64_t K_g, int64_t N_g, uint8_t* ws, int flags, const PeerOut& peers, cudaStream_t stream) {
+int run_gemv(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], int64_t ld_w, const PackedW& pw,
+             const T* bias, const T* lora_a, const T* lora_b, int rank, float lora_scale, T* y, int64_t ld_y,
+             int64_t M, int64_t K_g, int64_t N_g, uint8_t* ws, int flags, const PeerOut& peers,
+             cudaStream_t stream) {
   GemvParams prm{};
   prm.x = x;
   prm.ld_x = ld_x;
   for (int p = 0; p < 4; ++p) prm.w[p] = w[p];
   prm.ld_w = ld_w;
+  prm.wq = pw.w;
+  prm.ld_wq = pw.ld;
+  if (!pw.w && !w[0]) return QLIN_ERR_ALIGN;
   prm.bias = bias;
   prm.lora_a = rank > 0 ? lora_a : nullptr;
   prm.lora_b = rank > 0 ? lora_b : nullptr;
@@ -880,7 +920,7 @@ int run_gemv(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], 
 
 template <typename T>
 int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void* const w[4],
-             int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b, int rank,
+             int64_t ld_w, const PackedW& pw, const void* bias, const void* lora_a, const void* lora_b, int rank,
              float lora_scale, void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
              uint8_t* ws, int flags, const PeerOut& peers, cudaStream_t stream) {
   const T* xt = static_cast<const T*>(x);
@@ -889,6 +929,7 @@ int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void*
   const T* lb = static_cast<const T*>(lora_b);
   T* yt = static_cast<T*>(y);
   // peer outputs (column-partitioned layer) are written by the tensor-core path only
+  if (!w[0] && (algo == QLIN_ALGO_SIMT || std::is_same<T, float>::value)) return QLIN_ERR_ALIGN;
   if constexpr (std::is_same<T, float>::value) {
     if (peers.n > 0) return QLIN_ERR_ALIGN;
     return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
@@ -897,10 +938,10 @@ int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void*
     // peer outputs (the fused all-gather) are written by the tensor-core kernel only
     if (algo == QLIN_ALGO_GEMV && peers.n > 0) return QLIN_ERR_ALIGN;
     if (algo == QLIN_ALGO_GEMV)
-      return run_gemv<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws, flags,
+      return run_gemv<T>(dev, xt, ld_x, w, ld_w, pw, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws, flags,
                          peers, stream);
     if (algo == QLIN_ALGO_TC)
-      return run_tc<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
+      return run_tc<T>(dev, xt, ld_x, w, ld_w, pw, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
                        flags, peers, stream);
     if (peers.n > 0) return QLIN_ERR_ALIGN;
     return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
@@ -935,8 +976,8 @@ static int forward_common(int dtype, const void* x, int64_t ld_x, const void* wr
                           const void* wj, const void* wk, int64_t ld_w, const void* bias, const void* lora_a,
                           const void* lora_b, int rank, float lora_scale, void* y, int64_t ld_y, int64_t M,
                           int64_t K_g, int64_t N_g, void* workspace, size_t workspace_bytes, int algo, int flags,
-                          void* stream, const PeerOut& peers) {
-  int st = validate(dtype, x, ld_x, wr, wi, wj, wk, ld_w, lora_a, lora_b, rank, y, ld_y, M, K_g, N_g);
+                          void* stream, const PeerOut& peers, const PackedW& packed = PackedW()) {
+  int st = validate(dtype, x, ld_x, wr, wi, wj, wk, ld_w, lora_a, lora_b, rank, y, ld_y, M, K_g, N_g, &packed);
   if (st != QLIN_OK) return st;
   if (M == 0) return QLIN_OK;
   if (algo < QLIN_ALGO_AUTO || algo > QLIN_ALGO_GEMV) return QLIN_ERR_ARG;
@@ -947,10 +988,19 @@ static int forward_common(int dtype, const void* x, int64_t ld_x, const void* wr
   st = device_info(&dev);
   if (st != QLIN_OK) return st;
   const void* w[4] = {wr, wi, wj, wk};
+  // The packed weight cache serves the kernels that read it (the decode GEMV
+  // and the CTA-pair kernel): 16-bit types, a 16-byte aligned buffer, an even
+  // row length; the other paths read the planar weights.
+  PackedW pw = packed;
+  if (pw.w && (dtype == QLIN_F32 || !aligned(pw.w, 16) || pw.ld % 2 != 0 || K_g % 8 != 0)) pw = PackedW();
+  if (!pw.w && !wr) return QLIN_ERR_ALIGN;
+  // the packed GEMV does not read the planar weights: their alignment does not count
+  const void* const wnone[4] = {nullptr, nullptr, nullptr, nullptr};
+  const void* const* wg = pw.w ? wnone : w;
   if (algo == QLIN_ALGO_AUTO) {
     algo = select_algo(dtype);
     if (algo == QLIN_ALGO_TC && gemv_auto(M, N_g, rank, dev) &&
-        gemv_eligible(dtype, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, y, ld_y, M, K_g))
+        gemv_eligible(dtype, x, ld_x, wg, ld_w, bias, lora_a, lora_b, rank, y, ld_y, M, K_g))
       algo = QLIN_ALGO_GEMV;
     else if (algo == QLIN_ALGO_TC &&
              !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g))
@@ -959,7 +1009,7 @@ static int forward_common(int dtype, const void* x, int64_t ld_x, const void* wr
              !tc_eligible(dtype, x, ld_x, w, ld_w, lora_a, lora_b, rank, y, ld_y, K_g)) {
     return QLIN_ERR_ALIGN;
   } else if (algo == QLIN_ALGO_GEMV &&
-             !gemv_eligible(dtype, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, y, ld_y, M, K_g)) {
+             !gemv_eligible(dtype, x, ld_x, wg, ld_w, bias, lora_a, lora_b, rank, y, ld_y, M, K_g)) {
     return QLIN_ERR_ALIGN;
   }
   const WsLayout L = ws_layout(dtype, M, K_g, N_g, rank);
@@ -970,15 +1020,15 @@ static int forward_common(int dtype, const void* x, int64_t ld_x, const void* wr
   cudaGetLastError();  // clear stale errors so the check below is this call's
   switch (dtype) {
     case QLIN_F32:
-      st = dispatch<float>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
+      st = dispatch<float>(algo, dev, x, ld_x, w, ld_w, pw, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
                            K_g, N_g, ws, flags, peers, s);
       break;
     case QLIN_BF16:
-      st = dispatch<__nv_bfloat16>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
+      st = dispatch<__nv_bfloat16>(algo, dev, x, ld_x, w, ld_w, pw, bias, lora_a, lora_b, rank, lora_scale, y,
                                    ld_y, M, K_g, N_g, ws, flags, peers, s);
       break;
     default:
-      st = dispatch<__half>(algo, dev, x, ld_x, w, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
+      st = dispatch<__half>(algo, dev, x, ld_x, w, ld_w, pw, bias, lora_a, lora_b, rank, lora_scale, y, ld_y, M,
                             K_g, N_g, ws, flags, peers, s);
       break;
   }
@@ -1119,6 +1169,21 @@ int qlin_forward_ex(int dtype, const void* x, int64_t ld_x, const void* wr, cons
   none.n = 0;
   return forward_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y,
                         M, K_g, N_g, workspace, workspace_bytes, algo, flags, stream, none);
+}
+
+int qlin_forward_packed(int dtype, const void* x, int64_t ld_x, const void* wq, int64_t ld_wq, const void* wr,
+                        const void* wi, const void* wj, const void* wk, int64_t ld_w, const void* bias,
+                        const void* lora_a, const void* lora_b, int rank, float lora_scale, void* y, int64_t ld_y,
+                        int64_t M, int64_t K_g, int64_t N_g, void* workspace, size_t workspace_bytes, int flags,
+                        void* stream) {
+  if (!wq && M > 0) return QLIN_ERR_ARG;
+  PeerOut none;
+  none.n = 0;
+  PackedW pw;
+  pw.w = wq;
+  pw.ld = ld_wq;
+  return forward_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_y,
+                        M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_AUTO, flags, stream, none, pw);
 }
 
 int qlin_forward_allgather(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi,

@@ -50,6 +50,8 @@ struct GemvParams {
   int64_t ld_x;
   const void* w[4];
   int64_t ld_w;
+  const void* wq;      // packed weights [N_g][ld_wq][4] (PACKED kernels), else null
+  int64_t ld_wq;       // quaternions per packed row (even)
   const void* bias;    // [4*N_g] or null
   const void* lora_a;  // [rank, 4*K_g] or null
   const void* lora_b;  // [4*N_g, rank] or null
@@ -108,7 +110,13 @@ __device__ __forceinline__ void named_bar_arrive(int id, int threads) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <typename T, int MT, bool LORA, bool PEERS>
+// PACKED: the weights come from one interleaved buffer wq[o][i][p] (the
+// packed weight cache; the same layout as x rows): lane l reads 16-byte
+// pieces l, l+32, l+64, l+96 of each 256-quaternion chunk of row o -- piece u
+// holds all four components of input quaternions 2u and 2u+1, one address
+// stream per row instead of four -- and x is staged with even and odd
+// quaternions in separate halves so those reads stay conflict-free.
+template <typename T, int MT, bool LORA, bool PEERS, bool PACKED = false>
 __global__ void __launch_bounds__(kGemvLoraThreads, 1)
 qlin_gemv_kernel(const GemvParams prm) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -127,12 +135,21 @@ qlin_gemv_kernel(const GemvParams prm) {
   // ---- row warps: weights, bias, LoRA B ----
   uint4 wv[kGemvDepth][4];
   auto load_chunk = [&](int d, int c) {
-    const int i = c * kGemvChunk + 8 * lane;
-    const bool ok = row_ok && c < nch && i < prm.K_g;
+    if constexpr (PACKED) {
+      const T* row = reinterpret_cast<const T*>(prm.wq) + (int64_t)o * prm.ld_wq * 4;
 #pragma unroll
-    for (int p = 0; p < 4; ++p)
-      wv[d][p] = ok ? ld_w_v4(reinterpret_cast<const T*>(prm.w[p]) + (int64_t)o * prm.ld_w + i)
-                    : make_uint4(0u, 0u, 0u, 0u);
+      for (int u = 0; u < 4; ++u) {
+        const int i = c * kGemvChunk + 2 * (lane + 32 * u);  // first of the piece's two quaternions
+        wv[d][u] = (row_ok && c < nch && i < prm.K_g) ? ld_w_v4(row + 4 * (int64_t)i) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    } else {
+      const int i = c * kGemvChunk + 8 * lane;
+      const bool ok = row_ok && c < nch && i < prm.K_g;
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+        wv[d][p] = ok ? ld_w_v4(reinterpret_cast<const T*>(prm.w[p]) + (int64_t)o * prm.ld_w + i)
+                      : make_uint4(0u, 0u, 0u, 0u);
+    }
   };
   uint2 braw = make_uint2(0u, 0u);   // lane 0: bias of the 4 components
   uint2 lb = make_uint2(0u, 0u);     // LoRA B[4o + (lane>>3)][4*(lane&7) .. +4)
@@ -184,9 +201,16 @@ qlin_gemv_kernel(const GemvParams prm) {
         if (q < items) {
           const T* h = reinterpret_cast<const T*>(&raw[u]);
           const int m = q / nq, i = q - m * nq;
-          const int c = i / kGemvChunk, l = (i / 8) & 31, j = i & 7;
-          xs[((m * nch + c) * 8 + j) * 32 + (l ^ j)] =
-              make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
+          const int c = i / kGemvChunk;
+          const float4 v = make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
+          if constexpr (PACKED) {
+            // [m][c][parity][128 quaternion pairs]
+            const int ic = i - c * kGemvChunk;
+            xs[((m * nch + c) * 2 + (ic & 1)) * (kGemvChunk / 2) + (ic >> 1)] = v;
+          } else {
+            const int l = (i / 8) & 31, j = i & 7;
+            xs[((m * nch + c) * 8 + j) * 32 + (l ^ j)] = v;
+          }
         }
       }
     }
@@ -223,19 +247,36 @@ qlin_gemv_kernel(const GemvParams prm) {
     for (int d = 0; d < kGemvDepth; ++d) {
       const int c = cb + d;
       if (c < nch) {
+        // w0..w3[j]: components r, i, j, k of this lane's 8 weight quaternions
         float w0[8], w1[8], w2[8], w3[8];
-        unpack8<T>(wv[d][0], w0);
-        unpack8<T>(wv[d][1], w1);
-        unpack8<T>(wv[d][2], w2);
-        unpack8<T>(wv[d][3], w3);
+        if constexpr (PACKED) {
+          // piece u holds quaternions 2u' and 2u'+1 (u' = lane + 32u) as r,i,j,k,r,i,j,k
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float f[8];
+            unpack8<T>(wv[d][u], f);
+            w0[2 * u] = f[0]; w1[2 * u] = f[1]; w2[2 * u] = f[2]; w3[2 * u] = f[3];
+            w0[2 * u + 1] = f[4]; w1[2 * u + 1] = f[5]; w2[2 * u + 1] = f[6]; w3[2 * u + 1] = f[7];
+          }
+        } else {
+          unpack8<T>(wv[d][0], w0);
+          unpack8<T>(wv[d][1], w1);
+          unpack8<T>(wv[d][2], w2);
+          unpack8<T>(wv[d][3], w3);
+        }
         // refill: the chunk kGemvDepth further on reuses these registers
         if (c + kGemvDepth < nch) load_chunk(d, c + kGemvDepth);
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          const float4* xp = xs + ((m * nch + c) * 8) * 32;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float4 v = xp[j * 32 + (lane ^ j)];
+            float4 v;
+            if constexpr (PACKED) {
+              // quaternion 2 (lane + 32 (j / 2)) + (j % 2) of the chunk
+              v = xs[((m * nch + c) * 2 + (j & 1)) * (kGemvChunk / 2) + lane + 32 * (j >> 1)];
+            } else {
+              v = xs[((m * nch + c) * 8) * 32 + j * 32 + (lane ^ j)];
+            }
             float y0 = acc[m][0], y1 = acc[m][1], y2 = acc[m][2], y3 = acc[m][3];
             y0 = fmaf(w0[j], v.x, y0); y0 = fmaf(-w1[j], v.y, y0); y0 = fmaf(-w2[j], v.z, y0); y0 = fmaf(-w3[j], v.w, y0);
             y1 = fmaf(w0[j], v.y, y1); y1 = fmaf(w1[j], v.x, y1); y1 = fmaf(w2[j], v.w, y1); y1 = fmaf(-w3[j], v.z, y1);

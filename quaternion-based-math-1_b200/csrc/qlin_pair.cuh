@@ -206,7 +206,12 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) 
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-template <typename T, bool PEERS, int NTOK>
+// PACKED: the weights come from the interleaved buffer wq[o][i][p] (the
+// packed weight cache): a stage's W tile is two 32-row x 64-element boxes
+// (16 input quaternions each, 128-byte swizzle) loaded through map_wr, and
+// every builder lane reads all four components of an input quaternion from
+// one 8-byte piece of its row -- no shuffles between lanes.
+template <typename T, bool PEERS, int NTOK, bool PACKED = false>
 __global__ void __launch_bounds__(kPairThreads, 1)
 qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_wr,
                  const __grid_constant__ CUtensorMap map_wi, const __grid_constant__ CUtensorMap map_wj,
@@ -256,9 +261,11 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
     fence_mbar_init();
     tma_prefetch_desc(&map_x);
     tma_prefetch_desc(&map_wr);
-    tma_prefetch_desc(&map_wi);
-    tma_prefetch_desc(&map_wj);
-    tma_prefetch_desc(&map_wk);
+    if (!PACKED) {
+      tma_prefetch_desc(&map_wi);
+      tma_prefetch_desc(&map_wj);
+      tma_prefetch_desc(&map_wk);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, 512);
@@ -298,9 +305,18 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
           mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
           tma_load_2d(dst, &map_x, &full[s], k * kPairStageK, mrow);
           tma_load_2d(dst + Cfg::kXAtomBytes, &map_x, &full[s], k * kPairStageK + 64, mrow);
+          if constexpr (PACKED) {
+            // quaternions 32k .. 32k+15 and 32k+16 .. 32k+31 of rows n0/4 .. +31
 #pragma unroll
-          for (int p = 0; p < 4; ++p)
-            tma_load_2d(dst + Cfg::kXBytes + p * kPairWTileBytes, wmap[p], &full[s], k * (kPairStageK / 4), n0 / 4);
+            for (int h = 0; h < 2; ++h)
+              tma_load_2d(dst + Cfg::kXBytes + h * 2 * kPairWTileBytes, &map_wr, &full[s],
+                          k * kPairStageK + 64 * h, n0 / 4);
+          } else {
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+              tma_load_2d(dst + Cfg::kXBytes + p * kPairWTileBytes, wmap[p], &full[s], k * (kPairStageK / 4),
+                          n0 / 4);
+          }
           *issued = g + 1;
         }
         if (*abort_flag) break;
@@ -366,7 +382,43 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
       bool ok = !*abort_flag && mbar_wait(&full[s], n & 1);
       if (ok && na > 0) ok = mbar_wait(&aempty[sa], (na - 1) & 1);
       if (!ok) *abort_flag = 1;
-      if (!*abort_flag) {
+      if (!*abort_flag && PACKED) {
+        // row `row` of the two packed boxes: 128 bytes each, 16-byte chunk c
+        // (input quaternions 2c, 2c+1 of the box) at chunk c ^ (row & 7)
+        const uint32_t col = tmem + tm_lane + Cfg::kAColBase + sa * kPairACols;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t wrow = smem_u32(smem + s * Cfg::kStageBytes + Cfg::kXBytes + h * 2 * kPairWTileBytes + row * 128);
+          uint32_t r[32];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint32_t q[4];
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3])
+                         : "r"(wrow + ((c ^ (row & 7)) << 4))
+                         : "memory");
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              // quaternion 2c+e: lo = (W_0, W_1), hi = (W_2, W_3); this row wants
+              // (W_a, W_{a^1}) and (W_{a^2}, W_{a^3}), signed
+              uint32_t lo = q[2 * e], hi = q[2 * e + 1];
+              if (a & 2) {
+                const uint32_t t = lo;
+                lo = hi;
+                hi = t;
+              }
+              if (a & 1) {
+                lo = __byte_perm(lo, lo, 0x1032);
+                hi = __byte_perm(hi, hi, 0x1032);
+              }
+              r[4 * c + 2 * e] = lo ^ sg01;
+              r[4 * c + 2 * e + 1] = hi ^ sg23;
+            }
+          }
+          tmem_st32(col + 32 * h, r);
+        }
+        tmem_st_wait();
+      } else if (!*abort_flag) {
         // W_a[o, 32 inputs]: 64 bytes, chunk c at chunk c ^ ((row >> 1) & 3) (64-byte swizzle)
         const uint32_t wrow =
             smem_u32(smem + s * Cfg::kStageBytes + Cfg::kXBytes + a * kPairWTileBytes + row * 64);

@@ -69,7 +69,7 @@ void shape_error(const std::string& msg) { throw pybind11::value_error(msg); }
 at::Tensor forward(const at::Tensor& x, const at::Tensor& wr, const at::Tensor& wi, const at::Tensor& wj,
                    const at::Tensor& wk, const c10::optional<at::Tensor>& bias_opt,
                    const c10::optional<at::Tensor>& lora_a_opt, const c10::optional<at::Tensor>& lora_b_opt,
-                   double lora_scale, bool static_weights) {
+                   double lora_scale, bool static_weights, const c10::optional<at::Tensor>& packed_opt) {
   // shapes first, as the reference validates them before touching devices
   const int64_t K = x.dim() > 0 ? x.size(-1) : 0;
   if (x.dim() == 0 || K % 4 != 0)
@@ -107,6 +107,14 @@ at::Tensor forward(const at::Tensor& x, const at::Tensor& wr, const at::Tensor& 
   if (has_a) {
     all.push_back(&*lora_a_opt);
     all.push_back(&*lora_b_opt);
+  }
+  // the packed weight cache [out_groups, in_groups, 4] (the module's, or none)
+  const bool has_packed = packed_opt.has_value() && packed_opt->defined();
+  if (has_packed) {
+    TORCH_CHECK(packed_opt->dim() == 3 && packed_opt->size(0) == out_groups && packed_opt->size(1) == in_groups &&
+                    packed_opt->size(2) == 4 && packed_opt->is_contiguous(),
+                "packed weights must be a contiguous [out_groups, in_groups, 4] tensor");
+    all.push_back(&*packed_opt);
   }
   for (const at::Tensor* t : all) {
     TORCH_CHECK(t->is_cuda(),
@@ -152,11 +160,19 @@ at::Tensor forward(const at::Tensor& x, const at::Tensor& wr, const at::Tensor& 
     }
     if (!ws.defined() && ws_bytes > 0)
       ws = at::empty({static_cast<int64_t>(ws_bytes)}, at::TensorOptions().dtype(at::kByte).device(x.device()));
-    st = qlin_forward_ex(code, x2.data_ptr(), x2.stride(0), w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(),
-                         w[3].data_ptr(), ld_w, has_bias ? b.data_ptr() : nullptr, rank ? la.data_ptr() : nullptr,
-                         rank ? lb.data_ptr() : nullptr, static_cast<int>(rank), static_cast<float>(lora_scale),
-                         y.data_ptr(), 4 * out_groups, M, in_groups, out_groups,
-                         ws.defined() ? ws.data_ptr() : nullptr, ws_bytes, QLIN_ALGO_AUTO, flags, stream);
+    if (has_packed)
+      st = qlin_forward_packed(code, x2.data_ptr(), x2.stride(0), packed_opt->data_ptr(), in_groups,
+                               w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(), w[3].data_ptr(), ld_w,
+                               has_bias ? b.data_ptr() : nullptr, rank ? la.data_ptr() : nullptr,
+                               rank ? lb.data_ptr() : nullptr, static_cast<int>(rank),
+                               static_cast<float>(lora_scale), y.data_ptr(), 4 * out_groups, M, in_groups,
+                               out_groups, ws.defined() ? ws.data_ptr() : nullptr, ws_bytes, flags, stream);
+    else
+      st = qlin_forward_ex(code, x2.data_ptr(), x2.stride(0), w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(),
+                           w[3].data_ptr(), ld_w, has_bias ? b.data_ptr() : nullptr, rank ? la.data_ptr() : nullptr,
+                           rank ? lb.data_ptr() : nullptr, static_cast<int>(rank), static_cast<float>(lora_scale),
+                           y.data_ptr(), 4 * out_groups, M, in_groups, out_groups,
+                           ws.defined() ? ws.data_ptr() : nullptr, ws_bytes, QLIN_ALGO_AUTO, flags, stream);
     if (st == QLIN_ERR_SHAPE) shape_error(std::string("qlin_forward: ") + qlin_status_string(st));
     TORCH_CHECK(st == QLIN_OK, "qlin_forward: ", qlin_status_string(st), " (status ", st, ")");
   }
@@ -179,6 +195,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("wr"), pybind11::arg("wi"), pybind11::arg("wj"), pybind11::arg("wk"),
         pybind11::arg("bias") = pybind11::none(), pybind11::arg("lora_a") = pybind11::none(),
         pybind11::arg("lora_b") = pybind11::none(), pybind11::arg("lora_scale") = 0.0,
-        pybind11::arg("static_weights") = false);
+        pybind11::arg("static_weights") = false, pybind11::arg("packed") = pybind11::none());
   m.def("workspaces", &workspaces, "the cached zero-filled decode workspaces");
 }

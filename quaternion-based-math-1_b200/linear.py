@@ -105,13 +105,13 @@ def _weights(ws):
 
 
 def _forward_impl(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=None, lora_scale=0.0,
-                  algo=_lib.ALGO_AUTO, static_weights=False):
+                  algo=_lib.ALGO_AUTO, static_weights=False, packed=None):
     if algo == _lib.ALGO_AUTO:
         ext = _lib._torch_ext if _lib._lib is not None else (_lib.load() and _lib._torch_ext)
         if ext is not None:
             # the same checks, allocation and call in C++ (csrc/qlin_torch_ext.cpp)
             return ext.forward(x, wr, wi, wj, wk, bias, lora_a, lora_b, float(lora_scale),
-                               bool(static_weights))
+                               bool(static_weights), packed)
     in_groups, out_groups = _validate(x, wr, wi, wj, wk)
     if bias is not None and (bias.dim() != 1 or bias.shape[0] != 4 * out_groups):
         raise ValueError(f"bias must be [{4 * out_groups}], got {tuple(bias.shape)}")
@@ -148,11 +148,11 @@ def _forward_impl(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=None, lora_s
         # the library launches on the current device: switch only when needed
         if torch._C._cuda_getDevice() == dev.index:
             _lib.forward_raw(x2, ld_x, ws, ld_w, b, la, lb, rank, float(lora_scale), y, 4 * out_groups,
-                             M, in_groups, out_groups, int(algo), flags)
+                             M, in_groups, out_groups, int(algo), flags, packed=packed)
         else:
             with torch.cuda.device(dev):
                 _lib.forward_raw(x2, ld_x, ws, ld_w, b, la, lb, rank, float(lora_scale), y,
-                                 4 * out_groups, M, in_groups, out_groups, int(algo), flags)
+                                 4 * out_groups, M, in_groups, out_groups, int(algo), flags, packed=packed)
     return y.reshape(*lead, 4 * out_groups)
 
 
@@ -218,19 +218,30 @@ class _QLinFn(torch.autograd.Function):
 
 
 def fused_quaternion_linear(x, wr, wi, wj, wk, bias=None, lora_a=None, lora_b=None,
-                            lora_scale: float = 0.0, static_weights: bool = False):
+                            lora_scale: float = 0.0, static_weights: bool = False, packed=None):
     """``quaternion_linear(x) + bias + lora_scale * (x A^T) B^T`` in one device call.
 
     ``static_weights=True`` declares that nothing queued earlier on the current
     stream writes the weights, bias or LoRA A/B (inference with fixed weights):
     the kernel may then stream them while the previous kernel finishes.
+    ``packed``: the same weights as one ``[out_groups, in_groups, 4]`` tensor
+    (:func:`pack_quaternion_weights`), read by the kernels that take it (the
+    decode GEMV and the CTA-pair prefill kernel); ignored under autograd.
     """
     if torch.is_grad_enabled():
         for t in (x, wr, wi, wj, wk, bias, lora_a, lora_b):
             if t is not None and t.requires_grad:
                 return _QLinFn.apply(x, wr, wi, wj, wk, bias, lora_a, lora_b, float(lora_scale))
     return _forward_impl(x, wr, wi, wj, wk, bias, lora_a, lora_b, lora_scale,
-                         static_weights=static_weights)
+                         static_weights=static_weights, packed=packed)
+
+
+def pack_quaternion_weights(wr, wi, wj, wk) -> torch.Tensor:
+    """The packed weight layout ``[out_groups, in_groups, 4]``: component p of
+    weight quaternion (o, i) at ``[o, i, p]`` -- the layout of ``x`` rows, so
+    one 16-byte load holds two whole weight quaternions."""
+    with torch.no_grad():
+        return torch.stack((wr, wi, wj, wk), dim=-1).contiguous()
 
 
 def quaternion_linear(x, wr, wi, wj, wk) -> torch.Tensor:
@@ -267,6 +278,12 @@ class QuaternionLinear(nn.Module):
         # declares the weights static for the duration of the call, letting
         # the kernel stream them while the previous kernel of the stream ends.
         self.static_weights = False
+        # Inference option (not part of the state dict; the parameters stay
+        # wr, wi, wj, wk): when True, forward without autograd also keeps the
+        # packed weight cache (packed_weights) and hands it to the kernels
+        # that read it.
+        self.packed = False
+        self._packed_cache = None
         self.reset_parameters()
 
     def reset_parameters(self) -> None:
@@ -278,9 +295,30 @@ class QuaternionLinear(nn.Module):
         if self.bias is not None:
             nn.init.uniform_(self.bias, -bound, bound)
 
+    def packed_weights(self) -> torch.Tensor:
+        """The packed weight cache ``[out_groups, in_groups, 4]``
+        (:func:`pack_quaternion_weights`), rebuilt whenever a component is
+        replaced, moved or updated in place (its version counter advances)."""
+        key = tuple((w.data_ptr(), w._version, w.dtype, w.device, tuple(w.shape))
+                    for w in (self.wr, self.wi, self.wj, self.wk))
+        cache = self._packed_cache
+        if cache is None or cache[0] != key:
+            cache = self._packed_cache = (key, pack_quaternion_weights(self.wr, self.wi, self.wj, self.wk))
+        return cache[1]
+
+    def _packed_for_call(self, *tensors):
+        """The packed cache when this call may use it (``packed`` set, no autograd)."""
+        if not getattr(self, "packed", False):
+            return None
+        if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors):
+            return None
+        return self.packed_weights()
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return fused_quaternion_linear(x, self.wr, self.wi, self.wj, self.wk, self.bias,
-                                       static_weights=self.static_weights)
+                                       static_weights=self.static_weights,
+                                       packed=self._packed_for_call(x, self.wr, self.wi, self.wj, self.wk,
+                                                                    self.bias))
 
     def real_block_matrix(self) -> torch.Tensor:
         """The equivalent real ``[out_features, in_features]`` matrix (verification only)."""

@@ -67,7 +67,8 @@ class LoRAQuaternionLinear(nn.Module):
             lora = (self.lora_dropout(x) @ self.lora_A.t()) @ self.lora_B.t()
             return out + self.scale * lora
         return fused_quaternion_linear(x, b.wr, b.wi, b.wj, b.wk, b.bias, self.lora_A, self.lora_B,
-                                       self.scale, static_weights=b.static_weights)
+                                       self.scale, static_weights=b.static_weights,
+                                       packed=b._packed_for_call(x, self.lora_A, self.lora_B))
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
