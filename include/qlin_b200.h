@@ -175,7 +175,8 @@ int qlin_forward_ex(int dtype,
  *
  *   wq     [N_g][ld_wq][4]: wq[o][i][p] = W_p[o][i], all four components of a
  *          weight quaternion side by side (the layout of x rows); ld_wq in
- *          quaternions, even; 16-byte aligned; bf16/f16 only
+ *          quaternions, even; 16-byte aligned; bf16/f16 only; K_g a multiple
+ *          of 8 (otherwise the planar weights are used)
  *   wr..wk the planar components as in qlin_forward, or all four NULL
  * The kernels that read the packed buffer take it: the decode GEMV (at most
  * 2 tokens) reads one address stream per output row instead of four, and the

@@ -57,7 +57,7 @@ def _planar_call(qb, d, M, K_g, N_g, rank):
 @pytest.mark.parametrize("dtype,M,fin,fout,rank", [
     ("bf16", 1, 4096, 4096, 32),   # decode GEMV with its LoRA prologue
     ("bf16", 2, 1024, 2048, 0),
-    ("f16", 1, 520, 264, 8),       # K tail inside a chunk
+    ("f16", 1, 544, 264, 8),       # 136 input quaternions: a partial 256-quaternion chunk
     ("bf16", 300, 1024, 1040, 0),  # CTA-pair kernel, partial tiles
     ("bf16", 2048, 4096, 11008, 0),
 ])
