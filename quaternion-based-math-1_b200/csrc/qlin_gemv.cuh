@@ -110,6 +110,149 @@ __device__ __forceinline__ void named_bar_arrive(int id, int threads) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Stages x as fp32 quaternions in shared memory (zeros past K_g and past M).
+// Item (token m, input quaternion i), numbered m * nq + i: thread tid of
+// nthr converts items tid, tid + nthr, ...  (m, i) advance by nthr (at most
+// 2 nq) without a division: measured, a division per load delayed the x
+// loads by half a microsecond.  issue() requests a batch of 8 items (all its
+// loads before any is used), store() converts and stores it.
+template <typename T, int MT, bool PACKED>
+struct GemvXStager {
+  const T* xg;
+  int64_t ld_x;
+  int M, K_g, nch, nq, nthr, xm, xi;
+  float4* xs;
+  uint2 raw[8];
+  __device__ __forceinline__ GemvXStager(const void* x, int64_t ld, int M_, int K_g_, int nch_, int tid, int nthr_,
+                                         float4* xs_)
+      : xg(reinterpret_cast<const T*>(x)), ld_x(ld), M(M_), K_g(K_g_), nch(nch_), nq(nch_ * kGemvChunk),
+        nthr(nthr_), xm(tid / (nch_ * kGemvChunk)), xi(tid - (tid / (nch_ * kGemvChunk)) * (nch_ * kGemvChunk)),
+        xs(xs_) {}
+  __device__ __forceinline__ void advance(int& m, int& i) const {
+    i += nthr;
+    if (i >= nq) { i -= nq; ++m; }
+    if (i >= nq) { i -= nq; ++m; }
+  }
+  __device__ __forceinline__ bool more() const { return xm < MT; }
+  __device__ __forceinline__ void issue() {
+    int m = xm, i = xi;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      raw[u] = (m < MT && m < M && i < K_g) ? ld_cg_v2(xg + (int64_t)m * ld_x + 4 * (int64_t)i) : make_uint2(0u, 0u);
+      advance(m, i);
+    }
+  }
+  __device__ __forceinline__ void store() {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (xm < MT) {
+        const T* h = reinterpret_cast<const T*>(&raw[u]);
+        const float4 v = make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
+        const int c = xi / kGemvChunk;
+        if constexpr (PACKED) {
+          // [m][c][parity][128 quaternion pairs]
+          const int ic = xi - c * kGemvChunk;
+          xs[((xm * nch + c) * 2 + (ic & 1)) * (kGemvChunk / 2) + (ic >> 1)] = v;
+        } else {
+          const int l = (xi / 8) & 31, j = xi & 7;
+          xs[((xm * nch + c) * 8 + j) * 32 + (l ^ j)] = v;
+        }
+      }
+      advance(xm, xi);
+    }
+  }
+};
+
+// One chunk of a row warp's Hamilton products: w0..w3[j] are components r,
+// i, j, k of this lane's 8 weight quaternions of chunk c, x comes from the
+// staged copy.
+template <int MT, bool PACKED>
+__device__ __forceinline__ void gemv_chunk_fma(float (&acc)[MT][4], const float (&w0)[8], const float (&w1)[8],
+                                               const float (&w2)[8], const float (&w3)[8], const float4* xs,
+                                               int nch, int c, int lane) {
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 v;
+      if constexpr (PACKED) {
+        // quaternion 2 (lane + 32 (j / 2)) + (j % 2) of the chunk
+        v = xs[((m * nch + c) * 2 + (j & 1)) * (kGemvChunk / 2) + lane + 32 * (j >> 1)];
+      } else {
+        v = xs[((m * nch + c) * 8) * 32 + j * 32 + (lane ^ j)];
+      }
+      float y0 = acc[m][0], y1 = acc[m][1], y2 = acc[m][2], y3 = acc[m][3];
+      y0 = fmaf(w0[j], v.x, y0); y0 = fmaf(-w1[j], v.y, y0); y0 = fmaf(-w2[j], v.z, y0); y0 = fmaf(-w3[j], v.w, y0);
+      y1 = fmaf(w0[j], v.y, y1); y1 = fmaf(w1[j], v.x, y1); y1 = fmaf(w2[j], v.w, y1); y1 = fmaf(-w3[j], v.z, y1);
+      y2 = fmaf(w0[j], v.z, y2); y2 = fmaf(-w1[j], v.w, y2); y2 = fmaf(w2[j], v.x, y2); y2 = fmaf(w3[j], v.y, y2);
+      y3 = fmaf(w0[j], v.w, y3); y3 = fmaf(w1[j], v.z, y3); y3 = fmaf(-w2[j], v.y, y3); y3 = fmaf(w3[j], v.x, y3);
+      acc[m][0] = y0; acc[m][1] = y1; acc[m][2] = y2; acc[m][3] = y3;
+    }
+  }
+}
+
+// After a row warp's last chunk: sum the 32 lanes, add the LoRA up
+// projection (lane l takes component l>>3, ranks 4(l&7)..+3 of this row's
+// B, braw/lb as loaded; t in shared memory once the named barrier with the
+// LoRA warp passes) and the bias, round once and let lane 0 store the
+// output quaternion of every token.
+template <typename T, int MT, bool LORA, bool PEERS>
+__device__ __forceinline__ void gemv_finish(float (&acc)[MT][4], uint2 braw, uint2 lb, const float* tsum, int lane,
+                                            bool row_ok, int o, int M, void* y_, int64_t ld_y, const PeerOut& peers) {
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int s = 16; s >= 1; s >>= 1) acc[m][a] += __shfl_xor_sync(0xffffffffu, acc[m][a], s);
+
+  float lora[MT][4];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int a = 0; a < 4; ++a) lora[m][a] = 0.f;
+  if constexpr (LORA) {
+    named_bar_sync(kGemvLoraBar, kGemvLoraThreads);  // the LoRA warp has written t
+    const T* bh = reinterpret_cast<const T*>(&lb);
+    const int lb_r = 4 * (lane & 7);
+    float part[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float4 t = *reinterpret_cast<const float4*>(tsum + m * kGemvMaxRank + lb_r);
+      float s = to_f32(bh[0]) * t.x;
+      s = fmaf(to_f32(bh[1]), t.y, s);
+      s = fmaf(to_f32(bh[2]), t.z, s);
+      s = fmaf(to_f32(bh[3]), t.w, s);
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      part[m] = s;  // lanes 8a..8a+7 hold component a (t carries lora_scale)
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int a = 0; a < 4; ++a) lora[m][a] = __shfl_sync(0xffffffffu, part[m], 8 * a);
+  }
+
+  if (row_ok && lane == 0) {
+    const T* bh = reinterpret_cast<const T*>(&braw);
+    float b[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) b[a] = to_f32(bh[a]);
+    T* __restrict__ y = reinterpret_cast<T*>(y_);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m < M)
+        store_out<T, PEERS>(y, peers, (int64_t)m * ld_y + 4 * (int64_t)o,
+                            pack4<T>(acc[m][0] + lora[m][0] + b[0], acc[m][1] + lora[m][1] + b[1],
+                                     acc[m][2] + lora[m][2] + b[2], acc[m][3] + lora[m][3] + b[3]));
+    }
+  }
+  // Outputs stored to peers are performed at system scope before the CTA
+  // ends, so the barrier kernel that follows may signal them.
+  if (PEERS) fence_sys();
+}
+
 // PACKED: the weights come from one interleaved buffer wq[o][i][p] (the
 // packed weight cache; the same layout as x rows): lane l reads 16-byte
 // pieces l, l+32, l+64, l+96 of each 256-quaternion chunk of row o -- piece u
@@ -165,12 +308,15 @@ qlin_gemv_kernel(const GemvParams prm) {
   // they are static).  With LoRA it follows this call's prologue, whose
   // launch of it implies that all earlier work is complete: no wait before
   // the weights and x, only the LoRA warp waits, for t.
+  // x (a few KB) is requested ahead of the weight stream
+  GemvXStager<T, MT, PACKED> xst(prm.x, prm.ld_x, prm.M, prm.K_g, nch, tid, nthr, xs);
   if (!LORA && prm.static_weights) {
 #pragma unroll
     for (int d = 0; d < kGemvDepth; ++d) load_chunk(d, d);
     load_small();
   }
   if (!LORA) pdl_wait_prior();
+  xst.issue();
   if (LORA || !prm.static_weights) {
     if (!lora_warp) {
 #pragma unroll
@@ -180,40 +326,10 @@ qlin_gemv_kernel(const GemvParams prm) {
   }
 
   // ---- stage x as fp32 quaternions (zeros past K_g and past M) ----
-  // Item q = (token m, input quaternion i) with i running over all chunks;
-  // thread tid converts items tid, tid + blockDim, ...  All of a batch's
-  // loads are issued before any is stored.
-  {
-    const T* __restrict__ x = reinterpret_cast<const T*>(prm.x);
-    const int nq = nch * kGemvChunk, items = MT * nq;
-    for (int b0 = 0; b0 < items; b0 += 8 * nthr) {
-      uint2 raw[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int q = b0 + u * nthr + tid, m = q / nq, i = q - m * nq;
-        raw[u] = (q < items && m < prm.M && i < prm.K_g)
-                     ? ld_cg_v2(x + (int64_t)m * prm.ld_x + 4 * (int64_t)i)
-                     : make_uint2(0u, 0u);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int q = b0 + u * nthr + tid;
-        if (q < items) {
-          const T* h = reinterpret_cast<const T*>(&raw[u]);
-          const int m = q / nq, i = q - m * nq;
-          const int c = i / kGemvChunk;
-          const float4 v = make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
-          if constexpr (PACKED) {
-            // [m][c][parity][128 quaternion pairs]
-            const int ic = i - c * kGemvChunk;
-            xs[((m * nch + c) * 2 + (ic & 1)) * (kGemvChunk / 2) + (ic >> 1)] = v;
-          } else {
-            const int l = (i / 8) & 31, j = i & 7;
-            xs[((m * nch + c) * 8 + j) * 32 + (l ^ j)] = v;
-          }
-        }
-      }
-    }
+  xst.store();
+  while (xst.more()) {
+    xst.issue();
+    xst.store();
   }
   __syncthreads();
 
@@ -266,81 +382,11 @@ qlin_gemv_kernel(const GemvParams prm) {
         }
         // refill: the chunk kGemvDepth further on reuses these registers
         if (c + kGemvDepth < nch) load_chunk(d, c + kGemvDepth);
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 v;
-            if constexpr (PACKED) {
-              // quaternion 2 (lane + 32 (j / 2)) + (j % 2) of the chunk
-              v = xs[((m * nch + c) * 2 + (j & 1)) * (kGemvChunk / 2) + lane + 32 * (j >> 1)];
-            } else {
-              v = xs[((m * nch + c) * 8) * 32 + j * 32 + (lane ^ j)];
-            }
-            float y0 = acc[m][0], y1 = acc[m][1], y2 = acc[m][2], y3 = acc[m][3];
-            y0 = fmaf(w0[j], v.x, y0); y0 = fmaf(-w1[j], v.y, y0); y0 = fmaf(-w2[j], v.z, y0); y0 = fmaf(-w3[j], v.w, y0);
-            y1 = fmaf(w0[j], v.y, y1); y1 = fmaf(w1[j], v.x, y1); y1 = fmaf(w2[j], v.w, y1); y1 = fmaf(-w3[j], v.z, y1);
-            y2 = fmaf(w0[j], v.z, y2); y2 = fmaf(-w1[j], v.w, y2); y2 = fmaf(w2[j], v.x, y2); y2 = fmaf(w3[j], v.y, y2);
-            y3 = fmaf(w0[j], v.w, y3); y3 = fmaf(w1[j], v.z, y3); y3 = fmaf(-w2[j], v.y, y3); y3 = fmaf(w3[j], v.x, y3);
-            acc[m][0] = y0; acc[m][1] = y1; acc[m][2] = y2; acc[m][3] = y3;
-          }
-        }
+        gemv_chunk_fma<MT, PACKED>(acc, w0, w1, w2, w3, xs, nch, c, lane);
       }
     }
   }
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-      for (int s = 16; s >= 1; s >>= 1) acc[m][a] += __shfl_xor_sync(0xffffffffu, acc[m][a], s);
-
-  // ---- LoRA up projection: lane l takes component l>>3, ranks 4(l&7)..+3 ----
-  float lora[MT][4];
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int a = 0; a < 4; ++a) lora[m][a] = 0.f;
-  if constexpr (LORA) {
-    named_bar_sync(kGemvLoraBar, kGemvLoraThreads);  // the LoRA warp has written t
-    const T* bh = reinterpret_cast<const T*>(&lb);
-    float part[MT];
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      const float4 t = *reinterpret_cast<const float4*>(tsum + m * kGemvMaxRank + lb_r);
-      float s = to_f32(bh[0]) * t.x;
-      s = fmaf(to_f32(bh[1]), t.y, s);
-      s = fmaf(to_f32(bh[2]), t.z, s);
-      s = fmaf(to_f32(bh[3]), t.w, s);
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      s += __shfl_xor_sync(0xffffffffu, s, 4);
-      part[m] = s;  // lanes 8a..8a+7 hold component a (t carries lora_scale)
-    }
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-      for (int a = 0; a < 4; ++a) lora[m][a] = __shfl_sync(0xffffffffu, part[m], 8 * a);
-  }
-
-  // ---- epilogue: lane 0 adds bias and LoRA, rounds once, stores 8 bytes per token ----
-  if (row_ok && lane == 0) {
-    const T* bh = reinterpret_cast<const T*>(&braw);
-    float b[4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a) b[a] = to_f32(bh[a]);
-    T* __restrict__ y = reinterpret_cast<T*>(prm.y);
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      if (m < prm.M)
-        store_out<T, PEERS>(y, prm.peers, (int64_t)m * prm.ld_y + 4 * (int64_t)o,
-                            pack4<T>(acc[m][0] + lora[m][0] + b[0], acc[m][1] + lora[m][1] + b[1],
-                                     acc[m][2] + lora[m][2] + b[2], acc[m][3] + lora[m][3] + b[3]));
-    }
-  }
-  // Outputs stored to peers are performed at system scope before the CTA
-  // ends, so the barrier kernel that follows may signal them.
-  if (PEERS) fence_sys();
+  gemv_finish<T, MT, LORA, PEERS>(acc, braw, lb, tsum, lane, row_ok, o, prm.M, prm.y, prm.ld_y, prm.peers);
 }
 
 }  // namespace qlin
