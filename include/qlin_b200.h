@@ -40,7 +40,8 @@ enum {
   QLIN_ERR_LAUNCH = 5,    /* a CUDA runtime call or kernel launch failed        */
   QLIN_ERR_DEVICE = 6,    /* the current device is not sm_100 (B200 class)      */
   QLIN_ERR_TIMEOUT = 7,   /* a bounded device-side wait ran out (see below)     */
-  QLIN_ERR_ARG = 8        /* null pointer or invalid option                     */
+  QLIN_ERR_ARG = 8,       /* null pointer or invalid option                     */
+  QLIN_ERR_COLLECTIVE = 9 /* NCCL not loadable, or an NCCL call failed          */
 };
 
 /* Kernel selection for qlin_forward_ex (QLIN_ALGO_AUTO is what qlin_forward uses). */
@@ -247,6 +248,54 @@ int qlin_forward_allgather(int dtype,
                            void* const* outs, int64_t ld_out, int64_t col_offset,
                            unsigned* const* flag_arrays, unsigned* epoch_word,
                            void* stream);
+
+/*
+ * Column-partitioned layer over NCCL (no reference counterpart: the exchange
+ * of a layer whose output quaternions are split over `world` GPUs), for
+ * hosts that hold an NCCL communicator but no peer-mapped output buffers.
+ *
+ * This process is rank world_rank of nccl_comm (an ncclComm_t of `world`
+ * ranks on the current device).  Every rank passes its own slice of the
+ * layer: wr..wk [N_g, ld_w] are its output quaternions [world_rank * N_g,
+ * (world_rank + 1) * N_g), bias [4 N_g] and lora_b [4 N_g, rank] the same
+ * rows; x and lora_a are the full inputs, equal on every rank.  y [M, ld_y]
+ * with ld_y >= world * 4 * N_g receives every rank's columns, rank r's at
+ * column offset r * 4 * N_g (the full layer's output on every rank).
+ *
+ * On `stream`: this rank's columns by the single-GPU kernels (for M == 1
+ * straight into y, else into the workspace), one ncclAllGather of M * 4 * N_g
+ * elements per rank, and for M > 1 one kernel that places the gathered
+ * column blocks into y's rows.  workspace: at least
+ * qlin_sharded_workspace_size() bytes, used as qlin_forward_ex's with the
+ * same flags.  The NCCL library is the one the process has already loaded,
+ * else libnccl.so.2; QLIN_ERR_COLLECTIVE when neither is found or an NCCL
+ * call fails.  Capturable in a CUDA graph when NCCL's own calls are.
+ */
+int qlin_sharded_fwd(int dtype,
+                     const void* x, int64_t ld_x,
+                     const void* wr, const void* wi, const void* wj, const void* wk,
+                     int64_t ld_w,
+                     const void* bias,
+                     const void* lora_a, const void* lora_b, int rank, float lora_scale,
+                     void* y, int64_t ld_y,
+                     int64_t M, int64_t K_g, int64_t N_g,
+                     void* workspace, size_t workspace_bytes, int flags,
+                     void* nccl_comm, int world, int world_rank,
+                     void* stream);
+int qlin_sharded_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int world,
+                                size_t* bytes);
+
+/*
+ * NCCL bootstrap for callers of qlin_sharded_fwd that have no NCCL binding of
+ * their own (the same library it calls): qlin_nccl_unique_id writes a
+ * 128-byte ncclUniqueId, which the caller sends to every rank by its own
+ * means; qlin_nccl_comm_init creates this rank's communicator on the current
+ * device (blocking until all `world` ranks joined, as ncclCommInitRank);
+ * qlin_nccl_comm_destroy releases it.
+ */
+int qlin_nccl_unique_id(void* id);
+int qlin_nccl_comm_init(void** comm, int world, const void* id, int world_rank);
+int qlin_nccl_comm_destroy(void* comm);
 
 /*
  * Buffers shared between the processes of a column-partitioned layer (no

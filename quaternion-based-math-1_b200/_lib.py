@@ -55,6 +55,11 @@ EXPORTED = (
     "qlin_ipc_free",
     "qlin_ipc_open",
     "qlin_ipc_close",
+    "qlin_sharded_fwd",
+    "qlin_sharded_workspace_size",
+    "qlin_nccl_unique_id",
+    "qlin_nccl_comm_init",
+    "qlin_nccl_comm_destroy",
 )
 
 
@@ -110,6 +115,17 @@ def load(path: str | None = None):
         lib.qlin_ipc_open.restype = I
         lib.qlin_ipc_close.argtypes = [P]
         lib.qlin_ipc_close.restype = I
+        lib.qlin_sharded_fwd.argtypes = [I, P, I64, P, P, P, P, I64, P, P, P, I, ctypes.c_float, P, I64, I64, I64,
+                                         I64, P, ctypes.c_size_t, I, P, I, I, P]
+        lib.qlin_sharded_fwd.restype = I
+        lib.qlin_sharded_workspace_size.argtypes = [I, I64, I64, I64, I, I, ctypes.POINTER(ctypes.c_size_t)]
+        lib.qlin_sharded_workspace_size.restype = I
+        lib.qlin_nccl_unique_id.argtypes = [ctypes.c_char_p]
+        lib.qlin_nccl_unique_id.restype = I
+        lib.qlin_nccl_comm_init.argtypes = [PP, I, ctypes.c_char_p, I]
+        lib.qlin_nccl_comm_init.restype = I
+        lib.qlin_nccl_comm_destroy.argtypes = [P]
+        lib.qlin_nccl_comm_destroy.restype = I
         if path is None:
             _lib = lib
             _load_fast(os.path.dirname(p))

@@ -8,6 +8,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>  // types only: the functions are resolved at run time
 
 #include <algorithm>
 #include <cstdint>
@@ -1036,6 +1038,41 @@ static int forward_common(int dtype, const void* x, int64_t ld_x, const void* wr
   return cudaGetLastError() == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
 }
 
+// NCCL, resolved at run time: the library the process already loaded (a
+// host framework's, so that one NCCL serves the whole process), else
+// libnccl.so.2.  Only qlin_sharded_fwd and the bootstrap helpers use it; the
+// rest of the library loads and runs without NCCL.
+struct NcclApi {
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  bool tried = false;
+};
+NcclApi g_nccl;
+
+const NcclApi* nccl_api() {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!g_nccl.tried) {
+    g_nccl.tried = true;
+    void* h = RTLD_DEFAULT;
+    if (!dlsym(h, "ncclAllGather")) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h) {
+      g_nccl.all_gather = reinterpret_cast<decltype(g_nccl.all_gather)>(dlsym(h, "ncclAllGather"));
+      g_nccl.unique_id = reinterpret_cast<decltype(g_nccl.unique_id)>(dlsym(h, "ncclGetUniqueId"));
+      g_nccl.comm_init = reinterpret_cast<decltype(g_nccl.comm_init)>(dlsym(h, "ncclCommInitRank"));
+      g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    }
+  }
+  return (g_nccl.all_gather && g_nccl.unique_id && g_nccl.comm_init && g_nccl.comm_destroy) ? &g_nccl : nullptr;
+}
+
+// Workspace of qlin_sharded_fwd: the gathered column blocks [world][M][4 N_g]
+// (M > 1), then the single-GPU forward's workspace.
+size_t sharded_gather_bytes(int dtype, int64_t M, int64_t N_g, int world) {
+  return M > 1 ? (size_t)round_up((int64_t)world * M * 4 * N_g * elem_size(dtype), 256) : 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1051,11 +1088,12 @@ const char* qlin_status_string(int status) {
     case QLIN_ERR_DEVICE: return "current device is not sm_100 (B200 class)";
     case QLIN_ERR_TIMEOUT: return "a bounded device-side wait ran out";
     case QLIN_ERR_ARG: return "null pointer or invalid option";
+    case QLIN_ERR_COLLECTIVE: return "NCCL not loadable, or an NCCL call failed";
     default: return "unknown status";
   }
 }
 
-int qlin_abi_version(void) { return 102; }
+int qlin_abi_version(void) { return 103; }
 
 int qlin_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, size_t* bytes) {
   if (!bytes) return QLIN_ERR_ARG;
@@ -1302,6 +1340,78 @@ int qlin_gather_columns(int dtype, const void* src, void* dst, int64_t G, int64_
     qlin_gather_kernel<uint16_t><<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(src),
                                                         static_cast<uint16_t*>(dst), G, M, n_shard, ld_dst);
   return cudaGetLastError() == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+}
+
+int qlin_sharded_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int world,
+                                size_t* bytes) {
+  if (!bytes || world < 1) return QLIN_ERR_ARG;
+  size_t local = 0;
+  const int st = qlin_workspace_size(dtype, M, K_g, N_g, rank, &local);
+  if (st != QLIN_OK) return st;
+  *bytes = sharded_gather_bytes(dtype, M, N_g, world) + local;
+  return QLIN_OK;
+}
+
+int qlin_sharded_fwd(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi, const void* wj,
+                     const void* wk, int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b,
+                     int rank, float lora_scale, void* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
+                     void* workspace, size_t workspace_bytes, int flags, void* nccl_comm, int world,
+                     int world_rank, void* stream) {
+  if (world < 1 || world_rank < 0 || world_rank >= world || !nccl_comm) return QLIN_ERR_ARG;
+  if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
+  if (M < 0 || N_g <= 0 || ld_y < (int64_t)world * 4 * N_g) return QLIN_ERR_SHAPE;
+  const int64_t cols = 4 * N_g;  // this rank's output columns
+  const size_t es = elem_size(dtype);
+  // this rank's columns: for one token straight into its place in y (the
+  // all-gather then runs in place), else into its block of the gathered buffer
+  const size_t gather = sharded_gather_bytes(dtype, M, N_g, world);
+  if (M > 1 && (!workspace || workspace_bytes < gather)) return QLIN_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint8_t* blocks = M > 1 ? ws : static_cast<uint8_t*>(y);
+  uint8_t* mine = blocks + (size_t)world_rank * (M > 1 ? M * cols : cols) * es;
+  int st = qlin_forward_ex(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, mine,
+                           M > 1 ? cols : ld_y, M, K_g, N_g, ws ? ws + gather : nullptr,
+                           workspace_bytes > gather ? workspace_bytes - gather : 0, QLIN_ALGO_AUTO, flags, stream);
+  if (st != QLIN_OK || M == 0) return st;
+  const NcclApi* nc = nccl_api();
+  if (!nc) return QLIN_ERR_COLLECTIVE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // in place: rank r's block is already at offset r * count of the receive buffer
+  if (nc->all_gather(mine, blocks, (size_t)(M > 1 ? M * cols : cols) * es, ncclUint8,
+                     static_cast<ncclComm_t>(nccl_comm), s) != ncclSuccess)
+    return QLIN_ERR_COLLECTIVE;
+  if (M == 1) return QLIN_OK;
+  return qlin_gather_columns(dtype, blocks, y, world, M, cols, ld_y, stream);
+}
+
+int qlin_nccl_unique_id(void* id) {
+  if (!id) return QLIN_ERR_ARG;
+  const NcclApi* nc = nccl_api();
+  if (!nc) return QLIN_ERR_COLLECTIVE;
+  ncclUniqueId u;
+  if (nc->unique_id(&u) != ncclSuccess) return QLIN_ERR_COLLECTIVE;
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+  std::memcpy(id, &u, sizeof(u));
+  return QLIN_OK;
+}
+
+int qlin_nccl_comm_init(void** comm, int world, const void* id, int world_rank) {
+  if (!comm || !id || world < 1 || world_rank < 0 || world_rank >= world) return QLIN_ERR_ARG;
+  const NcclApi* nc = nccl_api();
+  if (!nc) return QLIN_ERR_COLLECTIVE;
+  ncclUniqueId u;
+  std::memcpy(&u, id, sizeof(u));
+  ncclComm_t c = nullptr;
+  if (nc->comm_init(&c, world, u, world_rank) != ncclSuccess) return QLIN_ERR_COLLECTIVE;
+  *comm = c;
+  return QLIN_OK;
+}
+
+int qlin_nccl_comm_destroy(void* comm) {
+  if (!comm) return QLIN_ERR_ARG;
+  const NcclApi* nc = nccl_api();
+  if (!nc) return QLIN_ERR_COLLECTIVE;
+  return nc->comm_destroy(static_cast<ncclComm_t>(comm)) == ncclSuccess ? QLIN_OK : QLIN_ERR_COLLECTIVE;
 }
 
 }  // extern "C"

@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol(qb):
 
 
 def test_status_strings(qb):
-    for code in range(0, 9):
+    for code in range(0, 10):
         assert qb._lib.status_string(code)
     assert qb._lib.status_string(1).startswith("invalid shape")
 
@@ -110,3 +110,28 @@ def test_cpython_binding_matches_ctypes_on_refusals(qb):
         assert fast.forward_ex(*c) == lib.qlin_forward_ex(*c)
     with pytest.raises(TypeError):
         fast.forward_ex(1, 2, 3)
+
+
+def test_sharded_nccl_entry_refusals_and_workspace(qb):
+    # qlin_sharded_fwd checks its arguments before any device or NCCL use
+    lib = qb._lib.load()
+    P = None
+    comm = ctypes.c_void_p(1)  # never dereferenced: every call below is refused first
+    args = (1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 32, 2, 4, 4, P, 0, 0)
+    assert lib.qlin_sharded_fwd(*args, P, 2, 0, P) == 8          # no communicator
+    assert lib.qlin_sharded_fwd(*args, comm, 0, 0, P) == 8       # empty world
+    assert lib.qlin_sharded_fwd(*args, comm, 2, 2, P) == 8       # rank outside the world
+    bad_ld = (1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 31, 2, 4, 4, P, 0, 0)
+    assert lib.qlin_sharded_fwd(*bad_ld, comm, 2, 1, P) == 1     # ld_y < world * 4 * N_g
+    assert lib.qlin_sharded_fwd(*args, comm, 2, 1, P) == 4       # M > 1 needs the gather buffer
+    assert lib.qlin_nccl_comm_init(None, 1, b"\0" * 128, 0) == 8
+    assert lib.qlin_nccl_comm_destroy(None) == 8
+    assert qb._lib.status_string(9).startswith("NCCL")
+    n = ctypes.c_size_t(0)
+    assert lib.qlin_sharded_workspace_size(1, 16, 1024, 128, 0, 4, ctypes.byref(n)) == 0
+    one = ctypes.c_size_t(0)
+    assert lib.qlin_workspace_size(1, 16, 1024, 128, 0, ctypes.byref(one)) == 0
+    # the gathered [world, M, 4 N_g] blocks (bf16, 256-byte rounded) ahead of the forward's workspace
+    assert n.value == 4 * 16 * 512 * 2 + one.value
+    assert lib.qlin_sharded_workspace_size(1, 1, 1024, 128, 0, 4, ctypes.byref(n)) == 0
+    assert n.value == qb._lib.workspace_size(__import__("torch").bfloat16, 1, 1024, 128, 0)
