@@ -1055,13 +1055,17 @@ const NcclApi* nccl_api() {
   std::lock_guard<std::mutex> lock(g_mutex);
   if (!g_nccl.tried) {
     g_nccl.tried = true;
-    void* h = RTLD_DEFAULT;
-    if (!dlsym(h, "ncclAllGather")) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-    if (h) {
+    // RTLD_DEFAULT is a null handle: resolve through it when it sees NCCL
+    auto resolve = [](void* h) {
       g_nccl.all_gather = reinterpret_cast<decltype(g_nccl.all_gather)>(dlsym(h, "ncclAllGather"));
       g_nccl.unique_id = reinterpret_cast<decltype(g_nccl.unique_id)>(dlsym(h, "ncclGetUniqueId"));
       g_nccl.comm_init = reinterpret_cast<decltype(g_nccl.comm_init)>(dlsym(h, "ncclCommInitRank"));
       g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+      return g_nccl.all_gather && g_nccl.unique_id && g_nccl.comm_init && g_nccl.comm_destroy;
+    };
+    if (!resolve(RTLD_DEFAULT)) {
+      void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+      if (h) resolve(h);
     }
   }
   return (g_nccl.all_gather && g_nccl.unique_id && g_nccl.comm_init && g_nccl.comm_destroy) ? &g_nccl : nullptr;

@@ -135,3 +135,13 @@ def test_sharded_nccl_entry_refusals_and_workspace(qb):
     assert n.value == 4 * 16 * 512 * 2 + one.value
     assert lib.qlin_sharded_workspace_size(1, 1, 1024, 128, 0, 4, ctypes.byref(n)) == 0
     assert n.value == qb._lib.workspace_size(__import__("torch").bfloat16, 1, 1024, 128, 0)
+
+
+def test_nccl_is_found_without_a_gpu(qb):
+    # the library resolves NCCL at run time (here: the copy torch loaded) and
+    # its bootstrap helper returns a 128-byte unique id, no device needed
+    import torch  # noqa: F401  (loads torch's NCCL into the process)
+    lib = qb._lib.load()
+    uid = ctypes.create_string_buffer(128)
+    assert lib.qlin_nccl_unique_id(uid) == 0
+    assert any(uid.raw)
