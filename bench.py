@@ -19,8 +19,10 @@ graph and replayed once between CUDA events (device time), bracketed by a
 barrier and torch.cuda.synchronize() on both sides; the max over ranks is
 reported.  Consecutive steps rotate through enough copies of the weights
 (and inputs) to exceed the 126 MB L2, so every step streams its weights from
-HBM.  "e2e" times K steps through the public module API with the input copied
-from pinned host memory and the output read back every step.
+HBM.  "e2e" times K calls of the C ABI's host-buffer entry (qlin_forward_host):
+every step copies the input from pinned host memory, runs the layer and
+reads the output back; "e2e_module" does the same through the public module
+API (torch copies around the module call).
 
 With torchrun (N>1) the headline is the 5120 -> 27648 layer column-partitioned
 over the N ranks (out/4 quaternion rows each) at --shard-m tokens (8192 by
@@ -38,6 +40,7 @@ policy (cpu_sample).
 from __future__ import annotations
 
 import argparse
+import ctypes
 import importlib
 import json
 import math
@@ -650,6 +653,52 @@ def time_dense(lay, torch, dev, K, W):
     return s.elapsed_time(e) * 1e3 / K
 
 
+def time_e2e_abi(qb, lay, torch, dev, K, W):
+    """K calls of the C ABI's host-buffer entry (qlin_forward_host, through
+    the package's CPython binding of it): every step copies x from page-locked
+    host memory to the device, runs the layer and copies y back to
+    page-locked host memory, all on the stream; the device weights rotate
+    over copies larger than L2 as in the device timing."""
+    _, ncopy, copies, _, _ = _device_case(qb, lay, torch, dev)
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
+    M, K_g, N_g = lay.M, lay.K_g, lay.N_g
+    rank = 0 if lay.lora_a is None else lay.lora_a.shape[0]
+    lib = qb._lib.load()
+    code = qb._lib.dtype_code(dt)
+    x_host = torch.from_numpy(lay.x).to(dt).pin_memory()
+    y_host = torch.empty(M, 4 * N_g, dtype=dt).pin_memory()
+    n = ctypes.c_size_t(0)
+    qb._lib.check(lib.qlin_host_workspace_size(code, M, K_g, N_g, rank, ctypes.byref(n)), "qlin_host_workspace_size")
+    ws = torch.zeros(max(n.value, 256), dtype=torch.uint8, device=dev)
+    fn = qb._lib._fast.forward_host if qb._lib._fast is not None else lib.qlin_forward_host
+    stream = qb._lib.stream_handle(dev)
+    flags = qb._lib.FLAG_ZEROED_WORKSPACE
+    args = []
+    for c in copies:
+        args.append((code, x_host.data_ptr(), 4 * K_g, *(w.data_ptr() for w in c["w"]), K_g,
+                     c["b"].data_ptr() if c["b"] is not None else None,
+                     c["la"].data_ptr() if c["la"] is not None else None,
+                     c["lb"].data_ptr() if c["lb"] is not None else None, rank, float(lay.lora_scale),
+                     y_host.data_ptr(), 4 * N_g, M, K_g, N_g, ws.data_ptr(), n.value, 0, flags, stream))
+
+    def step(i):
+        st = fn(*args[i % ncopy])
+        if st != 0:
+            qb._lib.check(st, "qlin_forward_host")
+
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(K):
+        step(i)
+    e.record()
+    torch.cuda.synchronize(dev)
+    es = x_host.element_size()
+    return s.elapsed_time(e) * 1e3 / K, M * 4 * K_g * es, M * 4 * N_g * es
+
+
 def time_e2e(qb, lay, torch, dev, K, W):
     """K steps through the public module API with host input and host output."""
     dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[lay.dtype]
@@ -973,8 +1022,15 @@ def main():
     # the same calls on the packed weight cache only (qlin_forward_packed)
     pms, _, _ = time_device(qb, lay, torch, dev, K, W, packed=True)
     result["packed_weights_us_per_call"] = pms * 1e3 / K
-    e2e_us, h2d, d2h = time_e2e(qb, lay, torch, dev, K, W)
-    result["e2e"] = {"value": e2e_us, "unit": "us/call", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    # end to end with host buffers: through the C ABI's host entry (the
+    # reference-facing boundary a non-Python host binds), and through the
+    # Python module API (copies by torch around the module call)
+    e2e_us, h2d, d2h = time_e2e_abi(qb, lay, torch, dev, K, W)
+    result["e2e"] = {"value": e2e_us, "unit": "us/call", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                     "through": "qlin_forward_host (C ABI, pinned host x and y)"}
+    m_us, h2d, d2h = time_e2e(qb, lay, torch, dev, K, W)
+    result["e2e_module"] = {"value": m_us, "unit": "us/call", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                            "through": "LoRAQuaternionLinear / QuaternionLinear forward, torch copies"}
     result["dense_cublas_us"] = time_dense(lay, torch, dev, K, W)
     if rank == 0:
         ref, port = cpu_baselines(lay, K, W, budget_s=args.cpu_budget)

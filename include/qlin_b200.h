@@ -250,6 +250,31 @@ int qlin_forward_allgather(int dtype,
                            void* stream);
 
 /*
+ * qlin_forward_ex with the input and output in host memory (no reference
+ * counterpart: the reference's CPU callers hand over host tensors).  x_host
+ * [M, ld_x] is copied to the device, the layer runs, and y [M, ld_y] is
+ * copied back to y_host, all enqueued on `stream` in that order; y_host
+ * holds the result once the stream has reached that point (synchronise the
+ * stream or an event).  Host buffers should be page-locked (cudaHostAlloc /
+ * cudaHostRegister) for the copies to be asynchronous.  Weights, bias and
+ * LoRA stay device pointers.  workspace (device): at least
+ * qlin_host_workspace_size() bytes -- the staged x and y, then the
+ * workspace of qlin_forward_ex, which QLIN_FLAG_ZEROED_WORKSPACE refers to
+ * (zero-fill the whole buffer once).
+ */
+int qlin_forward_host(int dtype,
+                      const void* x_host, int64_t ld_x,
+                      const void* wr, const void* wi, const void* wj, const void* wk,
+                      int64_t ld_w,
+                      const void* bias,
+                      const void* lora_a, const void* lora_b, int rank, float lora_scale,
+                      void* y_host, int64_t ld_y,
+                      int64_t M, int64_t K_g, int64_t N_g,
+                      void* workspace, size_t workspace_bytes,
+                      int algo, int flags, void* stream);
+int qlin_host_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, size_t* bytes);
+
+/*
  * Column-partitioned layer over NCCL (no reference counterpart: the exchange
  * of a layer whose output quaternions are split over `world` GPUs), for
  * hosts that hold an NCCL communicator but no peer-mapped output buffers.

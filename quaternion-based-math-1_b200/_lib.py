@@ -55,6 +55,8 @@ EXPORTED = (
     "qlin_ipc_free",
     "qlin_ipc_open",
     "qlin_ipc_close",
+    "qlin_forward_host",
+    "qlin_host_workspace_size",
     "qlin_sharded_fwd",
     "qlin_sharded_workspace_size",
     "qlin_nccl_unique_id",
@@ -118,6 +120,10 @@ def load(path: str | None = None):
         lib.qlin_sharded_fwd.argtypes = [I, P, I64, P, P, P, P, I64, P, P, P, I, ctypes.c_float, P, I64, I64, I64,
                                          I64, P, ctypes.c_size_t, I, P, I, I, P]
         lib.qlin_sharded_fwd.restype = I
+        lib.qlin_forward_host.argtypes = fwd + [I, I, P]
+        lib.qlin_forward_host.restype = I
+        lib.qlin_host_workspace_size.argtypes = [I, I64, I64, I64, I, ctypes.POINTER(ctypes.c_size_t)]
+        lib.qlin_host_workspace_size.restype = I
         lib.qlin_sharded_workspace_size.argtypes = [I, I64, I64, I64, I, I, ctypes.POINTER(ctypes.c_size_t)]
         lib.qlin_sharded_workspace_size.restype = I
         lib.qlin_nccl_unique_id.argtypes = [ctypes.c_char_p]

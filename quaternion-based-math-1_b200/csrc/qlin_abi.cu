@@ -1071,6 +1071,45 @@ const NcclApi* nccl_api() {
   return (g_nccl.all_gather && g_nccl.unique_id && g_nccl.comm_init && g_nccl.comm_destroy) ? &g_nccl : nullptr;
 }
 
+// Device staging of qlin_forward_host: x [M][4 K_g] and y [M][4 N_g], each
+// 256-byte aligned, ahead of the forward's own workspace.
+size_t host_staging_bytes(int dtype, int64_t M, int64_t K_g, int64_t N_g) {
+  const int64_t es = (int64_t)elem_size(dtype);
+  return (size_t)(round_up(M * 4 * K_g * es, 256) + round_up(M * 4 * N_g * es, 256));
+}
+
+// Largest transfer qlin_forward_host runs as a kernel (stage-in / stage-out).
+constexpr size_t kHostDirectBytes = 64 * 1024;
+
+// The device address of a page-locked host buffer when qlin_forward_host may
+// move it with a kernel: mapped into the device's address space, at most
+// kHostDirectBytes of rows, rows and leading dimension in whole 16-byte
+// words, 16-byte aligned; else null (a copy-engine transfer).
+void* direct_host_map(const void* p, size_t row_bytes, size_t ld_bytes, int64_t M) {
+  if (row_bytes * (size_t)M > kHostDirectBytes || row_bytes % 16 || ld_bytes % 16 || !aligned(p, 16)) return nullptr;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
+// A small kernel as a programmatic dependent of the previous kernel of the stream.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned blocks, cudaStream_t s, Args... args) {
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Workspace of qlin_sharded_fwd: the gathered column blocks [world][M][4 N_g]
 // (M > 1), then the single-GPU forward's workspace.
 size_t sharded_gather_bytes(int dtype, int64_t M, int64_t N_g, int world) {
@@ -1344,6 +1383,61 @@ int qlin_gather_columns(int dtype, const void* src, void* dst, int64_t G, int64_
     qlin_gather_kernel<uint16_t><<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(src),
                                                         static_cast<uint16_t*>(dst), G, M, n_shard, ld_dst);
   return cudaGetLastError() == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+}
+
+int qlin_host_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, size_t* bytes) {
+  if (!bytes) return QLIN_ERR_ARG;
+  size_t local = 0;
+  const int st = qlin_workspace_size(dtype, M, K_g, N_g, rank, &local);
+  if (st != QLIN_OK) return st;
+  *bytes = host_staging_bytes(dtype, M, K_g, N_g) + local;
+  return QLIN_OK;
+}
+
+int qlin_forward_host(int dtype, const void* x_host, int64_t ld_x, const void* wr, const void* wi, const void* wj,
+                      const void* wk, int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b,
+                      int rank, float lora_scale, void* y_host, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g,
+                      void* workspace, size_t workspace_bytes, int algo, int flags, void* stream) {
+  if (dtype != QLIN_F32 && dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
+  if (M < 0 || K_g <= 0 || N_g <= 0 || ld_x < 4 * K_g || ld_y < 4 * N_g) return QLIN_ERR_SHAPE;
+  if (M == 0) return QLIN_OK;
+  if (!x_host || !y_host) return QLIN_ERR_ARG;
+  const size_t es = elem_size(dtype), staging = host_staging_bytes(dtype, M, K_g, N_g);
+  if (!workspace || workspace_bytes < staging) return QLIN_ERR_WORKSPACE;
+  uint8_t* xd = static_cast<uint8_t*>(workspace);
+  uint8_t* yd = xd + round_up(M * 4 * K_g * (int64_t)es, 256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t xrow = (size_t)(4 * K_g) * es, yrow = (size_t)(4 * N_g) * es;
+  // Decode-sized transfers between page-locked, device-mapped host buffers
+  // and the device run as kernels of the dependent-launch chain; larger or
+  // pageable ones as copy-engine transfers.
+  void* xmap = direct_host_map(x_host, xrow, (size_t)ld_x * es, M);
+  void* ymap = direct_host_map(y_host, yrow, (size_t)ld_y * es, M);
+  cudaError_t e;
+  if (xmap) {
+    const int64_t row = (int64_t)(xrow / 16), n = M * row;
+    e = launch_pdl(qlin_stage_in_kernel, (unsigned)((n + 511) / 512), s, static_cast<const uint4*>(xmap),
+                   (int64_t)(ld_x * es / 16), reinterpret_cast<uint4*>(xd), row, row, M);
+  } else {
+    // one copy when the host rows are contiguous, else a strided one
+    e = ld_x == 4 * K_g
+            ? cudaMemcpyAsync(xd, x_host, xrow * M, cudaMemcpyHostToDevice, s)
+            : cudaMemcpy2DAsync(xd, xrow, x_host, (size_t)ld_x * es, xrow, (size_t)M, cudaMemcpyHostToDevice, s);
+  }
+  if (e != cudaSuccess) return QLIN_ERR_LAUNCH;
+  const int st = qlin_forward_ex(dtype, xd, 4 * K_g, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, yd,
+                                 4 * N_g, M, K_g, N_g, xd + staging, workspace_bytes - staging, algo, flags, stream);
+  if (st != QLIN_OK) return st;
+  if (ymap) {
+    const int64_t row = (int64_t)(yrow / 16), n = M * row;
+    e = launch_pdl(qlin_stage_out_kernel, (unsigned)((n + 511) / 512), s, reinterpret_cast<const uint4*>(yd), row,
+                   static_cast<uint4*>(ymap), (int64_t)(ld_y * es / 16), row, M);
+  } else {
+    e = ld_y == 4 * N_g
+            ? cudaMemcpyAsync(y_host, yd, yrow * M, cudaMemcpyDeviceToHost, s)
+            : cudaMemcpy2DAsync(y_host, (size_t)ld_y * es, yd, yrow, yrow, (size_t)M, cudaMemcpyDeviceToHost, s);
+  }
+  return e == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
 }
 
 int qlin_sharded_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, int world,

@@ -145,3 +145,20 @@ def test_nccl_is_found_without_a_gpu(qb):
     uid = ctypes.create_string_buffer(128)
     assert lib.qlin_nccl_unique_id(uid) == 0
     assert any(uid.raw)
+
+
+def test_host_entry_refusals_and_workspace(qb):
+    # qlin_forward_host checks shapes, host pointers and the staging size before any device use
+    lib = qb._lib.load()
+    P = None
+    base = (1, 1, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4)
+    assert lib.qlin_forward_host(1, 1, 10, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 0, P) == 1
+    assert lib.qlin_forward_host(1, P, 16, 1, 1, 1, 1, 4, P, P, P, 0, 0.0, 1, 16, 2, 4, 4, P, 0, 0, 0, P) == 8
+    assert lib.qlin_forward_host(*base, P, 0, 0, 0, P) == 4
+    assert lib.qlin_forward_host(1, P, 16, P, P, P, P, 4, P, P, P, 0, 0.0, P, 16, 0, 4, 4, P, 0, 0, 0, P) == 0
+    n = ctypes.c_size_t(0)
+    one = ctypes.c_size_t(0)
+    assert lib.qlin_host_workspace_size(1, 3, 256, 128, 0, ctypes.byref(n)) == 0
+    assert lib.qlin_workspace_size(1, 3, 256, 128, 0, ctypes.byref(one)) == 0
+    # staged x [3, 1024] and y [3, 512] bf16, each rounded to 256 bytes, then the forward's workspace
+    assert n.value == 6144 + 3072 + one.value
