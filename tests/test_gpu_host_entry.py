@@ -69,3 +69,56 @@ def test_host_entry_matches_the_device_entry(qb, oracle, workloads, cuda, M, fin
     # too small a workspace: refused before any copy
     assert lib.qlin_forward_host(*args, _ptr(ws), 256, 0, FLAG_ZEROED, stream) == ERR_WORKSPACE
     assert qb.device_error(cuda) == 0
+
+
+
+def test_host_entry_reads_fresh_inputs_and_captures_in_a_graph(qb, workloads, cuda):
+    # repeated calls read each call's host x and write that call's y; the
+    # call's launches (the stage kernels reading and writing host memory
+    # through its device mapping) can be captured in the caller's CUDA graph
+    lib = qb._lib.load()
+    M, fin, fout, rank = 1, 1024, 1024, 16
+    lay = workloads.make_layer("bf16", M, fin, fout, 77, bias="normal", lora_rank=rank, lora_std=0.02)
+    d = to_device(lay, cuda)
+    K_g, N_g = fin // 4, fout // 4
+    code = qb._lib.dtype_code(torch.bfloat16)
+    x_host = torch.empty(M, fin, dtype=torch.bfloat16).pin_memory()
+    y_host = torch.empty(M, fout, dtype=torch.bfloat16).pin_memory()
+    n = ctypes.c_size_t(0)
+    assert lib.qlin_host_workspace_size(code, M, K_g, N_g, rank, ctypes.byref(n)) == 0
+    ws = torch.zeros(n.value, dtype=torch.uint8, device=cuda)
+
+    def call(stream):
+        return lib.qlin_forward_host(code, x_host.data_ptr(), fin, *(_ptr(t) for t in d["w"]), K_g, _ptr(d["bias"]),
+                                     _ptr(d["lora_a"]), _ptr(d["lora_b"]), rank, float(d["scale"]), y_host.data_ptr(),
+                                     fout, M, K_g, N_g, _ptr(ws), n.value, 0, FLAG_ZEROED, stream)
+
+    def device_result():
+        want = torch.empty(M, fout, dtype=torch.bfloat16, device=cuda)
+        nd = qb._lib.workspace_size(torch.bfloat16, M, K_g, N_g, rank)
+        wsd = torch.zeros(max(nd, 256), dtype=torch.uint8, device=cuda)
+        assert lib.qlin_forward_ex(code, _ptr(x_host.to(cuda)), fin, *(_ptr(t) for t in d["w"]), K_g,
+                                   _ptr(d["bias"]), _ptr(d["lora_a"]), _ptr(d["lora_b"]), rank, float(d["scale"]),
+                                   _ptr(want), fout, M, K_g, N_g, _ptr(wsd), nd, 0, FLAG_ZEROED,
+                                   qb._lib.stream_handle(cuda)) == 0
+        torch.cuda.synchronize()
+        return want.cpu()
+
+    g = torch.Generator().manual_seed(5)
+    for _ in range(4):
+        x_host.copy_(torch.randn(M, fin, generator=g).to(torch.bfloat16))
+        assert call(qb._lib.stream_handle(cuda)) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(y_host, device_result())
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        assert call(s.cuda_stream) == 0
+    for _ in range(2):
+        x_host.copy_(torch.randn(M, fin, generator=g).to(torch.bfloat16))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(y_host, device_result())
+    del graph
+    assert qb.device_error(cuda) == 0
