@@ -703,6 +703,12 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
     cuuint64_t strides[2] = {(cuuint64_t)(K_g * 2), (cuuint64_t)(M * K_g * 2)};
     cuuint32_t box[3] = {kTcChunk, (cuuint32_t)n_tok, 1};
     if (encode(&maps[4], dt, 3, xp, dims, strides, box) != CUDA_SUCCESS) return QLIN_ERR_ALIGN;
+  } else {
+    // raw x rows of a stacked tile: 32 elements (64 bytes, 64-byte swizzle) x n_tok tokens
+    cuuint64_t dims[2] = {(cuuint64_t)(4 * K_g), (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld_x * 2)};
+    cuuint32_t box[2] = {32, (cuuint32_t)n_tok};
+    if (encode(&maps[4], dt, 2, const_cast<T*>(x), dims, strides, box) != CUDA_SUCCESS) return QLIN_ERR_ALIGN;
   }
   int lora_chunks = 0;
   if (rank > 0) {

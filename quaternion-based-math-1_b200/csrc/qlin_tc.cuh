@@ -102,17 +102,19 @@ struct TcCfg {
   // Activation operand per weight component and stage: stacked [4*N_TOK rows]
   // or one plane [N_TOK rows], 64 bytes per row either way.
   static constexpr int kXTileBytes = (STACK ? 4 : 1) * N_TOK * kTcChunk * 2;
-  // In-kernel LoRA down projection: the chunk's raw x rows (4 sub-tiles of
-  // 32 elements x N_TOK rows) and the matching 32-element columns of lora_a
-  // (4 sub-tiles x kTcLoraInRank rows).
-  static constexpr int kRawXBytes = LORA == kLoraTc ? 4 * N_TOK * 64 : 0;
+  // Stacked tiles: the chunk's raw x rows (4 sub-tiles of 32 elements x N_TOK
+  // rows, 64-byte swizzle), brought by TMA and read by the builder warps
+  // (and, in the tensor-core LoRA mode, the down projection's A operand);
+  // there also the matching 32-element columns of lora_a (4 sub-tiles x
+  // kTcLoraInRank rows).
+  static constexpr int kRawXBytes = STACK ? 4 * N_TOK * 64 : 0;
   static constexpr int kLoraABytes = LORA == kLoraTc ? 4 * kTcLoraInRank * 64 : 0;
   static constexpr int kStageBytes = 4 * kTcWTileBytes + 4 * kXTileBytes + kRawXBytes + kLoraABytes;
   // CUDA-core LoRA: the split's lora_a slice [32 rows][<= 512 elements],
   // loaded once, ahead of the weights, as row pieces of kTcLoraSliceBox
   static constexpr int kSliceBytes = LORA == kLoraSimt ? kTcLoraInRank * kTcLoraSliceMax * 2 : 0;
   static constexpr int kRecvBytes = CLUSTER ? kTcClusterSlots * kTcBlockO * 16 : 0;
-  static constexpr int kFit = ((CLUSTER ? 212 : 200) * 1024 - kSliceBytes - kRecvBytes) / kStageBytes;
+  static constexpr int kFit = (220 * 1024 - kSliceBytes - kRecvBytes) / kStageBytes;
   static constexpr int kStages = kFit > 6 ? 6 : (kFit < 2 ? 2 : kFit);
   static constexpr int kSliceOffset = kStages * kStageBytes;
   static constexpr int kRecvOffset = kSliceOffset + kSliceBytes;
@@ -175,6 +177,9 @@ __device__ __forceinline__ void lora_bar_sync() {
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+__device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "r"(addr) : "memory");
+}
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
@@ -219,7 +224,8 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   uint64_t* t_full = acc_full + 1;  // LoRA: down projection complete (tensor cores) / lora_a slice loaded (CUDA cores)
   uint64_t* red_full = t_full + 1;  // fused K-split reduction: all partials are in shared memory
   uint64_t* gather = red_full + 1;  // cluster K split (leader): every peer's partial has arrived
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gather + 1);
+  uint64_t* xfull = gather + 1;     // stacked tiles: the stage's raw x rows have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + S);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued_count = const_cast<int*>(abort_flag) + 1;
   int* consumed_count = issued_count + 1;
@@ -262,6 +268,14 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   };
   const CUtensorMap* wmap[4] = {&map_wr, &map_wi, &map_wj, &map_wk};
   const int pre = total < S ? total : S;
+  // Stacked tiles: the raw x rows of main-loop stage it (after the
+  // dependency wait: x may come from the previous kernel of the stream).
+  auto issue_raw_x = [&](int it) {
+    const int s = it % S, k = (c_begin + it) * kTcChunk;
+    mbar_arrive_expect_tx(&xfull[s], (uint32_t)Cfg::kRawXBytes);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tma_load_2d(raw_tile(s, j), &map_x, &xfull[s], 4 * k + 32 * j, t0);
+  };
   // Weight (and LoRA B) tiles of the first stages; in the CUDA-core LoRA mode
   // preceded by this split's lora_a slice, so that it arrives first.
   auto issue_pre_weights = [&]() {
@@ -310,6 +324,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], kBuilt ? 2 : 1);  // producer (+ builders)
       mbar_init(&empty[s], 1);
+      mbar_init(&xfull[s], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(t_full, 1);
@@ -330,7 +345,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     tma_prefetch_desc(&map_wi);
     tma_prefetch_desc(&map_wj);
     tma_prefetch_desc(&map_wk);
-    if (!kBuilt) tma_prefetch_desc(&map_x);
+    tma_prefetch_desc(&map_x);
     if (LORA != kLoraPrologue) tma_prefetch_desc(&map_la);
     // With static weights the caller guarantees that no earlier work on the
     // stream writes the weights, bias or LoRA A/B, so their first tiles are
@@ -357,6 +372,8 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   if (threadIdx.x == 0) {
     // ---------------- TMA producer ----------------
     if (!early) issue_pre_weights();
+    if (kBuilt)
+      for (int it = 0; it < pre && it < my_main; ++it) issue_raw_x(it);
     if (prm.after_prologue && (!kBuilt || my_lora > 0)) pdl_wait_prior();  // x planes / LoRA t
     for (int it = 0; it < pre; ++it) {
       if (it < my_main) {
@@ -379,6 +396,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
       if (*abort_flag) break;
       if (it < my_main) {
         const int k = (c_begin + it) * kTcChunk;
+        if (kBuilt) issue_raw_x(it);
         mbar_arrive_expect_tx(&full[s], 4 * kTcWTileBytes + (kBuilt ? 0 : 4 * Cfg::kXTileBytes) +
                                             Cfg::kLoraABytes);
 #pragma unroll
@@ -462,7 +480,6 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     // builder runs every iteration (and meets every named barrier) even after
     // an abort, so no builder can be left waiting.
     const int bt = threadIdx.x - 64;
-    const T* __restrict__ x = reinterpret_cast<const T*>(prm.x);
     bool t_seen = false;
     // With the CUDA-core LoRA the LoRA stages belong to warps 4-5.
     const int b_total = LORA == kLoraSimt ? my_main : total;
@@ -470,59 +487,39 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
       const int s = it % S, n = it / S;
       if (it >= S && !*abort_flag && !mbar_wait(&empty[s], (n - 1) & 1)) *abort_flag = 1;
       if (it < my_main && !*abort_flag) {
-        const int g0 = (c_begin + it) * kTcChunk;
-        // N_TOK*4 items of 64 bytes per stage, 64 builders: kItems each, in
-        // batches of up to 4 whose loads are all issued before any is used
-        // (one L2 round trip per batch, not per item).
+        // The stage's raw x rows arrive by TMA (64-byte swizzle: 16-byte
+        // chunk c of row r at chunk c ^ ((r >> 1) & 3)); N_TOK*4 items of 64
+        // bytes, kItems per builder.  (Loading x here from global memory put
+        // one L2 round trip per stage on the builders' path: measured, it
+        // held the decode kernel at one stage per microsecond per CTA.)
+        if (!mbar_wait(&xfull[s], n & 1)) *abort_flag = 1;
         constexpr int kItems = N_TOK * 4 / 64;
-        constexpr int kBatch = kItems < 4 ? kItems : 4;
-#pragma unroll 1
-        for (int b0 = 0; b0 < kItems; b0 += kBatch) {
-          uint4 ld[kBatch][4];
 #pragma unroll
-          for (int k = 0; k < kBatch; ++k) {
-            const int item = bt + 64 * (b0 + k);
-            const int m = t0 + (item >> 2), gbase = g0 + 8 * (item & 3);
-            const bool live = m < prm.M && gbase < prm.K_g;
-            const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(live ? m : 0) * prm.ld_x + 4 * (live ? gbase : 0));
+        for (int k = 0; k < kItems; ++k) {
+          const int item = bt + 64 * k;
+          const int tok = item >> 2, gb = item & 3;
+          const uint32_t rbase = smem_u32(raw_tile(s, gb)) + tok * 64;
+          uint32_t w[16];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) ld[k][c] = live ? ld_cg_v4(src + c) : make_uint4(0u, 0u, 0u, 0u);
-          }
+          for (int c = 0; c < 4; ++c)
+            ld_shared_v4(rbase + ((c ^ ((tok >> 1) & 3)) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+          // plane q of the 8 quaternions: word j = (X_q[2j], X_q[2j+1])
+          uint32_t pl[4][4];
 #pragma unroll
-          for (int k = 0; k < kBatch; ++k) {
-            const int item = bt + 64 * (b0 + k);
-            const int tok = item >> 2, gb = item & 3;
-            uint32_t w[16];
+          for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              w[4 * c + 0] = ld[k][c].x; w[4 * c + 1] = ld[k][c].y; w[4 * c + 2] = ld[k][c].z; w[4 * c + 3] = ld[k][c].w;
-            }
-            // plane q of the 8 quaternions: word j = (X_q[2j], X_q[2j+1])
-            uint32_t pl[4][4];
+            for (int j = 0; j < 4; ++j)
+              pl[q][j] = __byte_perm(w[4 * j + (q >> 1)], w[4 * j + 2 + (q >> 1)], (q & 1) ? 0x7632 : 0x5410);
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
+          for (int p = 0; p < 4; ++p) {
+            const uint32_t base = smem_u32(x_tile(s, p));
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                pl[q][j] = __byte_perm(w[4 * j + (q >> 1)], w[4 * j + 2 + (q >> 1)], (q & 1) ? 0x7632 : 0x5410);
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-              const uint32_t base = smem_u32(x_tile(s, p));
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int a = p ^ q;
-                const uint32_t sg = quat_neg(a, p) ? 0x80008000u : 0u;
-                const int row = a * N_TOK + tok;
-                const uint32_t addr = base + row * 64 + ((gb ^ ((row >> 1) & 3)) << 4);
-                st_shared_v4(addr, pl[q][0] ^ sg, pl[q][1] ^ sg, pl[q][2] ^ sg, pl[q][3] ^ sg);
-              }
-            }
-            if (LORA == kLoraTc) {
-              // the same 64 bytes unchanged: row tok of raw sub-tile gb
-              const uint32_t rbase = smem_u32(raw_tile(s, gb)) + tok * 64;
-#pragma unroll
-              for (int c = 0; c < 4; ++c)
-                st_shared_v4(rbase + ((c ^ ((tok >> 1) & 3)) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2],
-                             w[4 * c + 3]);
+            for (int q = 0; q < 4; ++q) {
+              const int a = p ^ q;
+              const uint32_t sg = quat_neg(a, p) ? 0x80008000u : 0u;
+              const int row = a * N_TOK + tok;
+              const uint32_t addr = base + row * 64 + ((gb ^ ((row >> 1) & 3)) << 4);
+              st_shared_v4(addr, pl[q][0] ^ sg, pl[q][1] ^ sg, pl[q][2] ^ sg, pl[q][3] ^ sg);
             }
           }
         }
