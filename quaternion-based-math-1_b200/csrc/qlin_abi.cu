@@ -381,12 +381,12 @@ bool cluster_fits(DeviceInfo* dev, int split, int64_t tiles) {
 // kTcClusterTokens tokens (tiles of 16), the K split split_for chose (at most
 // 8 for one or two tokens: with static weights and no LoRA the 16 plain
 // splits, prefetching their weights, measured faster), when all clusters of
-// the grid fit at once; else, for at most 8 tokens, 8 CTAs per cluster when
-// that fits (and keeps the CUDA-core LoRA mode's slice of at most 4 chunks per
-// split).  Same-box measurements, 4096 layer with bias and LoRA r=32: 3, 4, 8
-// tokens 8.7, 9.8, 9.3 us/call in 8-CTA clusters against 10.3, 11.7, 10.0
-// through the workspace; at 16 tokens (16-CTA clusters did not fit) 10.6 in
-// 8-CTA clusters, whose 64 CTAs stream the weights slower, against 10.2.
+// the grid fit at once; else 8 CTAs per cluster when that fits (and keeps
+// the CUDA-core LoRA mode's slice of at most 4 chunks per split).  Same-box
+// measurements, 4096 layer with bias and LoRA r=32 (x rows by TMA): 4, 8, 16
+// tokens 9.95, 9.32, 10.46 us/call in 8-CTA clusters (one launch) against
+// 11.75, 10.44, 10.56 through the workspace (16-CTA clusters do not all fit
+// at once on this part).
 template <typename T, int LORA>
 int cluster_split(DeviceInfo* dev, int64_t M, int64_t K_g, int split, int64_t tiles) {
   if (M > kTcClusterTokens || split < 2 || (M <= 2 && split > 8)) return 0;
@@ -394,7 +394,7 @@ int cluster_split(DeviceInfo* dev, int64_t M, int64_t K_g, int split, int64_t ti
   auto slots_ok = [&](int c) { return (c - 1) * ((M + c - 1) / c) <= kTcClusterSlots; };
   if (slots_ok(split) && cluster_fits<T, LORA>(dev, split, tiles)) return split;
   const int64_t chunks = (K_g + kTcChunk - 1) / kTcChunk;
-  if (split > 8 && M <= 8 && slots_ok(8) && (LORA != kLoraSimt || (chunks + 7) / 8 <= 4) &&
+  if (split > 8 && M <= 16 && slots_ok(8) && (LORA != kLoraSimt || (chunks + 7) / 8 <= 4) &&
       cluster_fits<T, LORA>(dev, 8, tiles))
     return 8;
   return 0;
