@@ -113,14 +113,18 @@ struct TcCfg {
   // CUDA-core LoRA: the split's lora_a slice [32 rows][<= 512 elements],
   // loaded once, ahead of the weights, as row pieces of kTcLoraSliceBox
   static constexpr int kSliceBytes = LORA == kLoraSimt ? kTcLoraInRank * kTcLoraSliceMax * 2 : 0;
+  // Cluster K split: the receive buffer of the reduce-scatter aliases the
+  // start of the stage ring (used only once every CTA of the cluster is past
+  // its main loop), so it costs no stage.
   static constexpr int kRecvBytes = CLUSTER ? kTcClusterSlots * kTcBlockO * 16 : 0;
-  static constexpr int kFit = (220 * 1024 - kSliceBytes - kRecvBytes) / kStageBytes;
+  static constexpr int kFit = (220 * 1024 - kSliceBytes) / kStageBytes;
   static constexpr int kStages = kFit > 6 ? 6 : (kFit < 2 ? 2 : kFit);
   static constexpr int kSliceOffset = kStages * kStageBytes;
-  static constexpr int kRecvOffset = kSliceOffset + kSliceBytes;
+  static constexpr int kRecvOffset = 0;
+  static_assert(kRecvBytes <= kStages * kStageBytes, "receive buffer inside the stage ring");
   // accumulators: 4*N_TOK columns of Y (+ kTcLoraInRank columns of t)
   static constexpr int kTmemCols = tmem_cols_for(4 * N_TOK + (LORA == kLoraTc ? kTcLoraInRank : 0));
-  static constexpr int kBarOffset = kRecvOffset + kRecvBytes;
+  static constexpr int kBarOffset = kSliceOffset + kSliceBytes;
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
   static_assert(N_TOK == 16 || N_TOK == 32 || N_TOK == 64 || N_TOK == 128, "UMMA N");
   static_assert(!STACK || N_TOK <= 64, "stacked operand has 4*N_TOK <= 256 rows");
@@ -177,6 +181,10 @@ __device__ __forceinline__ void lora_bar_sync() {
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Arrive (default semantics) on an mbarrier of another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 __device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "r"(addr) : "memory");
 }
@@ -225,7 +233,8 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   uint64_t* red_full = t_full + 1;  // fused K-split reduction: all partials are in shared memory
   uint64_t* gather = red_full + 1;  // cluster K split (leader): every peer's partial has arrived
   uint64_t* xfull = gather + 1;     // stacked tiles: the stage's raw x rows have landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + S);
+  uint64_t* peers_free = xfull + S; // cluster K split: every other CTA is past its main loop
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(peers_free + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued_count = const_cast<int*>(abort_flag) + 1;
   int* consumed_count = issued_count + 1;
@@ -330,6 +339,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     mbar_init(t_full, 1);
     mbar_init(red_full, 1);
     mbar_init(gather, 1);
+    mbar_init(peers_free, CLUSTER && prm.split_k > 1 ? prm.split_k - 1 : 1);
     // every owner arms its receive barrier before any peer can send (the
     // cluster barrier below orders this before every peer's epilogue)
     if (CLUSTER) {
@@ -695,6 +705,14 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
 #pragma unroll
       for (int a = 0; a < 4; ++a) tmem_ld16(lane_addr + a * N_TOK, v[a]);
       tmem_ld_wait();
+      // The receive buffers alias the stage rings: tell every other CTA that
+      // this one is past its main loop (its last UMMA has read its stages),
+      // and send only once all of them are.
+      if (threadIdx.x == 0)
+        for (int q = 0; q < C; ++q)
+          if (q != ks) mbar_arrive_remote(map_peer_smem(smem_u32(peers_free), (uint32_t)q));
+      const bool peers_ok = mbar_wait(peers_free, 0);
+      if (!peers_ok) *abort_flag = 1;
       const uint32_t recv_local = smem_u32(smem + Cfg::kRecvOffset);
       const uint32_t gather_local = smem_u32(gather);
 #pragma unroll
