@@ -1019,9 +1019,13 @@ def main():
     # streams its weights while the previous call's kernels finish.
     sms, _, _ = time_device(qb, lay, torch, dev, K, W, flags=qb._lib.FLAG_STATIC_WEIGHTS)
     result["static_weights_us_per_call"] = sms * 1e3 / K
-    # the same calls on the packed weight cache only (qlin_forward_packed)
-    pms, _, _ = time_device(qb, lay, torch, dev, K, W, packed=True)
-    result["packed_weights_us_per_call"] = pms * 1e3 / K
+    # the same calls on the packed weight cache only (qlin_forward_packed;
+    # null where the layer's kernel needs the planar weights)
+    try:
+        pms, _, _ = time_device(qb, lay, torch, dev, K, W, packed=True)
+        result["packed_weights_us_per_call"] = pms * 1e3 / K
+    except RuntimeError:
+        result["packed_weights_us_per_call"] = None
     # end to end with host buffers: through the C ABI's host entry (the
     # reference-facing boundary a non-Python host binds), and through the
     # Python module API (copies by torch around the module call)
