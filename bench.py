@@ -549,12 +549,32 @@ def time_sharded(qb, wl, torch, dev, dist, world, rank, W, cases):
             if st != 0:
                 qb._lib.check(st, "qlin_forward_allgather")
 
+        # and with one multicast store per output piece (NVLink multicast
+        # through NVSwitch), where every rank has it
+        ok = torch.tensor([int(qb.MulticastOutputs.available(dev))], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        mco = qb.MulticastOutputs(M, 4 * n * world, torch.bfloat16, dev) if ok.item() else None
+
+        def call_mc(i):
+            w = shards[i % ncopy]
+            st = lib.qlin_forward_allgather_mc(code, x.data_ptr(), 4 * K_g, *(a.data_ptr() for a in w), K_g, None,
+                                               None, None, 0, 0.0, M, K_g, n, wsb.data_ptr(), nws,
+                                               qb._lib.FLAG_ZEROED_WORKSPACE, world, rank, mco.out.data_ptr(),
+                                               mco.mc, 4 * n * world, 4 * n * rank, mco._flags,
+                                               mco.epoch.data_ptr(), stream_of(dev))
+            if st != 0:
+                qb._lib.check(st, "qlin_forward_allgather_mc")
+
         us, mode = _time_ranks(torch, dev, dist, call, steps, W)
         us_f, mode_f = _time_ranks(torch, dev, dist, call_fused, steps, W)
         same = bool(torch.equal(po.out, y_full if M > 1 else flat.view(M, -1)))
+        us_mc = same_mc = None
+        if mco is not None:
+            us_mc, _ = _time_ranks(torch, dev, dist, call_mc, steps, W)
+            same_mc = bool(torch.equal(mco.out, po.out))
         nbytes = 2 * (4 * n * K_g + M * 4 * K_g + M * 4 * n)
         flops = 2.0 * M * 4 * K_g * 4 * n
-        best = min(us, us_f)
+        best = min(v for v in (us, us_f, us_mc) if v is not None)
         if M <= 16:
             a = nbytes / (best * 1e-6) / 1e9
             roof = {"bound": "hbm", "achieved_per_gpu": a, "unit": "GB/s", "peak": peaks_ref["hbm_gbs"],
@@ -565,13 +585,17 @@ def time_sharded(qb, wl, torch, dev, dist, world, rank, W, cases):
                     "frac_per_gpu": a / peaks_ref["bf16_tflops"], "basis": "shard FLOP per GPU"}
         egress = (world - 1) * M * 4 * n * 2  # bytes each rank stores to its peers
         t_nvl = egress / 770e9 * 1e6          # at the measured 770 GB/s peer copy, per direction
+        t_nvl_mc = M * 4 * n * 2 / 770e9 * 1e6  # multicast: each rank's columns cross its links once
         t_cmp = (nbytes / (peaks_ref["hbm_gbs"] * 1e9) if M <= 16 else flops / (peaks_ref["bf16_tflops"] * 1e12)) * 1e6
         launches = qb._lib.plan(torch.bfloat16, M, K_g, n, 0, flags=qb._lib.FLAG_ZEROED_WORKSPACE)["launches"]
         out[M] = {"us_nccl": us, "us_fused": us_f, "steps": steps, "timing": [mode, mode_f], "shard_rows": n,
                   "fused_equals_nccl": same, "roofline": roof,
                   "fused_target_us": max(t_nvl, t_cmp), "fused_frac_of_target": max(t_nvl, t_cmp) / us_f,
                   "nvlink_us": t_nvl, "launches_fused": launches + 2}
-        del shards, x, y_loc, flat, y_full, wsb
+        if us_mc is not None:
+            out[M].update({"us_fused_mc": us_mc, "mc_equals_fused": same_mc,
+                           "mc_target_us": max(t_nvl_mc, t_cmp), "mc_frac_of_target": max(t_nvl_mc, t_cmp) / us_mc})
+        del shards, x, y_loc, flat, y_full, wsb, mco
         torch.cuda.empty_cache()
     return out
 
@@ -1079,13 +1103,19 @@ def main_partitioned(qb, wl, torch, dev, dist, world, rank, K, W, M, metric, pea
         head = time_sharded(qb, wl, torch, dev, dist, world, rank, W, [(M, K)])[M]
     clocks = clk.summary()
     fused = M >= 64
-    us = head["us_fused"] if fused else head["us_nccl"]
+    mc = fused and head.get("us_fused_mc") is not None
+    us = (head["us_fused_mc"] if mc else head["us_fused"]) if fused else head["us_nccl"]
     lay = wl.sharded_27648(M)
     n = head["shard_rows"]
     flops = 2.0 * M * 4 * lay.K_g * 4 * n
     nbytes = 2 * (4 * n * lay.K_g + M * 4 * lay.K_g + M * 4 * n)
     roof = _roofline("tensor" if M > 16 else "hbm", nbytes, flops, us, peaks, peak_src)
     roof["basis"] = "one rank's shard FLOP (or bytes) / call time incl. the output all-gather"
+    if fused:
+        # the fused call's target: the slower of the shard's compute and its NVLink egress
+        target = head["mc_target_us"] if mc else head["fused_target_us"]
+        roof["target_us"] = target
+        roof["frac_of_target"] = target / us
     # the same layer unpartitioned on this GPU (the N = 1 point of the sweep)
     one_ms, _, _ = time_device(qb, lay, torch, dev, K, W, dist)
     single_us = one_ms * 1e3 / K
@@ -1103,7 +1133,8 @@ def main_partitioned(qb, wl, torch, dev, dist, world, rank, K, W, M, metric, pea
         "config": {"workload": f"qlinear_5120x27648_bf16_m{M}_column_partitioned", "M": M,
                    "in_features": 5120, "out_features": 27648, "shard_rows_per_gpu": n,
                    "parallelism": f"column{world} (out/4 quaternion rows) + "
-                                  + ("fused NVLink all-gather" if fused else "NCCL all-gather"),
+                                  + (("fused NVLink multicast all-gather" if mc else "fused NVLink all-gather")
+                                     if fused else "NCCL all-gather"),
                    "inputs": "seeded synthetic N(0,1) activations, N(0,1/in) weights (variance)",
                    "l2": "inputs larger than L2: rotating weight shard copies"},
         "roofline": roof,

@@ -250,6 +250,29 @@ int qlin_forward_allgather(int dtype,
                            void* stream);
 
 /*
+ * qlin_forward_allgather with the full output bound to an NVLink multicast
+ * object (e.g. a symmetric-memory buffer): `out` is this rank's full output
+ * [M, ld_out] and out_mc the multicast address of the same buffer on every
+ * rank.  Each output piece of this rank's columns is stored once through
+ * out_mc (multimem.st): NVSwitch writes it into every rank's output, this
+ * rank's included, so each rank sends its columns over NVLink once instead
+ * of once per peer.  The entry and exit flag barriers are those of
+ * qlin_forward_allgather (flag_arrays[2 * world], epoch_word[2]).
+ */
+int qlin_forward_allgather_mc(int dtype,
+                              const void* x, int64_t ld_x,
+                              const void* wr, const void* wi, const void* wj, const void* wk,
+                              int64_t ld_w,
+                              const void* bias,
+                              const void* lora_a, const void* lora_b, int rank, float lora_scale,
+                              int64_t M, int64_t K_g, int64_t N_g,
+                              void* workspace, size_t workspace_bytes, int flags,
+                              int world, int world_rank,
+                              void* out, void* out_mc, int64_t ld_out, int64_t col_offset,
+                              unsigned* const* flag_arrays, unsigned* epoch_word,
+                              void* stream);
+
+/*
  * qlin_forward_ex with the input and output in host memory (no reference
  * counterpart: the reference's CPU callers hand over host tensors).  x_host
  * [M, ld_x] is copied to the device, the layer runs, and y [M, ld_y] is

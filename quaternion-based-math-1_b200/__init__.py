@@ -34,7 +34,7 @@ from .packing import (
 )
 from .planar import planar_coefficient_tensor, quaternion_linear_naive, quaternion_linear_planar
 from .reparam import FactorizedQuaternionLinear, UnitQuaternionLinear, normalize_quaternion, parameter_count
-from .sharded import ColumnParallelQuaternionLinear, PeerOutputs, gather_columns, shard_bounds
+from .sharded import ColumnParallelQuaternionLinear, MulticastOutputs, PeerOutputs, gather_columns, shard_bounds
 
 __all__ = [
     "QuaternionLinear",
@@ -65,6 +65,7 @@ __all__ = [
     "ConversionRecord",
     "ColumnParallelQuaternionLinear",
     "PeerOutputs",
+    "MulticastOutputs",
     "gather_columns",
     "shard_bounds",
     "device_error",

@@ -51,6 +51,7 @@ EXPORTED = (
     "qlin_forward_noalloc",
     "qlin_forward_packed",
     "qlin_forward_allgather",
+    "qlin_forward_allgather_mc",
     "qlin_ipc_alloc",
     "qlin_ipc_free",
     "qlin_ipc_open",
@@ -109,6 +110,10 @@ def load(path: str | None = None):
             [I, P, I64, P, P, P, P, I64, P, P, P, I, ctypes.c_float, I64, I64, I64, P, ctypes.c_size_t, I,
              I, I, PP, I64, I64, PP, P, P])
         lib.qlin_forward_allgather.restype = I
+        lib.qlin_forward_allgather_mc.argtypes = (
+            [I, P, I64, P, P, P, P, I64, P, P, P, I, ctypes.c_float, I64, I64, I64, P, ctypes.c_size_t, I,
+             I, I, P, P, I64, I64, PP, P, P])
+        lib.qlin_forward_allgather_mc.restype = I
         lib.qlin_ipc_alloc.argtypes = [ctypes.c_size_t, PP, ctypes.c_char_p]
         lib.qlin_ipc_alloc.restype = I
         lib.qlin_ipc_free.argtypes = [P]

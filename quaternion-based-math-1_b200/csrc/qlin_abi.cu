@@ -405,7 +405,7 @@ int launch_tc_impl(DeviceInfo* dev, const CUtensorMap* maps, const TcParams& bas
                    int64_t K_g, int64_t N_g, float4* partials, cudaStream_t stream) {
   using Cfg = TcCfg<N_TOK, kStackFor<N_TOK>, LORA>;
   // outputs also stored to peers only in the column-partitioned path's build
-  const bool peers = base_prm.peers.n > 0;
+  const bool peers = has_peers(base_prm.peers);
   {
     const int64_t o_blocks = (N_g + kTcBlockO - 1) / kTcBlockO, t_blocks = (M + N_TOK - 1) / N_TOK;
     const int split = split_for(M, K_g, N_g, base_prm.rank, dev->num_sms, base_prm.static_weights != 0);
@@ -498,7 +498,7 @@ bool pair_eligible(int64_t M, int64_t N_g, int rank, const void* y, int64_t ld_y
     return false;
   for (int p = 0; p < peers.n; ++p)
     if (!aligned(peers.y[p], 16)) return false;
-  return true;
+  return !peers.mc || aligned(peers.mc, 16);
 }
 
 template <typename T, bool PEERS, int NTOK, bool PACKED = false>
@@ -635,7 +635,7 @@ int run_pair(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], 
              const T* bias, T* y, int64_t ld_y, int64_t M, int64_t K_g, int64_t N_g, const PeerOut& peers,
              cudaStream_t stream) {
   if (get_encoder() != QLIN_OK) return QLIN_ERR_LAUNCH;
-  if (peers.n > 0) return run_pair_p<T, true>(dev, x, ld_x, w, ld_w, pw, bias, y, ld_y, M, K_g, N_g, peers, stream);
+  if (has_peers(peers)) return run_pair_p<T, true>(dev, x, ld_x, w, ld_w, pw, bias, y, ld_y, M, K_g, N_g, peers, stream);
   return run_pair_p<T, false>(dev, x, ld_x, w, ld_w, pw, bias, y, ld_y, M, K_g, N_g, peers, stream);
 }
 
@@ -939,19 +939,19 @@ int dispatch(int algo, DeviceInfo* dev, const void* x, int64_t ld_x, const void*
   // peer outputs (column-partitioned layer) are written by the tensor-core path only
   if (!w[0] && (algo == QLIN_ALGO_SIMT || std::is_same<T, float>::value)) return QLIN_ERR_ALIGN;
   if constexpr (std::is_same<T, float>::value) {
-    if (peers.n > 0) return QLIN_ERR_ALIGN;
+    if (has_peers(peers)) return QLIN_ERR_ALIGN;
     return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
                        stream);
   } else {
     // peer outputs (the fused all-gather) are written by the tensor-core kernel only
-    if (algo == QLIN_ALGO_GEMV && peers.n > 0) return QLIN_ERR_ALIGN;
+    if (algo == QLIN_ALGO_GEMV && has_peers(peers)) return QLIN_ERR_ALIGN;
     if (algo == QLIN_ALGO_GEMV)
       return run_gemv<T>(dev, xt, ld_x, w, ld_w, pw, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws, flags,
                          peers, stream);
     if (algo == QLIN_ALGO_TC)
       return run_tc<T>(dev, xt, ld_x, w, ld_w, pw, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
                        flags, peers, stream);
-    if (peers.n > 0) return QLIN_ERR_ALIGN;
+    if (has_peers(peers)) return QLIN_ERR_ALIGN;
     return run_simt<T>(dev, xt, ld_x, w, ld_w, bt, la, lb, rank, lora_scale, yt, ld_y, M, K_g, N_g, ws,
                        stream);
   }
@@ -1122,6 +1122,39 @@ size_t sharded_gather_bytes(int dtype, int64_t M, int64_t N_g, int world) {
   return M > 1 ? (size_t)round_up((int64_t)world * M * 4 * N_g * elem_size(dtype), 256) : 0;
 }
 
+// One rank's shard of the column-partitioned layer with its outputs stored
+// into every rank's full output (peer stores or one multicast store each),
+// between an entry and an exit flag barrier over the ranks' flag arrays.
+int allgather_common(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi, const void* wj,
+                     const void* wk, int64_t ld_w, const void* bias, const void* lora_a, const void* lora_b, int rank,
+                     float lora_scale, int64_t M, int64_t K_g, int64_t N_g, void* workspace, size_t workspace_bytes,
+                     int flags, int world, int world_rank, void* y, int64_t ld_out, const PeerOut& peers,
+                     unsigned* const* flag_arrays, unsigned* epoch_word, void* stream) {
+  if (world > 1 && (!flag_arrays || !epoch_word)) return QLIN_ERR_ARG;
+  for (int q = 0; q < world; ++q)
+    if (world > 1 && !flag_arrays[q]) return QLIN_ERR_ARG;
+  int st = validate(dtype, x, ld_x, wr, wi, wj, wk, ld_w, lora_a, lora_b, rank, y, ld_out, M, K_g, N_g);
+  if (st != QLIN_OK || M == 0) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  PeerFlags pf;
+  for (int q = 0; q < world; ++q) pf.f[q] = world > 1 ? flag_arrays[q] : nullptr;
+  if (world > 1) {
+    // Entry barrier (slots [world, 2*world), epoch word 1): no rank stores
+    // into a peer's output while that peer's work queued after the previous
+    // call (reading that output) may still be running.
+    cudaGetLastError();
+    qlin_peer_barrier_kernel<<<1, 32, 0, s>>>(pf, epoch_word + 1, world_rank, world, world);
+    if (cudaGetLastError() != cudaSuccess) return QLIN_ERR_LAUNCH;
+  }
+  st = forward_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y, ld_out, M,
+                      K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_TC, flags, stream, peers);
+  if (st != QLIN_OK || world == 1) return st;
+  // Exit barrier (slots [0, world), epoch word 0): every rank's columns are
+  // in every rank's output.
+  qlin_peer_barrier_kernel<<<1, 32, 0, s>>>(pf, epoch_word, world_rank, world, 0);
+  return cudaGetLastError() == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1142,7 +1175,7 @@ const char* qlin_status_string(int status) {
   }
 }
 
-int qlin_abi_version(void) { return 103; }
+int qlin_abi_version(void) { return 104; }
 
 int qlin_workspace_size(int dtype, int64_t M, int64_t K_g, int64_t N_g, int rank, size_t* bytes) {
   if (!bytes) return QLIN_ERR_ARG;
@@ -1281,35 +1314,35 @@ int qlin_forward_allgather(int dtype, const void* x, int64_t ld_x, const void* w
                            unsigned* epoch_word, void* stream) {
   if (dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
   if (world < 1 || world > kMaxPeers + 1 || world_rank < 0 || world_rank >= world) return QLIN_ERR_ARG;
-  if (!outs || (world > 1 && (!flag_arrays || !epoch_word))) return QLIN_ERR_ARG;
+  if (!outs) return QLIN_ERR_ARG;
   for (int q = 0; q < world; ++q)
-    if (!outs[q] || (world > 1 && !flag_arrays[q])) return QLIN_ERR_ARG;
+    if (!outs[q]) return QLIN_ERR_ARG;
   if (col_offset < 0 || col_offset % 4 != 0 || ld_out < col_offset + 4 * N_g) return QLIN_ERR_SHAPE;
   PeerOut peers;
-  peers.n = 0;
   for (int q = 0; q < world; ++q)
     if (q != world_rank) peers.y[peers.n++] = static_cast<uint8_t*>(outs[q]) + col_offset * 2;
   void* y = static_cast<uint8_t*>(outs[world_rank]) + col_offset * 2;
-  int st = validate(dtype, x, ld_x, wr, wi, wj, wk, ld_w, lora_a, lora_b, rank, y, ld_out, M, K_g, N_g);
-  if (st != QLIN_OK || M == 0) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  PeerFlags pf;
-  for (int q = 0; q < world; ++q) pf.f[q] = flag_arrays[q];
-  if (world > 1) {
-    // Entry barrier (slots [world, 2*world), epoch word 1): no rank stores
-    // into a peer's output while that peer's work queued after the previous
-    // call (reading that output) may still be running.
-    cudaGetLastError();
-    qlin_peer_barrier_kernel<<<1, 32, 0, s>>>(pf, epoch_word + 1, world_rank, world, world);
-    if (cudaGetLastError() != cudaSuccess) return QLIN_ERR_LAUNCH;
-  }
-  st = forward_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, y,
-                      ld_out, M, K_g, N_g, workspace, workspace_bytes, QLIN_ALGO_TC, flags, stream, peers);
-  if (st != QLIN_OK || world == 1) return st;
-  // Exit barrier (slots [0, world), epoch word 0): every rank's columns are
-  // in every rank's output.
-  qlin_peer_barrier_kernel<<<1, 32, 0, s>>>(pf, epoch_word, world_rank, world, 0);
-  return cudaGetLastError() == cudaSuccess ? QLIN_OK : QLIN_ERR_LAUNCH;
+  return allgather_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, M, K_g, N_g,
+                          workspace, workspace_bytes, flags, world, world_rank, y, ld_out, peers, flag_arrays,
+                          epoch_word, stream);
+}
+
+int qlin_forward_allgather_mc(int dtype, const void* x, int64_t ld_x, const void* wr, const void* wi,
+                              const void* wj, const void* wk, int64_t ld_w, const void* bias, const void* lora_a,
+                              const void* lora_b, int rank, float lora_scale, int64_t M, int64_t K_g, int64_t N_g,
+                              void* workspace, size_t workspace_bytes, int flags, int world, int world_rank,
+                              void* out, void* out_mc, int64_t ld_out, int64_t col_offset,
+                              unsigned* const* flag_arrays, unsigned* epoch_word, void* stream) {
+  if (dtype != QLIN_BF16 && dtype != QLIN_F16) return QLIN_ERR_DTYPE;
+  if (world < 1 || world > kMaxPeers + 1 || world_rank < 0 || world_rank >= world) return QLIN_ERR_ARG;
+  if (!out || !out_mc) return QLIN_ERR_ARG;
+  if (col_offset < 0 || col_offset % 4 != 0 || ld_out < col_offset + 4 * N_g) return QLIN_ERR_SHAPE;
+  PeerOut peers;
+  peers.mc = static_cast<uint8_t*>(out_mc) + col_offset * 2;
+  void* y = static_cast<uint8_t*>(out) + col_offset * 2;
+  return allgather_common(dtype, x, ld_x, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, M, K_g, N_g,
+                          workspace, workspace_bytes, flags, world, world_rank, y, ld_out, peers, flag_arrays,
+                          epoch_word, stream);
 }
 
 int qlin_ipc_alloc(size_t bytes, void** out, void* handle) {

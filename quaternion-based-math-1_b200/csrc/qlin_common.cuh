@@ -31,18 +31,44 @@ template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return
 // Four fp32 values -> four 16-bit values packed in 8 bytes (round to nearest even).
 // Output rows of the column-partitioned layer's other ranks: the same
 // [M, ld] layout, already offset to this rank's columns (peer memory mapped
-// through CUDA IPC; plain stores over NVLink, no multicast).
+// through CUDA IPC; plain stores over NVLink, no multicast), or, when mc is
+// set, the multicast address of every rank's full output (one multimem
+// store through NVSwitch reaches all ranks, this one included).
 constexpr int kMaxPeers = 7;
 struct PeerOut {
-  void* y[kMaxPeers];
-  int n;
+  void* y[kMaxPeers] = {};
+  int n = 0;
+  void* mc = nullptr;
 };
+__host__ __device__ __forceinline__ bool has_peers(const PeerOut& p) { return p.n > 0 || p.mc != nullptr; }
+
+// Stores through an NVLink multicast address (multimem.st: NVSwitch writes
+// the bytes into the same offset of every member's memory).  The data are
+// raw 16-bit pairs moved as .f32 words (the form the instruction takes).
+__device__ __forceinline__ void multimem_st8(void* p, uint2 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};"
+               ::"l"(p), "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y))
+               : "memory");
+}
+__device__ __forceinline__ void multimem_st16(void* p, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};"
+               ::"l"(p), "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+               "f"(__uint_as_float(v.w))
+               : "memory");
+}
 
 // Stores four 16-bit outputs (8 bytes) at element offset off of y and, for
-// kernels built with peer outputs, of every peer's output (a compile-time
-// choice: the runtime loop alone cost 8% of a prefill call).
+// kernels built with peer outputs, of every peer's output -- or once through
+// the multicast address (a compile-time choice: the runtime loop alone cost
+// 8% of a prefill call).
 template <typename T, bool PEERS>
 __device__ __forceinline__ void store_out(T* y, const PeerOut& peers, int64_t off, uint2 v) {
+  if constexpr (PEERS) {
+    if (peers.mc) {
+      multimem_st8(reinterpret_cast<T*>(peers.mc) + off, v);
+      return;
+    }
+  }
   *reinterpret_cast<uint2*>(y + off) = v;
   if constexpr (PEERS) {
     for (int p = 0; p < peers.n; ++p) *reinterpret_cast<uint2*>(reinterpret_cast<T*>(peers.y[p]) + off) = v;

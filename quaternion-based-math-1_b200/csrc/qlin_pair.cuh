@@ -517,10 +517,14 @@ qlin_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
             if (m < prm.M && nn < 4 * prm.N_g) {
               const uint4 v = *reinterpret_cast<const uint4*>(stage + t * kPairRows + 8 * cc);
               const int64_t off = (int64_t)m * prm.ld_y + nn;
-              *reinterpret_cast<uint4*>(y + off) = v;
-              if constexpr (PEERS) {
-                for (int pp = 0; pp < prm.peers.n; ++pp)
-                  *reinterpret_cast<uint4*>(reinterpret_cast<T*>(prm.peers.y[pp]) + off) = v;
+              if (PEERS && prm.peers.mc) {
+                multimem_st16(reinterpret_cast<T*>(prm.peers.mc) + off, v);
+              } else {
+                *reinterpret_cast<uint4*>(y + off) = v;
+                if constexpr (PEERS) {
+                  for (int pp = 0; pp < prm.peers.n; ++pp)
+                    *reinterpret_cast<uint4*>(reinterpret_cast<T*>(prm.peers.y[pp]) + off) = v;
+                }
               }
             }
           }

@@ -928,7 +928,7 @@ qlin_splitk_reduce_kernel(const float4* __restrict__ partials, int split, int t_
   for (int a = 0; a < 4; ++a) b[a] = to_f32(braw[a]);
   store_out<T, true>(y, peers, (int64_t)m * ld_y + 4 * o,
                      pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
-  if (peers.n > 0) fence_sys();
+  if (has_peers(peers)) fence_sys();
 }
 
 }  // namespace qlin

@@ -24,7 +24,12 @@ mapped into every other rank (CUDA IPC, exchanged once per output shape),
 each rank's epilogue stores its columns into all of them over NVLink, and
 bounded cross-rank flag barriers open the call (no rank writes into an
 output that a peer may still be copying from) and end it
-(``qlin_forward_allgather``).
+(``qlin_forward_allgather``).  Where the box offers NVLink multicast
+(NVSwitch; torch's symmetric memory reports it), the full outputs are one
+symmetric-memory buffer per rank bound to a multicast object and each output
+piece is stored once through the multicast address (``multimem.st``): every
+rank sends its columns over NVLink once instead of once per peer
+(``qlin_forward_allgather_mc``).
 """
 
 from __future__ import annotations
@@ -39,7 +44,7 @@ from . import _lib
 from .linear import QuaternionLinear, fused_quaternion_linear
 from .packing import check_divisible
 
-__all__ = ["shard_bounds", "ColumnParallelQuaternionLinear", "gather_columns", "PeerOutputs"]
+__all__ = ["shard_bounds", "ColumnParallelQuaternionLinear", "gather_columns", "PeerOutputs", "MulticastOutputs"]
 
 
 def shard_bounds(out_groups: int, world: int, rank: int) -> tuple[int, int, int]:
@@ -138,6 +143,53 @@ class PeerOutputs:
         self._mapped, self._owned = [], []
 
 
+class MulticastOutputs:
+    """Every rank's full ``[M, cols]`` output in one NVLink multicast group.
+
+    Built collectively (every rank of ``group`` constructs it with the same
+    shape) from torch's symmetric memory: ``out`` is this rank's buffer,
+    ``mc`` the multicast address of the same offset (a store through it lands
+    in every rank's ``out``), the barrier flags ``[2 * world]`` and two call
+    counters live in a second symmetric buffer, zero-filled before any rank
+    uses them (``_flags``: every rank's flag array as mapped here).  Raises
+    RuntimeError where multicast is not available (see ``available``).
+    """
+
+    @staticmethod
+    def available(device) -> bool:
+        """Whether this process's GPU offers NVLink multicast (torch's check)."""
+        try:
+            from torch._C._distributed_c10d import _SymmetricMemory
+            dev = torch.device(device)
+            return bool(_SymmetricMemory.has_multicast_support(torch._C._autograd.DeviceType.CUDA, dev.index))
+        except Exception:  # an older torch or no CUDA: the peer-store path
+            return False
+
+    def __init__(self, M: int, cols: int, dtype, device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        gname = (group if group is not None else dist.group.WORLD).group_name
+        self.out = symm_mem.empty((M, cols), dtype=dtype, device=self.device)
+        self._h_out = symm_mem.rendezvous(self.out, gname)
+        base = self._h_out.buffer_ptrs[self.rank]
+        if not self._h_out.multicast_ptr:
+            raise RuntimeError("NVLink multicast is not available for this group")
+        self.mc = self._h_out.multicast_ptr + (self.out.data_ptr() - base)
+        flags = symm_mem.empty((2 * self.world + 2,), dtype=torch.int32, device=self.device)
+        flags.zero_()
+        self._h_flags = symm_mem.rendezvous(flags, gname)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group)  # every rank's flags are zero before any rank signals
+        off = flags.data_ptr() - self._h_flags.buffer_ptrs[self.rank]
+        self._flag_buf = flags
+        self.flags = flags[:2 * self.world]
+        self.epoch = flags[2 * self.world:]
+        P = ctypes.c_void_p
+        self._flags = (P * self.world)(*(p + off for p in self._h_flags.buffer_ptrs))
+
+
 class _CudaArray:
     """__cuda_array_interface__ of a raw device buffer (zero-copy torch view)."""
 
@@ -167,7 +219,8 @@ class ColumnParallelQuaternionLinear(nn.Module):
         if fused_allgather not in (True, False, "auto"):
             raise ValueError("fused_allgather must be True, False or 'auto'")
         self.fused_allgather = fused_allgather
-        self._peer_outputs: dict[int, PeerOutputs] = {}
+        self._peer_outputs: dict[int, PeerOutputs | MulticastOutputs] = {}
+        self._multicast: bool | None = None  # decided on the first fused call
         self.in_features = in_features
         self.out_features = out_features
         self.in_groups = check_divisible(in_features, "in_features")
@@ -224,9 +277,15 @@ class ColumnParallelQuaternionLinear(nn.Module):
         M = x2.shape[0]
         G = self.world_size
         cols = 4 * self.shard * G
+        if self._multicast is None:
+            # the same answer on every rank: all must take the same (collective) path
+            ok = torch.tensor([int(MulticastOutputs.available(x2.device))], device=x2.device)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.process_group)
+            self._multicast = bool(ok.item())
         po = self._peer_outputs.get(M)
         if po is None:
-            po = self._peer_outputs[M] = PeerOutputs(M, cols, x2.dtype, x2.device, self.process_group)
+            make = MulticastOutputs if self._multicast else PeerOutputs
+            po = self._peer_outputs[M] = make(M, cols, x2.dtype, x2.device, self.process_group)
         la, lb = self.lora_A, self.lora_B
         rank_l = 0 if la is None else la.shape[0]
         if rank_l % 8:
@@ -240,13 +299,19 @@ class ColumnParallelQuaternionLinear(nn.Module):
         ws = _lib.zeroed_workspace(x2.device, ws_bytes) if ws_bytes else None
         flags = _lib.FLAG_ZEROED_WORKSPACE if ws is not None else 0
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        common = (_lib.dtype_code(x2.dtype), x2.data_ptr(), self.in_features,
+                  self.wr.data_ptr(), self.wi.data_ptr(), self.wj.data_ptr(), self.wk.data_ptr(), K_g,
+                  ptr(self.bias), ptr(la), ptr(lb), rank_l, float(self.lora_scale),
+                  M, K_g, n, ptr(ws), ws_bytes, flags, G, self.rank)
         with torch.cuda.device(x2.device):
-            code = _lib.load().qlin_forward_allgather(
-                _lib.dtype_code(x2.dtype), x2.data_ptr(), self.in_features,
-                self.wr.data_ptr(), self.wi.data_ptr(), self.wj.data_ptr(), self.wk.data_ptr(), K_g,
-                ptr(self.bias), ptr(la), ptr(lb), rank_l, float(self.lora_scale),
-                M, K_g, n, ptr(ws), ws_bytes, flags, G, self.rank, po._outs, cols, 4 * n * self.rank,
-                po._flags, po.epoch.data_ptr(), _lib.stream_handle(x2.device))
+            if isinstance(po, MulticastOutputs):
+                code = _lib.load().qlin_forward_allgather_mc(
+                    *common, po.out.data_ptr(), po.mc, cols, 4 * n * self.rank, po._flags, po.epoch.data_ptr(),
+                    _lib.stream_handle(x2.device))
+            else:
+                code = _lib.load().qlin_forward_allgather(
+                    *common, po._outs, cols, 4 * n * self.rank, po._flags, po.epoch.data_ptr(),
+                    _lib.stream_handle(x2.device))
         _lib.check(code, "qlin_forward_allgather")
         return po.out[:, :self.out_features].clone()
 

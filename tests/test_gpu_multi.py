@@ -1,10 +1,11 @@
 """Column-partitioned layer on two GPUs (skipped with fewer).
 
 Each rank holds half of the output quaternion rows.  The NCCL path (shard
-kernel, all-gather, column gather) and the fused path (the shard kernel's
+kernel, all-gather, column gather) and the fused paths (the shard kernel's
 epilogue stores into every rank's output over NVLink, then a bounded flag
-barrier; qlin_forward_allgather) must give the same [M, out] output on every
-rank, agreeing with each other (to fp32 summation order: the two paths may
+barrier: peer stores, qlin_forward_allgather, and -- where NVLink multicast
+is available -- one multicast store per piece, qlin_forward_allgather_mc)
+must give the same [M, out] output on every rank, agreeing with each other (to fp32 summation order: the two paths may
 run different device kernels) and within the bf16 tolerance of the
 unpartitioned layer.  Output widths that do not divide by the world size exercise the
 padded last shard; repeated calls exercise the barriers' call counters, and
@@ -68,11 +69,17 @@ def _rank_main(rank, port, out_q):
             plain = qb.ColumnParallelQuaternionLinear.from_full(full, lora_A=la, lora_B=lb, lora_scale=scale)
             plain.fused_allgather = False
             fused = qb.ColumnParallelQuaternionLinear.from_full(full, lora_A=la, lora_B=lb, lora_scale=scale)
-            fused.fused_allgather = True
+            fused.fused_allgather = True  # multicast stores where available
+            peer = qb.ColumnParallelQuaternionLinear.from_full(full, lora_A=la, lora_B=lb, lora_scale=scale)
+            peer.fused_allgather = True
+            peer._multicast = False  # peer stores
             for _ in range(3):
                 y_plain = plain(x)
                 y_fused = fused(x)
+                y_peer = peer(x)
             torch.cuda.synchronize()
+            # the same kernels on the same inputs: the two fused paths agree bit for bit
+            same_fused = bool(torch.equal(y_fused, y_peer))
             err = ((y_fused.float() - want.float()).norm() / want.float().norm()).item()
             # the NCCL path's per-shard calls may run the decode GEMV (1-2
             # tokens), the fused path the tensor-core kernel: fp32 summation
@@ -89,7 +96,7 @@ def _rank_main(rank, port, out_q):
             for gi, wi in zip(gots, wants):
                 e = ((gi.float() - wi.float()).norm() / wi.float().norm()).item()
                 err = max(err, e)
-            results.append((M, fout, diff <= 4e-3, err))
+            results.append((M, fout, diff <= 4e-3 and same_fused, err, bool(fused._multicast)))
         results.append(("device_error", qb.device_error(dev)))
         out_q.put((rank, results))
         ok = True
@@ -131,6 +138,6 @@ def test_column_partition_fused_allgather_matches_nccl_path():
     for r, res in got.items():
         *cases, (_, dev_err) = res
         assert dev_err == 0, (r, dev_err)
-        for M, fout, same, err in cases:
+        for M, fout, same, err, _multicast in cases:
             assert same, (r, M, fout)
             assert err <= 1e-2, (r, M, fout, err)
