@@ -496,7 +496,8 @@ def time_sharded(qb, wl, torch, dev, dist, world, rank, W, cases):
     capture is refused); device time, max over ranks.  Weight shards rotate
     across more than L2.  `cases` is a list of (M, steps).  The fused
     roofline target is the slower of the shard's compute (or HBM) time and
-    its NVLink egress at 770 GB/s."""
+    its NVLink traffic at 770 GB/s per direction: (world - 1) shards' outputs
+    leave each rank (peer stores) and, multicast or not, arrive at each rank."""
     lib = qb._lib.load()
     code = qb._lib.dtype_code(torch.bfloat16)
     stream_of = qb._lib.stream_handle
@@ -585,7 +586,9 @@ def time_sharded(qb, wl, torch, dev, dist, world, rank, W, cases):
                     "frac_per_gpu": a / peaks_ref["bf16_tflops"], "basis": "shard FLOP per GPU"}
         egress = (world - 1) * M * 4 * n * 2  # bytes each rank stores to its peers
         t_nvl = egress / 770e9 * 1e6          # at the measured 770 GB/s peer copy, per direction
-        t_nvl_mc = M * 4 * n * 2 / 770e9 * 1e6  # multicast: each rank's columns cross its links once
+        # multicast sends each rank's columns over its links once, but every
+        # rank still receives the other ranks' columns: the same ingress bound
+        t_nvl_mc = t_nvl
         t_cmp = (nbytes / (peaks_ref["hbm_gbs"] * 1e9) if M <= 16 else flops / (peaks_ref["bf16_tflops"] * 1e12)) * 1e6
         launches = qb._lib.plan(torch.bfloat16, M, K_g, n, 0, flags=qb._lib.FLAG_ZEROED_WORKSPACE)["launches"]
         out[M] = {"us_nccl": us, "us_fused": us_f, "steps": steps, "timing": [mode, mode_f], "shard_rows": n,
