@@ -894,6 +894,8 @@ int run_gemv(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], 
   prm.K_g = (int)K_g;
   prm.N_g = (int)N_g;
   prm.nch = (int)((K_g + kGemvChunk - 1) / kGemvChunk);
+  // bulk copies of the x rows need 16-byte aligned rows
+  prm.x_bulk = (aligned(x, 16) && (ld_x * 2) % 16 == 0) ? 1 : 0;
   prm.static_weights = (flags & QLIN_FLAG_STATIC_WEIGHTS) ? 1 : 0;
   prm.peers = peers;
   prm.t = nullptr;
