@@ -355,20 +355,30 @@ qlin_gemv_kernel(const GemvParams prm) {
   // ---- stage x as fp32 quaternions (zeros past K_g and past M) ----
   if (prm.x_bulk) {
     mbar_wait(xbar, 0);
-    const int nq = nch * kGemvChunk;
-    for (int q = tid; q < MT * nq; q += nthr) {
-      const int m = q / nq, i = q - m * nq;
-      uint2 r = make_uint2(0u, 0u);
-      if (m < prm.M && i < prm.K_g) r = *reinterpret_cast<const uint2*>(xraw + ((size_t)m * prm.K_g + i) * 8);
+    // two quaternions (16 bytes of raw x) per step; (m, i) advance without a division
+    const int nq = nch * kGemvChunk, np = nq / 2;
+    int m = tid / np, i = 2 * (tid - (tid / np) * np);
+    for (; m < MT;) {
+      uint4 r = make_uint4(0u, 0u, 0u, 0u);
+      if (m < prm.M && i < prm.K_g) r = *reinterpret_cast<const uint4*>(xraw + ((size_t)m * prm.K_g + i) * 8);
       const T* h = reinterpret_cast<const T*>(&r);
-      const float4 v = make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
-      const int c = i / kGemvChunk;
-      if constexpr (PACKED) {
-        const int ic = i - c * kGemvChunk;
-        xs[((m * nch + c) * 2 + (ic & 1)) * (kGemvChunk / 2) + (ic >> 1)] = v;
-      } else {
-        const int l = (i / 8) & 31, j = i & 7;
-        xs[((m * nch + c) * 8 + j) * 32 + (l ^ j)] = v;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int ie = i + e;
+        const float4 v = make_float4(to_f32(h[4 * e]), to_f32(h[4 * e + 1]), to_f32(h[4 * e + 2]), to_f32(h[4 * e + 3]));
+        const int c = ie / kGemvChunk;
+        if constexpr (PACKED) {
+          const int ic = ie - c * kGemvChunk;
+          xs[((m * nch + c) * 2 + (ic & 1)) * (kGemvChunk / 2) + (ic >> 1)] = v;
+        } else {
+          const int l = (ie / 8) & 31, j = ie & 7;
+          xs[((m * nch + c) * 8 + j) * 32 + (l ^ j)] = v;
+        }
+      }
+      i += 2 * nthr;
+      while (i >= nq) {
+        i -= nq;
+        ++m;
       }
     }
   } else {
