@@ -279,7 +279,10 @@ int qlin_forward_allgather_mc(int dtype,
  * copied back to y_host, all enqueued on `stream` in that order; y_host
  * holds the result once the stream has reached that point (synchronise the
  * stream or an event).  Host buffers should be page-locked (cudaHostAlloc /
- * cudaHostRegister) for the copies to be asynchronous.  Weights, bias and
+ * cudaHostRegister) for the copies to be asynchronous.  For decode-sized
+ * page-locked buffers (at most 64 KB, rows of whole 16-byte words) x comes
+ * in by a small kernel and the layer's kernels store y straight into the
+ * host buffer through its device mapping; otherwise copy-engine transfers.  Weights, bias and
  * LoRA stay device pointers.  workspace (device): at least
  * qlin_host_workspace_size() bytes -- the staged x and y, then the
  * workspace of qlin_forward_ex, which QLIN_FLAG_ZEROED_WORKSPACE refers to

@@ -1086,7 +1086,8 @@ size_t host_staging_bytes(int dtype, int64_t M, int64_t K_g, int64_t N_g) {
   return (size_t)(round_up(M * 4 * K_g * es, 256) + round_up(M * 4 * N_g * es, 256));
 }
 
-// Largest transfer qlin_forward_host runs as a kernel (stage-in / stage-out).
+// Largest transfer qlin_forward_host runs without the copy engine (the x
+// stage-in kernel, y stored by the kernels through the host mapping).
 constexpr size_t kHostDirectBytes = 64 * 1024;
 
 // The device address of a page-locked host buffer when qlin_forward_host may
@@ -1450,8 +1451,9 @@ int qlin_forward_host(int dtype, const void* x_host, int64_t ld_x, const void* w
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t xrow = (size_t)(4 * K_g) * es, yrow = (size_t)(4 * N_g) * es;
   // Decode-sized transfers between page-locked, device-mapped host buffers
-  // and the device run as kernels of the dependent-launch chain; larger or
-  // pageable ones as copy-engine transfers.
+  // and the device: x by a small kernel of the dependent-launch chain, y
+  // stored by the layer's own kernels; larger or pageable ones as
+  // copy-engine transfers.
   void* xmap = direct_host_map(x_host, xrow, (size_t)ld_x * es, M);
   void* ymap = direct_host_map(y_host, yrow, (size_t)ld_y * es, M);
   cudaError_t e;
@@ -1466,13 +1468,14 @@ int qlin_forward_host(int dtype, const void* x_host, int64_t ld_x, const void* w
             : cudaMemcpy2DAsync(xd, xrow, x_host, (size_t)ld_x * es, xrow, (size_t)M, cudaMemcpyHostToDevice, s);
   }
   if (e != cudaSuccess) return QLIN_ERR_LAUNCH;
-  const int st = qlin_forward_ex(dtype, xd, 4 * K_g, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale, yd,
-                                 4 * N_g, M, K_g, N_g, xd + staging, workspace_bytes - staging, algo, flags, stream);
+  // a decode-sized output goes straight from the kernels' epilogues into the
+  // page-locked host buffer through its device mapping
+  const int st = qlin_forward_ex(dtype, xd, 4 * K_g, wr, wi, wj, wk, ld_w, bias, lora_a, lora_b, rank, lora_scale,
+                                 ymap ? ymap : yd, ymap ? ld_y : 4 * N_g, M, K_g, N_g, xd + staging,
+                                 workspace_bytes - staging, algo, flags, stream);
   if (st != QLIN_OK) return st;
   if (ymap) {
-    const int64_t row = (int64_t)(yrow / 16), n = M * row;
-    e = launch_pdl(qlin_stage_out_kernel, (unsigned)((n + 511) / 512), s, reinterpret_cast<const uint4*>(yd), row,
-                   static_cast<uint4*>(ymap), (int64_t)(ld_y * es / 16), row, M);
+    e = cudaSuccess;
   } else {
     e = ld_y == 4 * N_g
             ? cudaMemcpyAsync(y_host, yd, yrow * M, cudaMemcpyDeviceToHost, s)

@@ -8,8 +8,8 @@
 //  * qlin_prologue_kernel  -- the tensor-core path's prologue: component planes
 //                             and the scaled LoRA down projection in one launch.
 //  * qlin_gather_kernel    -- [G, M, n] shards -> [M, G*n] columns.
-//  * qlin_stage_in_kernel / qlin_stage_out_kernel -- qlin_forward_host's small
-//                             copies between page-locked host memory and the device.
+//  * qlin_stage_in_kernel  -- qlin_forward_host's small copy of x from
+//                             page-locked host memory to the device.
 #pragma once
 
 #include "qlin_common.cuh"
@@ -534,19 +534,17 @@ __global__ void __launch_bounds__(32) qlin_peer_barrier_kernel(const PeerFlags p
   }
 }
 
-// qlin_forward_host for decode-sized inputs and outputs: the copies between
-// page-locked host memory (through its device mapping) and the device run as
-// kernels of the call's programmatic-dependent chain rather than copy-engine
-// transfers (measured: an 8 KB cudaMemcpyAsync each way cost about 6 us of
-// device time per call; a kernel's PCIe round trip about 1 us).  Rows of
-// `row` 16-byte words, leading dimensions in 16-byte words, two words per
-// thread.
-//
-// In: the host reads are issued before the dependency wait (earlier work of
-// the stream does not write the caller's host buffer; the host wrote it
-// before the call), the device stores after it (earlier calls' kernels may
-// still read the staging buffer).  Reads bypass the caches (ld.global.cv):
-// the host rewrites the buffer between calls.
+// qlin_forward_host for decode-sized inputs: x comes from page-locked host
+// memory (through its device mapping) by this kernel of the call's
+// programmatic-dependent chain rather than by a copy-engine transfer
+// (measured: an 8 KB cudaMemcpyAsync each way cost about 6 us of device time
+// per call; a kernel's PCIe round trip about 1 us).  Rows of `row` 16-byte
+// words, leading dimensions in 16-byte words, two words per thread.  The
+// host reads are issued before the dependency wait (earlier work of the
+// stream does not write the caller's host buffer; the host wrote it before
+// the call), the device stores after it (earlier calls' kernels may still
+// read the staging buffer).  Reads bypass the caches (ld.global.cv): the host
+// rewrites the buffer between calls.
 __global__ void __launch_bounds__(256)
 qlin_stage_in_kernel(const uint4* __restrict__ src, int64_t ld_src, uint4* __restrict__ dst, int64_t ld_dst,
                      int64_t row, int64_t M) {
@@ -572,25 +570,6 @@ qlin_stage_in_kernel(const uint4* __restrict__ src, int64_t ld_src, uint4* __res
 #pragma unroll
   for (int u = 0; u < 2; ++u)
     if (at[u] >= 0) dst[at[u]] = v[u];
-}
-
-// Out: after the forward's last kernel (dependency wait), device loads and
-// stores into the host mapping; visible to the host once the stream passes
-// this kernel.
-__global__ void __launch_bounds__(256)
-qlin_stage_out_kernel(const uint4* __restrict__ src, int64_t ld_src, uint4* __restrict__ dst, int64_t ld_dst,
-                      int64_t row, int64_t M) {
-  pdl_launch_dependents();
-  pdl_wait_prior();
-  const int64_t n = M * row;
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int64_t idx = ((int64_t)blockIdx.x * 2 + u) * blockDim.x + threadIdx.x;
-    if (idx < n) {
-      const int64_t m = idx / row, j = idx - m * row;
-      dst[m * ld_dst + j] = ld_cg_v4(src + m * ld_src + j);
-    }
-  }
 }
 
 }  // namespace qlin
