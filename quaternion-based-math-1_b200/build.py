@@ -21,7 +21,8 @@ CSRC = os.path.join(PKG, "csrc")
 LIB_DIR = os.path.join(PKG, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libqlin_b200.so")
 SOURCES = [os.path.join(CSRC, "qlin_abi.cu")]
-DEPENDS = SOURCES + [os.path.join(CSRC, f) for f in ("qlin_common.cuh", "qlin_gemv.cuh", "qlin_simt.cuh", "qlin_tc.cuh")] + [
+DEPENDS = SOURCES + [os.path.join(CSRC, f) for f in ("qlin_common.cuh", "qlin_gemv.cuh", "qlin_pair.cuh",
+                                                      "qlin_simt.cuh", "qlin_tc.cuh")] + [
     os.path.join(REPO, "include", "qlin_b200.h")
 ]
 
