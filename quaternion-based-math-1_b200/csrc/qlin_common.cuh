@@ -329,23 +329,22 @@ __device__ __forceinline__ uint32_t map_peer_smem(uint32_t local_addr, uint32_t 
   return r;
 }
 // Split cluster barrier (all threads of every CTA of the cluster).
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait_acquire() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// 16-byte store into another CTA's shared memory of the cluster, counted as
-// 16 transaction bytes on that CTA's mbarrier (both shared::cluster addresses).
-__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, float4 v, uint32_t remote_bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
-               ::"r"(remote_addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory into another CTA's of the cluster, counted as
+// transaction bytes on that CTA's mbarrier (dst and bar: shared::cluster
+// addresses).  The source must stay untouched, and its CTA alive, until the
+// destination's barrier has completed.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                  uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst_cluster), "r"(src_cta), "r"(bytes), "r"(bar_cluster)
                : "memory");
-}
-__device__ __forceinline__ float ld_peer_f32(uint32_t cluster_addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
-  return v;
 }
 
 // Programmatic dependent launch: let the next kernel in the stream start its

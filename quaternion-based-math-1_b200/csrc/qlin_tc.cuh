@@ -121,7 +121,12 @@ struct TcCfg {
   static constexpr int kStages = kFit > 6 ? 6 : (kFit < 2 ? 2 : kFit);
   static constexpr int kSliceOffset = kStages * kStageBytes;
   static constexpr int kRecvOffset = 0;
-  static_assert(kRecvBytes <= kStages * kStageBytes, "receive buffer inside the stage ring");
+  // ... followed by the send buffer: this CTA's partials of every token,
+  // [token][128 rows] x float4, from which one bulk copy per peer sends the
+  // tokens that peer owns.
+  static constexpr int kSendOffset = kRecvBytes;
+  static constexpr int kSendBytes = CLUSTER ? kTcClusterTokens * kTcBlockO * 16 : 0;
+  static_assert(kSendOffset + kSendBytes <= kStages * kStageBytes, "receive and send buffers inside the stage ring");
   // accumulators: 4*N_TOK columns of Y (+ kTcLoraInRank columns of t)
   static constexpr int kTmemCols = tmem_cols_for(4 * N_TOK + (LORA == kLoraTc ? kTcLoraInRank : 0));
   static constexpr int kBarOffset = kSliceOffset + kSliceBytes;
@@ -201,6 +206,30 @@ __device__ __forceinline__ unsigned atomic_add_release_gpu(unsigned* p, unsigned
   asm volatile("fence.acq_rel.gpu;\n\tatom.relaxed.gpu.global.add.u32 %0, [%1], %2;"
                : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
+}
+
+// Cluster K split, owner side: acc += the C splits' partials of one token in
+// split order (split ks from mine_addr, split sp != ks from receive slot
+// sp - (sp > ks), slot_bytes apart from recv_addr); MAXC >= C.  The loads are
+// issued together, then summed.
+template <int MAXC>
+__device__ __forceinline__ void tc_cluster_sum(float4& acc, int C, int ks, uint32_t mine_addr,
+                                               uint32_t recv_addr, uint32_t slot_bytes) {
+  uint32_t r[MAXC][4];
+#pragma unroll
+  for (int sp = 0; sp < MAXC; ++sp) {
+    const uint32_t addr = sp == ks ? mine_addr : recv_addr + (uint32_t)(sp - (sp > ks ? 1 : 0)) * slot_bytes;
+    if (sp < C) ld_shared_v4(addr, r[sp][0], r[sp][1], r[sp][2], r[sp][3]);
+  }
+#pragma unroll
+  for (int sp = 0; sp < MAXC; ++sp) {
+    if (sp < C) {
+      acc.x += __uint_as_float(r[sp][0]);
+      acc.y += __uint_as_float(r[sp][1]);
+      acc.z += __uint_as_float(r[sp][2]);
+      acc.w += __uint_as_float(r[sp][3]);
+    }
+  }
 }
 
 template <typename T, int N_TOK, bool STACK, int LORA, bool PEERS, bool CLUSTER = false>
@@ -694,9 +723,11 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
     } else if (CLUSTER) {
       // Cluster K split (reduce-scatter, see kTcClusterTokens): this CTA's
       // fp32 partials of the tokens other CTAs own go to their receive
-      // buffers (st.async, counted on the owner's gather barrier) -- sent even
-      // after an abort so every owner's count completes -- and the owned
-      // tokens are summed over all splits in split order, plus the bias.
+      // buffers -- staged in this CTA's send buffer, then one bulk copy per
+      // owner (shared::cta -> shared::cluster, counted on the owner's gather
+      // barrier), sent even after an abort so every owner's count completes
+      // -- and the owned tokens are summed over all splits in split order,
+      // plus the bias.
       const int C = prm.split_k;
       const int per = (m_tile + C - 1) / C;
       const int own0 = ks * per;
@@ -707,47 +738,55 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
       tmem_ld_wait();
       // The receive buffers alias the stage rings: tell every other CTA that
       // this one is past its main loop (its last UMMA has read its stages),
-      // and send only once all of them are.
-      if (threadIdx.x == 0)
-        for (int q = 0; q < C; ++q)
-          if (q != ks) mbar_arrive_remote(map_peer_smem(smem_u32(peers_free), (uint32_t)q));
-      const bool peers_ok = mbar_wait(peers_free, 0);
-      if (!peers_ok) *abort_flag = 1;
-      const uint32_t recv_local = smem_u32(smem + Cfg::kRecvOffset);
-      const uint32_t gather_local = smem_u32(gather);
+      // and send only once all of them are.  This CTA's own ring is free
+      // once its accumulator is complete, so the send buffer is filled first.
+      // Lane q of warp 0 handles peer q.  The code stays free of divisions
+      // and data-dependent branches: with one warp per SM sub-partition
+      // nothing hides their latency (a per-token owner test t / per cost
+      // ~1.3 us per call here, the unconditional stores 0.35 us).
+      const int q = lane;
+      const bool peer = warp == 0 && q < C && q != ks;
+      if (peer) mbar_arrive_remote(map_peer_smem(smem_u32(peers_free), (uint32_t)q));
+      const uint32_t send = smem_u32(smem + Cfg::kSendOffset);
 #pragma unroll
-      for (int t = 0; t < kTcClusterTokens; ++t) {
-        if (t < m_tile) {
-          const int owner = t / per;
-          if (owner != ks) {
-            const int slot = (ks < owner ? ks : ks - 1) * per + (t - owner * per);
-            st_async_v4(map_peer_smem(recv_local, (uint32_t)owner) + (uint32_t)((slot * kTcBlockO + o_local) * 16),
-                        make_float4(v[0][t], v[1][t], v[2][t], v[3][t]),
-                        map_peer_smem(gather_local, (uint32_t)owner));
-          }
+      for (int t = 0; t < kTcClusterTokens; ++t)  // every token; only the peers' ranges are sent
+        st_shared_v4(send + (uint32_t)((t * kTcBlockO + o_local) * 16), __float_as_uint(v[0][t]),
+                     __float_as_uint(v[1][t]), __float_as_uint(v[2][t]), __float_as_uint(v[3][t]));
+      fence_async_smem();  // generic-proxy stores -> bulk copy reads
+      epi_bar_sync();
+      if (warp == 0) {
+        if (!mbar_wait(peers_free, 0)) *abort_flag = 1;
+        const int nq = min(m_tile, (q + 1) * per) - q * per;  // tokens owner q holds
+        if (peer && nq > 0) {
+          const int slot = (ks < q ? ks : ks - 1) * per;
+          bulk_copy_to_peer(map_peer_smem(smem_u32(smem + Cfg::kRecvOffset), (uint32_t)q) +
+                                (uint32_t)(slot * kTcBlockO * 16),
+                            send + (uint32_t)(q * per * kTcBlockO * 16), (uint32_t)(nq * kTcBlockO * 16),
+                            map_peer_smem(smem_u32(gather), (uint32_t)q));
         }
       }
       if (n_own > 0) {
         const bool got = mbar_wait(gather, 0);
-        const float4* recv = reinterpret_cast<const float4*>(smem + Cfg::kRecvOffset);
         const int o = o0 + o_local;
         float b[4];
 #pragma unroll
         for (int a = 0; a < 4; ++a) b[a] = to_f32(bias_raw[a]);
+        // Split sp's partial of owned token own0 + tl: this CTA's own from
+        // the send buffer, the others from receive slot (sp - (sp > ks)) * per
+        // + tl.  All loads first, then the sum in split order.
+        const uint32_t mine_addr = send + (uint32_t)((own0 * kTcBlockO + o_local) * 16);
+        const uint32_t recv_addr = smem_u32(smem + Cfg::kRecvOffset) + (uint32_t)(o_local * 16);
+        const uint32_t slot_bytes = (uint32_t)(per * kTcBlockO * 16);
         for (int tl = 0; tl < n_own; ++tl) {
-          const int t = own0 + tl;
-          // this split's own partial of token t (registers, selected without a runtime index)
-          float4 mine = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int tt = 0; tt < kTcClusterTokens; ++tt)
-            if (tt == t) mine = make_float4(v[0][tt], v[1][tt], v[2][tt], v[3][tt]);
+          const uint32_t tok_off = (uint32_t)(tl * kTcBlockO * 16);
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int sp = 0; sp < C; ++sp) {
-            const float4 r = sp == ks ? mine : recv[((sp < ks ? sp : sp - 1) * per + tl) * kTcBlockO + o_local];
-            acc.x += r.x; acc.y += r.y; acc.z += r.z; acc.w += r.w;
+          if (C <= 8) {
+            tc_cluster_sum<8>(acc, C, ks, mine_addr + tok_off, recv_addr + tok_off, slot_bytes);
+          } else {
+            tc_cluster_sum<kTcClusterMax>(acc, C, ks, mine_addr + tok_off, recv_addr + tok_off, slot_bytes);
           }
           if (ok && got && o < prm.N_g)
-            store_out<T, PEERS>(y, prm.peers, (int64_t)(t0 + t) * prm.ld_y + 4 * o,
+            store_out<T, PEERS>(y, prm.peers, (int64_t)(t0 + own0 + tl) * prm.ld_y + 4 * o,
                                 pack4<T>(acc.x + b[0], acc.y + b[1], acc.z + b[2], acc.w + b[3]));
         }
       }
@@ -859,11 +898,12 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   // ---------------- teardown ----------------
   tc_fence_before();
   __syncthreads();
-  // No CTA of a cluster leaves while another may still store into it: an
-  // owner arrives once every partial of its tokens has landed, the others
-  // after sending.
+  // No CTA of a cluster leaves while a bulk copy may still read its send
+  // buffer or write its receive buffer: an owner arrives once every partial
+  // of its tokens has landed.  The arrive is relaxed: the barrier orders no
+  // global stores (a release arrive waited for the output stores to complete).
   if (CLUSTER) {
-    cluster_arrive_release();
+    cluster_arrive_relaxed();
     cluster_wait_acquire();
   }
   if (threadIdx.x == 0 && *abort_flag) {
