@@ -689,6 +689,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
     }
   }
   // 2. tensor maps
+  int sub3d = 0;
   CUtensorMap maps[8];
   std::memset(maps, 0, sizeof(maps));
   for (int p = 0; p < 4; ++p) {
@@ -704,11 +705,22 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
     cuuint32_t box[3] = {kTcChunk, (cuuint32_t)n_tok, 1};
     if (encode(&maps[4], dt, 3, xp, dims, strides, box) != CUDA_SUCCESS) return QLIN_ERR_ALIGN;
   } else {
-    // raw x rows of a stacked tile: 32 elements (64 bytes, 64-byte swizzle) x n_tok tokens
-    cuuint64_t dims[2] = {(cuuint64_t)(4 * K_g), (cuuint64_t)M};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld_x * 2)};
-    cuuint32_t box[2] = {32, (cuuint32_t)n_tok};
-    if (encode(&maps[4], dt, 2, const_cast<T*>(x), dims, strides, box) != CUDA_SUCCESS) return QLIN_ERR_ALIGN;
+    // raw x rows of a stacked tile: 32 elements (64 bytes, 64-byte swizzle) x n_tok tokens.
+    // With K_g a multiple of 8 the four 32-element sub-tiles of a chunk come in
+    // one box of a 3-D view [sub-tile (64-byte stride)][token][32 elements]: one
+    // TMA operation instead of four (the issue of each TMA operation, not its
+    // bytes, set the pace of these small tiles).
+    cuuint64_t dims3[3] = {32, (cuuint64_t)M, (cuuint64_t)(K_g / 8)};
+    cuuint64_t strides3[2] = {(cuuint64_t)(ld_x * 2), 64};
+    cuuint32_t box3[3] = {32, (cuuint32_t)n_tok, 4};
+    if (K_g % 8 == 0 && encode(&maps[4], dt, 3, const_cast<T*>(x), dims3, strides3, box3) == CUDA_SUCCESS) {
+      sub3d = 1;
+    } else {
+      cuuint64_t dims[2] = {(cuuint64_t)(4 * K_g), (cuuint64_t)M};
+      cuuint64_t strides[1] = {(cuuint64_t)(ld_x * 2)};
+      cuuint32_t box[2] = {32, (cuuint32_t)n_tok};
+      if (encode(&maps[4], dt, 2, const_cast<T*>(x), dims, strides, box) != CUDA_SUCCESS) return QLIN_ERR_ALIGN;
+    }
   }
   int lora_chunks = 0;
   if (rank > 0) {
@@ -730,9 +742,17 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
       cuuint64_t astrides[1] = {(cuuint64_t)(4 * K_g * 2)};
       const bool tc = lmode == kLoraTc;
       cuuint32_t abox[2] = {tc ? 32u : (cuuint32_t)kTcLoraSliceBox, (cuuint32_t)kTcLoraInRank};
-      if (encode(&maps[7], dt, 2, const_cast<T*>(lora_a), adims, astrides, abox,
-                 tc ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
+      // tensor-core mode with the 3-D x view: lora_a's chunk columns likewise in one box
+      cuuint64_t adims3[3] = {32, (cuuint64_t)rank, (cuuint64_t)(K_g / 8)};
+      cuuint64_t astrides3[2] = {(cuuint64_t)(4 * K_g * 2), 64};
+      cuuint32_t abox3[3] = {32, (cuuint32_t)kTcLoraInRank, 4};
+      if (tc && sub3d) {
+        if (encode(&maps[7], dt, 3, const_cast<T*>(lora_a), adims3, astrides3, abox3) != CUDA_SUCCESS)
+          return QLIN_ERR_ALIGN;
+      } else if (encode(&maps[7], dt, 2, const_cast<T*>(lora_a), adims, astrides, abox,
+                        tc ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS) {
         return QLIN_ERR_ALIGN;
+      }
     }
   }
   // 3. main kernel (+ split-K reduction)
@@ -751,6 +771,7 @@ int run_tc(DeviceInfo* dev, const T* x, int64_t ld_x, const void* const w[4], in
   prm.partials = nullptr;
   prm.static_weights = (flags & QLIN_FLAG_STATIC_WEIGHTS) ? 1 : 0;
   prm.no_cluster = (flags & QLIN_FLAG_NO_CLUSTER) ? 1 : 0;
+  prm.sub3d = sub3d;
   prm.counters = (flags & QLIN_FLAG_ZEROED_WORKSPACE) ? reinterpret_cast<unsigned*>(ws + L.cnt_off)
                                                        : nullptr;
   prm.fuse_reduce = 0;

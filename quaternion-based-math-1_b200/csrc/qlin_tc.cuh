@@ -167,6 +167,8 @@ struct TcParams {
   int static_weights;  // weights/bias/LoRA B are not written by earlier work on the stream
   int after_prologue;  // launched right after this call's prologue kernel (see below)
   int no_cluster;      // host-side choice only: QLIN_FLAG_NO_CLUSTER
+  int sub3d;           // stacked tiles: map_x (and the tensor-core mode's map_la) are 3-D views
+                       // [sub-tile][row][32 elements], one box per chunk instead of four
   int rank;            // LoRA rank (in-kernel LoRA: ranks >= rank are zero)
   float lora_scale;    // in-kernel LoRA: t = lora_scale * x A^T
   const void* lora_a;  // CUDA-core in-kernel LoRA: A [rank, ld_a]
@@ -311,8 +313,21 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
   auto issue_raw_x = [&](int it) {
     const int s = it % S, k = (c_begin + it) * kTcChunk;
     mbar_arrive_expect_tx(&xfull[s], (uint32_t)Cfg::kRawXBytes);
+    if (prm.sub3d) {
+      tma_load_3d(raw_tile(s, 0), &map_x, &xfull[s], 0, t0, k / 8);
+    } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) tma_load_2d(raw_tile(s, j), &map_x, &xfull[s], 4 * k + 32 * j, t0);
+      for (int j = 0; j < 4; ++j) tma_load_2d(raw_tile(s, j), &map_x, &xfull[s], 4 * k + 32 * j, t0);
+    }
+  };
+  // lora_a columns of the chunk at input quaternion k (tensor-core LoRA mode)
+  auto issue_lora_a = [&](int s, int k) {
+    if (prm.sub3d) {
+      tma_load_3d(la_tile(s, 0), &map_la, &full[s], 0, 0, k / 8);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) tma_load_2d(la_tile(s, j), &map_la, &full[s], 4 * k + 32 * j, 0);
+    }
   };
   // Weight (and LoRA B) tiles of the first stages; in the CUDA-core LoRA mode
   // preceded by this split's lora_a slice, so that it arrives first.
@@ -332,8 +347,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
 #pragma unroll
         for (int p = 0; p < 4; ++p) tma_load_2d(w_tile(it, p), wmap[p], &full[it], k, o0);
         if (LORA == kLoraTc) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) tma_load_2d(la_tile(it, j), &map_la, &full[it], 4 * k + 32 * j, 0);
+          issue_lora_a(it, k);
         }
       } else {
         const int r = (it - my_main) * kTcChunk;
@@ -445,8 +459,7 @@ qlin_tc_kernel(const __grid_constant__ CUtensorMap map_wr, const __grid_constant
           for (int q = 0; q < 4; ++q) tma_load_3d(x_tile(s, q), &map_x, &full[s], k, t0, q);
         }
         if (LORA == kLoraTc) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) tma_load_2d(la_tile(s, j), &map_la, &full[s], 4 * k + 32 * j, 0);
+          issue_lora_a(s, k);
         }
       } else {
         const int r = (it - my_main) * kTcChunk;
