@@ -16,11 +16,13 @@
 // quaternion/packing.py:18-21):
 //   y0 += w0 x0 - w1 x1 - w2 x2 - w3 x3      y1 += w0 x1 + w1 x0 + w2 x3 - w3 x2
 //   y2 += w0 x2 - w1 x3 + w2 x0 + w3 x1      y3 += w0 x3 + w1 x2 - w2 x1 + w3 x0
-// in fp32; the 32 lanes' sums are combined by warp shuffles and rounded once
-// with bias and LoRA.  x is staged once per CTA in shared memory as fp32
-// quaternions, laid out so that a warp's reads of one chunk are
-// conflict-free: float4 index ((m * nch + c) * 8 + j) * 32 + (l ^ j) holds
-// input quaternion 256c + 8l + j of token m.  Its rows arrive by bulk copies
+// in fp32, two input quaternions at a time on packed fp32x2 FMAs
+// (fma.rn.f32x2: 16 instead of 32 FMA instructions per quaternion pair; the
+// multiplies run after the weights land, so their issue count is on the
+// call's critical path); the 32 lanes' sums are combined by warp shuffles and
+// rounded once with bias and LoRA.  x is staged once per CTA in shared memory
+// as fp32, laid out so that a warp's reads are conflict-free and every float4
+// read holds two fp32x2 operands (gemv_put_x).  Its rows arrive by bulk copies
 // (TMA engine) requested before the weight loads when they are 16-byte
 // aligned: by loads, x queued behind the CTA's 64 KB of weight loads and the
 // multiplies could only start once the last weights had landed (measured:
@@ -117,6 +119,23 @@ __device__ __forceinline__ void named_bar_arrive(int id, int threads) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Staged x (planar weights): for token m, chunk c, lane l and input
+// quaternion pair jp (quaternions j = 2jp, 2jp + 1 of the lane's eight
+// 256c + 8l + j), two float4 -- A = (x0[j], x0[j+1], x1[j], x1[j+1]) at index
+// ((m * nch + c) * 8 + 2jp) * 32 + l and B = (x2[j], x2[j+1], x3[j], x3[j+1])
+// 32 float4 further -- so a warp's reads of one (c, jp) are 32 consecutive
+// float4 and every read gives the fp32x2 operands of the packed FMAs.
+// gemv_put_x stores one quaternion v of input i (chunk c) of token m.
+__device__ __forceinline__ void gemv_put_x(float4* xs, int m, int nch, int c, int i, float4 v) {
+  const int l = (i / 8) & 31, j = i & 7, e = j & 1;
+  float* a = reinterpret_cast<float*>(xs + ((m * nch + c) * 8 + (j & 6)) * 32 + l);
+  float* b = a + 32 * 4;
+  a[e] = v.x;
+  a[2 + e] = v.y;
+  b[e] = v.z;
+  b[2 + e] = v.w;
+}
+
 // Stages x as fp32 quaternions in shared memory (zeros past K_g and past M).
 // Item (token m, input quaternion i), numbered m * nq + i: thread tid of
 // nthr converts items tid, tid + nthr, ...  (m, i) advance by nthr (at most
@@ -161,8 +180,7 @@ struct GemvXStager {
           const int ic = xi - c * kGemvChunk;
           xs[((xm * nch + c) * 2 + (ic & 1)) * (kGemvChunk / 2) + (ic >> 1)] = v;
         } else {
-          const int l = (xi / 8) & 31, j = xi & 7;
-          xs[((xm * nch + c) * 8 + j) * 32 + (l ^ j)] = v;
+          gemv_put_x(xs, xm, nch, c, xi, v);
         }
       }
       advance(xm, xi);
@@ -170,30 +188,83 @@ struct GemvXStager {
   }
 };
 
-// One chunk of a row warp's Hamilton products: w0..w3[j] are components r,
-// i, j, k of this lane's 8 weight quaternions of chunk c, x comes from the
-// staged copy.
-template <int MT, bool PACKED>
-__device__ __forceinline__ void gemv_chunk_fma(float (&acc)[MT][4], const float (&w0)[8], const float (&w1)[8],
-                                               const float (&w2)[8], const float (&w3)[8], const float4* xs,
-                                               int nch, int c, int lane) {
+// One chunk of a row warp's Hamilton products, packed weights: w0..w3[j] are
+// components r, i, j, k of this lane's 8 weight quaternions of chunk c; x
+// comes from the staged copy ([m][c][parity][128 quaternion pairs]).
+template <int MT>
+__device__ __forceinline__ void gemv_chunk_fma_packed(float (&acc)[MT][4], const float (&w0)[8], const float (&w1)[8],
+                                                      const float (&w2)[8], const float (&w3)[8], const float4* xs,
+                                                      int nch, int c, int lane) {
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float4 v;
-      if constexpr (PACKED) {
-        // quaternion 2 (lane + 32 (j / 2)) + (j % 2) of the chunk
-        v = xs[((m * nch + c) * 2 + (j & 1)) * (kGemvChunk / 2) + lane + 32 * (j >> 1)];
-      } else {
-        v = xs[((m * nch + c) * 8) * 32 + j * 32 + (lane ^ j)];
-      }
+      // quaternion 2 (lane + 32 (j / 2)) + (j % 2) of the chunk
+      const float4 v = xs[((m * nch + c) * 2 + (j & 1)) * (kGemvChunk / 2) + lane + 32 * (j >> 1)];
       float y0 = acc[m][0], y1 = acc[m][1], y2 = acc[m][2], y3 = acc[m][3];
       y0 = fmaf(w0[j], v.x, y0); y0 = fmaf(-w1[j], v.y, y0); y0 = fmaf(-w2[j], v.z, y0); y0 = fmaf(-w3[j], v.w, y0);
       y1 = fmaf(w0[j], v.y, y1); y1 = fmaf(w1[j], v.x, y1); y1 = fmaf(w2[j], v.w, y1); y1 = fmaf(-w3[j], v.z, y1);
       y2 = fmaf(w0[j], v.z, y2); y2 = fmaf(-w1[j], v.w, y2); y2 = fmaf(w2[j], v.x, y2); y2 = fmaf(w3[j], v.y, y2);
       y3 = fmaf(w0[j], v.w, y3); y3 = fmaf(w1[j], v.z, y3); y3 = fmaf(-w2[j], v.y, y3); y3 = fmaf(w3[j], v.x, y3);
       acc[m][0] = y0; acc[m][1] = y1; acc[m][2] = y2; acc[m][3] = y3;
+    }
+  }
+}
+
+// fp32x2 operands: two fp32 values in one 64-bit register pair.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return make_float2(lo, hi);
+}
+// d += a * b on both halves (fma.rn.f32x2, sm_100): each half an IEEE fp32 FMA.
+__device__ __forceinline__ void f2_fma(uint64_t& d, uint64_t a, uint64_t b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
+// Two adjacent 16-bit weights (one 32-bit word, lower address in the low
+// half) -> fp32x2.
+template <typename T> __device__ __forceinline__ uint64_t w_pair(uint32_t u);
+template <> __device__ __forceinline__ uint64_t w_pair<__nv_bfloat16>(uint32_t u) {
+  return f2_pack(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+template <> __device__ __forceinline__ uint64_t w_pair<__half>(uint32_t u) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u));
+  return f2_pack(f.x, f.y);
+}
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
+  return k == 0 ? v.x : (k == 1 ? v.y : (k == 2 ? v.z : v.w));
+}
+
+// One chunk of a row warp's Hamilton products, planar weights: w[p] holds
+// component p of this lane's 8 weight quaternions (16-bit, as loaded).  Two
+// input quaternions at a time on packed fp32x2 FMAs (half the FMA
+// instructions of the scalar form): yp/yn[m][a] collect the positive and
+// the negative terms of output component a, each half one of the two
+// quaternions, summed when the row is finished.
+template <typename T, int MT>
+__device__ __forceinline__ void gemv_chunk_fma2(uint64_t (&yp)[MT][4], uint64_t (&yn)[MT][4], const uint4 (&w)[4],
+                                                const float4* xs, int nch, int c, int lane) {
+#pragma unroll
+  for (int jp = 0; jp < 4; ++jp) {
+    const uint64_t W0 = w_pair<T>(word_of(w[0], jp)), W1 = w_pair<T>(word_of(w[1], jp));
+    const uint64_t W2 = w_pair<T>(word_of(w[2], jp)), W3 = w_pair<T>(word_of(w[3], jp));
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float4 A = xs[((m * nch + c) * 8 + 2 * jp) * 32 + lane];
+      const float4 B = xs[((m * nch + c) * 8 + 2 * jp + 1) * 32 + lane];
+      const uint64_t X0 = f2_pack(A.x, A.y), X1 = f2_pack(A.z, A.w);
+      const uint64_t X2 = f2_pack(B.x, B.y), X3 = f2_pack(B.z, B.w);
+      // y0 = w0x0 - w1x1 - w2x2 - w3x3      y1 = w0x1 + w1x0 + w2x3 - w3x2
+      // y2 = w0x2 - w1x3 + w2x0 + w3x1      y3 = w0x3 + w1x2 - w2x1 + w3x0
+      f2_fma(yp[m][0], W0, X0); f2_fma(yn[m][0], W1, X1); f2_fma(yn[m][0], W2, X2); f2_fma(yn[m][0], W3, X3);
+      f2_fma(yp[m][1], W0, X1); f2_fma(yp[m][1], W1, X0); f2_fma(yp[m][1], W2, X3); f2_fma(yn[m][1], W3, X2);
+      f2_fma(yp[m][2], W0, X2); f2_fma(yn[m][2], W1, X3); f2_fma(yp[m][2], W2, X0); f2_fma(yp[m][2], W3, X1);
+      f2_fma(yp[m][3], W0, X3); f2_fma(yp[m][3], W1, X2); f2_fma(yn[m][3], W2, X1); f2_fma(yp[m][3], W3, X0);
     }
   }
 }
@@ -371,8 +442,7 @@ qlin_gemv_kernel(const GemvParams prm) {
           const int ic = ie - c * kGemvChunk;
           xs[((m * nch + c) * 2 + (ic & 1)) * (kGemvChunk / 2) + (ic >> 1)] = v;
         } else {
-          const int l = (ie / 8) & 31, j = ie & 7;
-          xs[((m * nch + c) * 8 + j) * 32 + (l ^ j)] = v;
+          gemv_put_x(xs, m, nch, c, ie, v);
         }
       }
       i += 2 * nthr;
@@ -415,31 +485,50 @@ qlin_gemv_kernel(const GemvParams prm) {
   for (int m = 0; m < MT; ++m)
 #pragma unroll
     for (int a = 0; a < 4; ++a) acc[m][a] = 0.f;
-  for (int cb = 0; cb < nch; cb += kGemvDepth) {
+  if constexpr (!PACKED) {
+    uint64_t yp[MT][4], yn[MT][4];
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int a = 0; a < 4; ++a) yp[m][a] = yn[m][a] = 0ull;
+    for (int cb = 0; cb < nch; cb += kGemvDepth) {
+#pragma unroll
+      for (int d = 0; d < kGemvDepth; ++d) {
+        const int c = cb + d;
+        if (c < nch) {
+          const uint4 w[4] = {wv[d][0], wv[d][1], wv[d][2], wv[d][3]};
+          // refill: the chunk kGemvDepth further on reuses these registers
+          if (c + kGemvDepth < nch) load_chunk(d, c + kGemvDepth);
+          gemv_chunk_fma2<T, MT>(yp, yn, w, xs, nch, c, lane);
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const float2 p = f2_unpack(yp[m][a]), n = f2_unpack(yn[m][a]);
+        acc[m][a] = (p.x + p.y) - (n.x + n.y);
+      }
+  }
+  for (int cb = 0; PACKED && cb < nch; cb += kGemvDepth) {
 #pragma unroll
     for (int d = 0; d < kGemvDepth; ++d) {
       const int c = cb + d;
       if (c < nch) {
         // w0..w3[j]: components r, i, j, k of this lane's 8 weight quaternions
         float w0[8], w1[8], w2[8], w3[8];
-        if constexpr (PACKED) {
-          // piece u holds quaternions 2u' and 2u'+1 (u' = lane + 32u) as r,i,j,k,r,i,j,k
+        // piece u holds quaternions 2u' and 2u'+1 (u' = lane + 32u) as r,i,j,k,r,i,j,k
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float f[8];
-            unpack8<T>(wv[d][u], f);
-            w0[2 * u] = f[0]; w1[2 * u] = f[1]; w2[2 * u] = f[2]; w3[2 * u] = f[3];
-            w0[2 * u + 1] = f[4]; w1[2 * u + 1] = f[5]; w2[2 * u + 1] = f[6]; w3[2 * u + 1] = f[7];
-          }
-        } else {
-          unpack8<T>(wv[d][0], w0);
-          unpack8<T>(wv[d][1], w1);
-          unpack8<T>(wv[d][2], w2);
-          unpack8<T>(wv[d][3], w3);
+        for (int u = 0; u < 4; ++u) {
+          float f[8];
+          unpack8<T>(wv[d][u], f);
+          w0[2 * u] = f[0]; w1[2 * u] = f[1]; w2[2 * u] = f[2]; w3[2 * u] = f[3];
+          w0[2 * u + 1] = f[4]; w1[2 * u + 1] = f[5]; w2[2 * u + 1] = f[6]; w3[2 * u + 1] = f[7];
         }
         // refill: the chunk kGemvDepth further on reuses these registers
         if (c + kGemvDepth < nch) load_chunk(d, c + kGemvDepth);
-        gemv_chunk_fma<MT, PACKED>(acc, w0, w1, w2, w3, xs, nch, c, lane);
+        gemv_chunk_fma_packed<MT>(acc, w0, w1, w2, w3, xs, nch, c, lane);
       }
     }
   }
