@@ -244,27 +244,47 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
 // component p of this lane's 8 weight quaternions (16-bit, as loaded).  Two
 // input quaternions at a time on packed fp32x2 FMAs (half the FMA
 // instructions of the scalar form): yp/yn[m][a] collect the positive and
-// the negative terms of output component a, each half one of the two
-// quaternions, summed when the row is finished.
+// the negative terms of output component a (at most 2 tokens; above, yp
+// takes all terms and yn stays zero), each half one of the two quaternions,
+// summed when the row is finished.
 template <typename T, int MT>
 __device__ __forceinline__ void gemv_chunk_fma2(uint64_t (&yp)[MT][4], uint64_t (&yn)[MT][4], const uint4 (&w)[4],
                                                 const float4* xs, int nch, int c, int lane) {
 #pragma unroll
   for (int jp = 0; jp < 4; ++jp) {
-    const uint64_t W0 = w_pair<T>(word_of(w[0], jp)), W1 = w_pair<T>(word_of(w[1], jp));
-    const uint64_t W2 = w_pair<T>(word_of(w[2], jp)), W3 = w_pair<T>(word_of(w[3], jp));
+    const uint32_t u1 = word_of(w[1], jp), u2 = word_of(w[2], jp), u3 = word_of(w[3], jp);
+    const uint64_t W0 = w_pair<T>(word_of(w[0], jp)), W1 = w_pair<T>(u1), W2 = w_pair<T>(u2), W3 = w_pair<T>(u3);
+    // y0 = w0x0 - w1x1 - w2x2 - w3x3      y1 = w0x1 + w1x0 + w2x3 - w3x2
+    // y2 = w0x2 - w1x3 + w2x0 + w3x1      y3 = w0x3 + w1x2 - w2x1 + w3x0
+    if constexpr (MT <= 2) {
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      const float4 A = xs[((m * nch + c) * 8 + 2 * jp) * 32 + lane];
-      const float4 B = xs[((m * nch + c) * 8 + 2 * jp + 1) * 32 + lane];
-      const uint64_t X0 = f2_pack(A.x, A.y), X1 = f2_pack(A.z, A.w);
-      const uint64_t X2 = f2_pack(B.x, B.y), X3 = f2_pack(B.z, B.w);
-      // y0 = w0x0 - w1x1 - w2x2 - w3x3      y1 = w0x1 + w1x0 + w2x3 - w3x2
-      // y2 = w0x2 - w1x3 + w2x0 + w3x1      y3 = w0x3 + w1x2 - w2x1 + w3x0
-      f2_fma(yp[m][0], W0, X0); f2_fma(yn[m][0], W1, X1); f2_fma(yn[m][0], W2, X2); f2_fma(yn[m][0], W3, X3);
-      f2_fma(yp[m][1], W0, X1); f2_fma(yp[m][1], W1, X0); f2_fma(yp[m][1], W2, X3); f2_fma(yn[m][1], W3, X2);
-      f2_fma(yp[m][2], W0, X2); f2_fma(yn[m][2], W1, X3); f2_fma(yp[m][2], W2, X0); f2_fma(yp[m][2], W3, X1);
-      f2_fma(yp[m][3], W0, X3); f2_fma(yp[m][3], W1, X2); f2_fma(yn[m][3], W2, X1); f2_fma(yp[m][3], W3, X0);
+      for (int m = 0; m < MT; ++m) {
+        const float4 A = xs[((m * nch + c) * 8 + 2 * jp) * 32 + lane];
+        const float4 B = xs[((m * nch + c) * 8 + 2 * jp + 1) * 32 + lane];
+        const uint64_t X0 = f2_pack(A.x, A.y), X1 = f2_pack(A.z, A.w);
+        const uint64_t X2 = f2_pack(B.x, B.y), X3 = f2_pack(B.z, B.w);
+        f2_fma(yp[m][0], W0, X0); f2_fma(yn[m][0], W1, X1); f2_fma(yn[m][0], W2, X2); f2_fma(yn[m][0], W3, X3);
+        f2_fma(yp[m][1], W0, X1); f2_fma(yp[m][1], W1, X0); f2_fma(yp[m][1], W2, X3); f2_fma(yn[m][1], W3, X2);
+        f2_fma(yp[m][2], W0, X2); f2_fma(yn[m][2], W1, X3); f2_fma(yp[m][2], W2, X0); f2_fma(yp[m][2], W3, X1);
+        f2_fma(yp[m][3], W0, X3); f2_fma(yp[m][3], W1, X2); f2_fma(yn[m][3], W2, X1); f2_fma(yp[m][3], W3, X0);
+      }
+    } else {
+      // more tokens: the negative terms use negated weight pairs (sign bits of
+      // both 16-bit halves flipped), one accumulator pair per component and
+      // token, so the accumulators stay within the register budget
+      const uint64_t N1 = w_pair<T>(u1 ^ 0x80008000u), N2 = w_pair<T>(u2 ^ 0x80008000u);
+      const uint64_t N3 = w_pair<T>(u3 ^ 0x80008000u);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        const float4 A = xs[((m * nch + c) * 8 + 2 * jp) * 32 + lane];
+        const float4 B = xs[((m * nch + c) * 8 + 2 * jp + 1) * 32 + lane];
+        const uint64_t X0 = f2_pack(A.x, A.y), X1 = f2_pack(A.z, A.w);
+        const uint64_t X2 = f2_pack(B.x, B.y), X3 = f2_pack(B.z, B.w);
+        f2_fma(yp[m][0], W0, X0); f2_fma(yp[m][0], N1, X1); f2_fma(yp[m][0], N2, X2); f2_fma(yp[m][0], N3, X3);
+        f2_fma(yp[m][1], W0, X1); f2_fma(yp[m][1], W1, X0); f2_fma(yp[m][1], W2, X3); f2_fma(yp[m][1], N3, X2);
+        f2_fma(yp[m][2], W0, X2); f2_fma(yp[m][2], N1, X3); f2_fma(yp[m][2], W2, X0); f2_fma(yp[m][2], W3, X1);
+        f2_fma(yp[m][3], W0, X3); f2_fma(yp[m][3], W1, X2); f2_fma(yp[m][3], N2, X1); f2_fma(yp[m][3], W3, X0);
+      }
     }
   }
 }
